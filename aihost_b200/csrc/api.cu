@@ -1,0 +1,564 @@
+// api.cu — the extern "C" boundary of libaihost_attn.so (declared in include/aihost_attn.h).
+//
+// Host-side work only: argument validation (each failure gets its own message and status, the
+// way ICompute/CUDA/CudaApi.cs:CheckError turns error codes into exceptions on the C# side),
+// the RoPE frequency table, cache-geometry resolution, TMA descriptor encoding and the choice
+// of split size for decode. No allocation happens outside create / reserve.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <utility>
+#include <vector>
+
+#include "../../include/aihost_attn.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace aihost;
+
+// Per-kernel-kind device-time accumulator (events recorded around each launch while enabled).
+struct ProfSlot {
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
+  int64_t launches = 0;
+  double total_ms = 0.0;
+};
+
+struct aihost_attn_ctx {
+  int32_t device = 0;
+  int32_t num_sms = 148;
+  int32_t* d_status = nullptr;
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  bool profiling = false;
+  std::mutex prof_mu;
+  ProfSlot prof[AIHOST_KERNEL_COUNT];
+  std::vector<cudaEvent_t> event_pool;
+};
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+aihost_status fail(aihost_status st, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+aihost_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(AIHOST_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// Runs `f` with the context's device current and restores the caller's device afterwards.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int32_t dev) {
+    ok_ = cudaGetDevice(&prev_) == cudaSuccess;
+    if (ok_ && prev_ != dev) ok_ = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (cudaGetDevice(&cur) == cudaSuccess && cur != prev_) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = 0;
+  bool ok_ = false;
+};
+
+int64_t row_bytes(int32_t dtype, int32_t head_dim) {
+  if (dtype == AIHOST_F32) return 4LL * head_dim;
+  if (dtype == AIHOST_F16) return 2LL * head_dim;
+  return 34LL * (head_dim / 32);
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Validates the static description; fills the resolved cache layout and scale.
+aihost_status check_desc(const aihost_attn_desc* d, KvLayout* kv, float* scale) {
+  if (!d) return fail(AIHOST_EINVAL, "desc is NULL");
+  if (d->n_q_heads < 1 || d->n_kv_heads < 1)
+    return fail(AIHOST_EINVAL, "n_q_heads (%d) and n_kv_heads (%d) must be >= 1", d->n_q_heads, d->n_kv_heads);
+  if (d->n_q_heads % d->n_kv_heads)
+    return fail(AIHOST_EINVAL, "n_q_heads (%d) must be a multiple of n_kv_heads (%d)", d->n_q_heads, d->n_kv_heads);
+  if (d->head_dim != 64 && d->head_dim != 128)
+    return fail(AIHOST_EUNSUPPORTED, "head_dim %d is not supported (64 or 128)", d->head_dim);
+  if (d->q_dtype != AIHOST_F32 && d->q_dtype != AIHOST_F16)
+    return fail(AIHOST_EINVAL, "q_dtype %d must be F32 (0) or F16 (1)", d->q_dtype);
+  if (d->out_dtype != AIHOST_F32 && d->out_dtype != AIHOST_F16)
+    return fail(AIHOST_EINVAL, "out_dtype %d must be F32 (0) or F16 (1)", d->out_dtype);
+  if (d->kv_dtype != AIHOST_F32 && d->kv_dtype != AIHOST_F16 && d->kv_dtype != AIHOST_Q8_0)
+    return fail(AIHOST_EINVAL, "kv_dtype %d must be F32 (0), F16 (1) or Q8_0 (6)", d->kv_dtype);
+  if (d->rope_mode < AIHOST_ROPE_INTERLEAVED || d->rope_mode > AIHOST_ROPE_NONE)
+    return fail(AIHOST_EINVAL, "rope_mode %d is not a valid aihost_rope_mode", d->rope_mode);
+  if (d->rope_mode != AIHOST_ROPE_NONE && !(d->rope_theta > 0.0f && isfinite(d->rope_theta)))
+    return fail(AIHOST_EINVAL, "rope_theta must be a positive finite number");
+  if (d->kv_capacity < 1) return fail(AIHOST_EINVAL, "kv_capacity must be >= 1");
+  if (!(isfinite(d->scale) && d->scale >= 0.0f)) return fail(AIHOST_EINVAL, "scale must be >= 0 and finite");
+  const int64_t rb = row_bytes(d->kv_dtype, d->head_dim);
+  kv->head_stride = d->kv_head_stride ? d->kv_head_stride : rb;
+  kv->token_stride = d->kv_token_stride ? d->kv_token_stride : kv->head_stride * d->n_kv_heads;
+  kv->seq_stride = d->kv_seq_stride ? d->kv_seq_stride : kv->token_stride * d->kv_capacity;
+  kv->capacity = d->kv_capacity;
+  kv->dtype = d->kv_dtype;
+  if (kv->head_stride < rb || kv->token_stride < rb || kv->seq_stride < 0)
+    return fail(AIHOST_EINVAL, "kv strides smaller than one head row (%lld bytes)", static_cast<long long>(rb));
+  const int64_t need_align = d->kv_dtype == AIHOST_Q8_0 ? 2 : 16;
+  if (kv->head_stride % need_align || kv->token_stride % need_align || kv->seq_stride % need_align)
+    return fail(AIHOST_EINVAL, "kv strides must be multiples of %lld bytes", static_cast<long long>(need_align));
+  *scale = d->scale != 0.0f ? d->scale : 1.0f / sqrtf(static_cast<float>(d->head_dim));
+  return AIHOST_OK;
+}
+
+RopeFreqs make_freqs(float theta, int32_t head_dim) {
+  RopeFreqs f;
+  memset(&f, 0, sizeof(f));
+  for (int i = 0; i < head_dim / 2 && i < kMaxHeadDim / 2; ++i)
+    f.f[i] = 1.0f / powf(theta, static_cast<float>(2 * i) / static_cast<float>(head_dim));
+  return f;
+}
+
+// Decode split plan: rows per split chosen from the capacity (so the scratch size is a
+// function of the description alone), aiming at ~8 resident CTAs per SM.
+struct DecodePlan {
+  int32_t chunk, max_splits;
+};
+DecodePlan plan_decode(const aihost_attn_desc* d, int32_t batch, int32_t num_sms) {
+  const int32_t G = d->n_q_heads / d->n_kv_heads;
+  const int32_t gt = G >= 8 ? 8 : G >= 4 ? 4 : G >= 2 ? 2 : 1;
+  const int64_t units = static_cast<int64_t>(batch) * d->n_kv_heads * ((G + gt - 1) / gt);
+  const int64_t target = static_cast<int64_t>(num_sms) * 8;
+  int64_t chunk = (static_cast<int64_t>(d->kv_capacity) * units + target - 1) / target;
+  chunk = (chunk + 31) / 32 * 32;
+  if (chunk < 64) chunk = 64;
+  if (chunk > 512) chunk = 512;
+  DecodePlan p;
+  p.chunk = static_cast<int32_t>(chunk);
+  p.max_splits = static_cast<int32_t>((d->kv_capacity + chunk - 1) / chunk);
+  return p;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// fp16 tensor [d3][d2][d1][d0 = head_dim] with byte strides s1, s2, s3; box {64, 1, 128, 1},
+// 128-byte swizzle (the canonical tcgen05 K-major / MN-major operand layout).
+aihost_status encode_f16_map(CUtensorMap* map, const void* base, int32_t d0, int64_t d1, int64_t d2, int64_t d3,
+                             int64_t s1, int64_t s2, int64_t s3, const char* what) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned(base, 16)) return fail(AIHOST_EINVAL, "%s must be 16-byte aligned", what);
+  if (s1 % 16 || s2 % 16 || s3 % 16) return fail(AIHOST_EINVAL, "%s strides must be multiples of 16 bytes", what);
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2),
+                        static_cast<cuuint64_t>(d3)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s1), static_cast<cuuint64_t>(s2), static_cast<cuuint64_t>(s3)};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what, static_cast<int>(r));
+  return AIHOST_OK;
+}
+
+aihost_status check_ctx(aihost_attn_ctx* ctx) {
+  if (!ctx) return fail(AIHOST_EINVAL, "ctx is NULL");
+  return AIHOST_OK;
+}
+
+cudaEvent_t take_event(aihost_attn_ctx* ctx) {
+  if (!ctx->event_pool.empty()) {
+    cudaEvent_t e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+// Launch through `fn`, bracketed by timing events on `st` when the profiler is on.
+template <class F>
+cudaError_t timed_launch(aihost_attn_ctx* ctx, int kind, cudaStream_t st, F&& fn) {
+  if (!ctx->profiling) return fn();
+  std::lock_guard<std::mutex> lk(ctx->prof_mu);
+  cudaEvent_t a = take_event(ctx), b = take_event(ctx);
+  if (!a || !b) return cudaErrorMemoryAllocation;
+  cudaError_t e = cudaEventRecord(a, st);
+  if (e != cudaSuccess) return e;
+  e = fn();
+  if (e != cudaSuccess) return e;
+  e = cudaEventRecord(b, st);
+  if (e != cudaSuccess) return e;
+  ctx->prof[kind].pending.emplace_back(a, b);
+  return cudaSuccess;
+}
+
+aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const KvLayout& kv, float scale,
+                         int32_t batch, const void* q, const void* kc, const void* vc, const int32_t* seq_len,
+                         int32_t start_scalar, int32_t len_offset, int32_t rope_mode, void* out, cudaStream_t st) {
+  DecodePlan plan = plan_decode(d, batch, ctx->num_sms);
+  const size_t need = decode_scratch_bytes(batch, d->n_q_heads, d->head_dim, plan.max_splits);
+  if (need > ctx->scratch_bytes)
+    return fail(AIHOST_ENOMEM, "decode needs %zu bytes of scratch, context has %zu (call aihost_attn_reserve)", need,
+                ctx->scratch_bytes);
+  DecodeArgs a;
+  memset(&a, 0, sizeof(a));
+  a.q = q;
+  a.q_dtype = d->q_dtype;
+  a.k_cache = kc;
+  a.v_cache = vc;
+  a.kv = kv;
+  a.seq_len = seq_len;
+  a.start_scalar = start_scalar;
+  a.len_offset = len_offset;
+  a.rope_pos_offset = 0;
+  a.batch = batch;
+  a.n_q_heads = d->n_q_heads;
+  a.n_kv_heads = d->n_kv_heads;
+  a.head_dim = d->head_dim;
+  a.scale = scale;
+  a.rope_mode = rope_mode;
+  if (rope_mode != AIHOST_ROPE_NONE) a.freqs = make_freqs(d->rope_theta, d->head_dim);
+  a.chunk = plan.chunk;
+  a.max_splits = plan.max_splits;
+  float* scratch = static_cast<float*>(ctx->scratch);
+  a.part_o = scratch;
+  a.part_ml = scratch ? scratch + static_cast<size_t>(batch) * d->n_q_heads * plan.max_splits * d->head_dim : nullptr;
+  a.out = out;
+  a.out_dtype = d->out_dtype;
+  a.status = ctx->d_status;
+  cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_DECODE, st, [&] { return launch_decode(a, st); });
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  if (a.max_splits > 1) {
+    e = timed_launch(ctx, AIHOST_KERNEL_COMBINE, st, [&] { return launch_decode_combine(a, st); });
+    if (e != cudaSuccess) return cuda_fail(e, "decode combine launch");
+  }
+  return AIHOST_OK;
+}
+
+aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const KvLayout& kv, float scale,
+                          int32_t batch, int32_t n_q, const void* q, const void* kc, const void* vc,
+                          const int32_t* seq_len, int32_t start_scalar, int32_t len_offset, int32_t rope_mode,
+                          void* out, cudaStream_t st) {
+  if (d->q_dtype != AIHOST_F16 || d->kv_dtype != AIHOST_F16)
+    return fail(AIHOST_EUNSUPPORTED, "prefill (n_new > 1) needs F16 q and F16 cache in this build");
+  if (!prefill_supported(d->head_dim)) return fail(AIHOST_EUNSUPPORTED, "prefill head_dim %d", d->head_dim);
+  PrefillArgs a;
+  memset(&a, 0, sizeof(a));
+  const int64_t D = d->head_dim, Hq = d->n_q_heads;
+  aihost_status s = encode_f16_map(&a.q_map, q, d->head_dim, Hq, n_q, batch, D * 2, Hq * D * 2,
+                                   static_cast<int64_t>(n_q) * Hq * D * 2, "q");
+  if (s != AIHOST_OK) return s;
+  s = encode_f16_map(&a.k_map, kc, d->head_dim, d->n_kv_heads, kv.capacity, batch, kv.head_stride, kv.token_stride,
+                     kv.seq_stride ? kv.seq_stride : kv.token_stride * kv.capacity, "k_cache");
+  if (s != AIHOST_OK) return s;
+  s = encode_f16_map(&a.v_map, vc, d->head_dim, d->n_kv_heads, kv.capacity, batch, kv.head_stride, kv.token_stride,
+                     kv.seq_stride ? kv.seq_stride : kv.token_stride * kv.capacity, "v_cache");
+  if (s != AIHOST_OK) return s;
+  a.q = q;
+  a.seq_len = seq_len;
+  a.start_scalar = start_scalar;
+  a.len_offset = len_offset;
+  a.batch = batch;
+  a.n_new = n_q;
+  a.n_q_heads = d->n_q_heads;
+  a.n_kv_heads = d->n_kv_heads;
+  a.head_dim = d->head_dim;
+  a.scale = scale;
+  a.rope_mode = rope_mode;
+  if (rope_mode != AIHOST_ROPE_NONE) a.freqs = make_freqs(d->rope_theta, d->head_dim);
+  a.out = out;
+  a.out_dtype = d->out_dtype;
+  a.status = ctx->d_status;
+  cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_PREFILL, st, [&] { return launch_prefill(a, st); });
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return AIHOST_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t aihost_attn_abi_version(void) { return AIHOST_ATTN_ABI_VERSION; }
+
+const char* aihost_attn_last_error(void) { return g_err; }
+
+aihost_status aihost_attn_create(int32_t device, aihost_attn_ctx** out_ctx) {
+  if (!out_ctx) return fail(AIHOST_EINVAL, "out_ctx is NULL");
+  *out_ctx = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return fail(AIHOST_EINVAL, "device %d out of range (%d devices)", device, n);
+  DeviceGuard g(device);
+  if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", device);
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+  if (prop.major != 10) return fail(AIHOST_EUNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device,
+                                    prop.major, prop.minor);
+  auto* ctx = new aihost_attn_ctx();
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  e = cudaMalloc(&ctx->d_status, sizeof(int32_t));
+  if (e != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(e, "cudaMalloc(status)");
+  }
+  e = cudaMemset(ctx->d_status, 0, sizeof(int32_t));
+  if (e != cudaSuccess) {
+    cudaFree(ctx->d_status);
+    delete ctx;
+    return cuda_fail(e, "cudaMemset(status)");
+  }
+  *out_ctx = ctx;
+  return AIHOST_OK;
+}
+
+aihost_status aihost_attn_destroy(aihost_attn_ctx* ctx) {
+  if (!ctx) return AIHOST_OK;
+  DeviceGuard g(ctx->device);
+  for (auto& slot : ctx->prof)
+    for (auto& pr : slot.pending) {
+      cudaEventDestroy(pr.first);
+      cudaEventDestroy(pr.second);
+    }
+  for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
+  cudaFree(ctx->scratch);
+  cudaFree(ctx->d_status);
+  delete ctx;
+  return AIHOST_OK;
+}
+
+aihost_status aihost_attn_workspace_size(const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
+                                         size_t* out_bytes) {
+  if (!out_bytes) return fail(AIHOST_EINVAL, "out_bytes is NULL");
+  KvLayout kv;
+  float scale;
+  aihost_status s = check_desc(desc, &kv, &scale);
+  if (s != AIHOST_OK) return s;
+  if (batch < 1 || n_new < 1) return fail(AIHOST_EINVAL, "batch (%d) and n_new (%d) must be >= 1", batch, n_new);
+  *out_bytes = 0;
+  if (n_new == 1) {
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    DecodePlan p = plan_decode(desc, batch, sms);
+    *out_bytes = decode_scratch_bytes(batch, desc->n_q_heads, desc->head_dim, p.max_splits);
+  }
+  return AIHOST_OK;
+}
+
+aihost_status aihost_attn_reserve(aihost_attn_ctx* ctx, size_t bytes) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  if (bytes <= ctx->scratch_bytes) return AIHOST_OK;
+  DeviceGuard g(ctx->device);
+  if (ctx->scratch) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize before scratch resize");
+    cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+  }
+  cudaError_t e = cudaMalloc(&ctx->scratch, bytes);
+  if (e != cudaSuccess) {
+    ctx->scratch = nullptr;
+    return fail(AIHOST_ENOMEM, "cudaMalloc(%zu) for scratch failed: %s", bytes, cudaGetErrorString(e));
+  }
+  ctx->scratch_bytes = bytes;
+  return AIHOST_OK;
+}
+
+aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
+                                  int32_t n_new, const void* q, const void* k_new, const void* v_new,
+                                  void* k_cache, void* v_cache, const int32_t* seq_len,
+                                  const int32_t* h_seq_len, void* out, void* stream) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  KvLayout kv;
+  float scale;
+  s = check_desc(desc, &kv, &scale);
+  if (s != AIHOST_OK) return s;
+  if (batch < 1 || n_new < 1) return fail(AIHOST_EINVAL, "batch (%d) and n_new (%d) must be >= 1", batch, n_new);
+  if (!q || !k_new || !v_new || !k_cache || !v_cache || !seq_len || !out)
+    return fail(AIHOST_EINVAL, "q, k_new, v_new, k_cache, v_cache, seq_len and out must be non-NULL");
+  if (!aligned(q, 16) || !aligned(k_new, 16) || !aligned(v_new, 16) || !aligned(out, 16) || !aligned(k_cache, 16) ||
+      !aligned(v_cache, 16) || !aligned(seq_len, 4))
+    return fail(AIHOST_EINVAL, "tensor pointers must be 16-byte aligned");
+  if (n_new > desc->kv_capacity) return fail(AIHOST_EINVAL, "n_new %d exceeds kv_capacity %d", n_new, desc->kv_capacity);
+  if (h_seq_len)
+    for (int32_t b = 0; b < batch; ++b)
+      if (h_seq_len[b] < 0 || static_cast<int64_t>(h_seq_len[b]) + n_new > desc->kv_capacity)
+        return fail(AIHOST_EINVAL, "sequence %d: %d cached + %d new rows exceed kv_capacity %d", b, h_seq_len[b],
+                    n_new, desc->kv_capacity);
+  DeviceGuard g(ctx->device);
+  if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_new > 1 && (desc->q_dtype != AIHOST_F16 || desc->kv_dtype != AIHOST_F16))
+    return fail(AIHOST_EUNSUPPORTED, "prefill (n_new > 1) needs F16 q and F16 cache in this build");
+  const RopeFreqs freqs = make_freqs(desc->rope_mode != AIHOST_ROPE_NONE ? desc->rope_theta : 1.0f, desc->head_dim);
+  cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_APPEND, st, [&] {
+    return launch_kv_append(k_new, v_new, desc->q_dtype, k_cache, v_cache, kv, seq_len, batch, n_new,
+                            desc->n_kv_heads, desc->head_dim, desc->rope_mode, freqs, ctx->d_status, st);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "kv append launch");
+  if (n_new == 1)
+    return run_decode(ctx, desc, kv, scale, batch, q, k_cache, v_cache, seq_len, 0, 1, desc->rope_mode, out, st);
+  return run_prefill(ctx, desc, kv, scale, batch, n_new, q, k_cache, v_cache, seq_len, 0, n_new, desc->rope_mode, out,
+                     st);
+}
+
+aihost_status aihost_attn_mha(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t n_q, int32_t n_kv,
+                              int32_t start_pos, const void* q, const void* k, const void* v, void* out,
+                              void* stream) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  KvLayout kv;
+  float scale;
+  s = check_desc(desc, &kv, &scale);
+  if (s != AIHOST_OK) return s;
+  if (n_q < 1 || n_kv < 1) return fail(AIHOST_EINVAL, "n_q (%d) and n_kv (%d) must be >= 1", n_q, n_kv);
+  if (n_kv > desc->kv_capacity) return fail(AIHOST_EINVAL, "n_kv %d exceeds kv_capacity %d", n_kv, desc->kv_capacity);
+  if (start_pos < 0 || (n_q > 1 && start_pos >= n_kv))
+    return fail(AIHOST_EINVAL, "start_pos %d outside [0, n_kv=%d)", start_pos, n_kv);
+  if (!q || !k || !v || !out) return fail(AIHOST_EINVAL, "q, k, v and out must be non-NULL");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
+    return fail(AIHOST_EINVAL, "tensor pointers must be 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_q == 1)  // FusedMHAGenerate: every row visible, no mask
+    return run_decode(ctx, desc, kv, scale, 1, q, k, v, nullptr, 0, n_kv, AIHOST_ROPE_NONE, out, st);
+  return run_prefill(ctx, desc, kv, scale, 1, n_q, q, k, v, nullptr, start_pos, n_kv - start_pos, AIHOST_ROPE_NONE,
+                     out, st);
+}
+
+aihost_status aihost_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
+                               int32_t start_pos, float theta, int32_t rope_mode, void* stream) {
+  if (!x) return fail(AIHOST_EINVAL, "x is NULL");
+  if (dtype != AIHOST_F32 && dtype != AIHOST_F16) return fail(AIHOST_EINVAL, "dtype %d must be F32 or F16", dtype);
+  if (seq < 0 || n_heads < 1 || head_dim < 2 || head_dim % 2 || head_dim > kMaxHeadDim)
+    return fail(AIHOST_EINVAL, "bad shape seq=%d n_heads=%d head_dim=%d", seq, n_heads, head_dim);
+  if (start_pos < 0) return fail(AIHOST_EINVAL, "start_pos must be >= 0");
+  if (rope_mode == AIHOST_ROPE_NONE) return AIHOST_OK;
+  if (rope_mode != AIHOST_ROPE_INTERLEAVED && rope_mode != AIHOST_ROPE_NEOX)
+    return fail(AIHOST_EINVAL, "rope_mode %d is not a valid aihost_rope_mode", rope_mode);
+  if (!(theta > 0.0f && isfinite(theta))) return fail(AIHOST_EINVAL, "theta must be a positive finite number");
+  cudaError_t e = launch_rope_full(x, dtype, seq, n_heads, head_dim, start_pos, rope_mode, make_freqs(theta, head_dim),
+                                   static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  return AIHOST_OK;
+}
+
+aihost_status aihost_kv_append(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
+                               const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                               const int32_t* seq_len, void* stream) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  KvLayout kv;
+  float scale;
+  s = check_desc(desc, &kv, &scale);
+  if (s != AIHOST_OK) return s;
+  if (batch < 1 || n_new < 1) return fail(AIHOST_EINVAL, "batch (%d) and n_new (%d) must be >= 1", batch, n_new);
+  if (!k_new || !v_new || !k_cache || !v_cache || !seq_len)
+    return fail(AIHOST_EINVAL, "k_new, v_new, k_cache, v_cache and seq_len must be non-NULL");
+  if (!aligned(k_new, 16) || !aligned(v_new, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16))
+    return fail(AIHOST_EINVAL, "tensor pointers must be 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const RopeFreqs freqs = make_freqs(1.0f, desc->head_dim);
+  cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_APPEND, st, [&] {
+    return launch_kv_append(k_new, v_new, desc->q_dtype, k_cache, v_cache, kv, seq_len, batch, n_new,
+                            desc->n_kv_heads, desc->head_dim, AIHOST_ROPE_NONE, freqs, ctx->d_status, st);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "kv append launch");
+  return AIHOST_OK;
+}
+
+aihost_status aihost_attn_profiler_enable(aihost_attn_ctx* ctx, int32_t enable) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  std::lock_guard<std::mutex> lk(ctx->prof_mu);
+  ctx->profiling = enable != 0;
+  return AIHOST_OK;
+}
+
+aihost_status aihost_attn_profiler_read(aihost_attn_ctx* ctx, int32_t kernel, int64_t* launches, double* total_ms) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  if (kernel < 0 || kernel >= AIHOST_KERNEL_COUNT) return fail(AIHOST_EINVAL, "kernel id %d out of range", kernel);
+  DeviceGuard g(ctx->device);
+  std::lock_guard<std::mutex> lk(ctx->prof_mu);
+  ProfSlot& slot = ctx->prof[kernel];
+  for (auto& pr : slot.pending) {
+    cudaError_t e = cudaEventSynchronize(pr.second);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize(profiler)");
+    float ms = 0.0f;
+    e = cudaEventElapsedTime(&ms, pr.first, pr.second);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventElapsedTime(profiler)");
+    slot.total_ms += ms;
+    slot.launches += 1;
+    ctx->event_pool.push_back(pr.first);
+    ctx->event_pool.push_back(pr.second);
+  }
+  slot.pending.clear();
+  if (launches) *launches = slot.launches;
+  if (total_ms) *total_ms = slot.total_ms;
+  return AIHOST_OK;
+}
+
+aihost_status aihost_attn_profiler_reset(aihost_attn_ctx* ctx) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  for (int k = 0; k < AIHOST_KERNEL_COUNT; ++k) {
+    s = aihost_attn_profiler_read(ctx, k, nullptr, nullptr);
+    if (s != AIHOST_OK) return s;
+    std::lock_guard<std::mutex> lk(ctx->prof_mu);
+    ctx->prof[k].launches = 0;
+    ctx->prof[k].total_ms = 0.0;
+  }
+  return AIHOST_OK;
+}
+
+aihost_status aihost_attn_sync_status(aihost_attn_ctx* ctx, int32_t* out_bits) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  DeviceGuard g(ctx->device);
+  if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int32_t bits = 0;
+  e = cudaMemcpy(&bits, ctx->d_status, sizeof(bits), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  e = cudaMemset(ctx->d_status, 0, sizeof(int32_t));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
+  if (out_bits) *out_bits = bits;
+  if (bits & kStatusWaitTimeout) return fail(AIHOST_ETIMEOUT, "a kernel's bounded wait expired (status 0x%x)", bits);
+  if (bits & kStatusBadLength) return fail(AIHOST_EINVAL, "a device-side sequence length exceeded kv_capacity");
+  return AIHOST_OK;
+}
+
+}  // extern "C"

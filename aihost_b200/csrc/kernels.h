@@ -1,0 +1,86 @@
+// kernels.h — host-side launch interface between the C-ABI layer (api.cu) and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace aihost {
+
+constexpr int kMaxHeadDim = 256;
+
+// RoPE frequencies of one call, computed on the host as 1 / powf(theta, 2i / d) so that every
+// kernel uses bit-identical angles (ComputeShaders.cs:536); passed by value.
+struct RopeFreqs {
+  float f[kMaxHeadDim / 2];
+};
+
+// Resolved cache geometry (bytes).
+struct KvLayout {
+  int64_t seq_stride, token_stride, head_stride;
+  int32_t capacity;
+  int32_t dtype;  // aihost_dtype
+};
+
+// ---------------------------------------------------------------- rope_append.cu
+// In-place RoPE of x [seq, n_heads, head_dim] (ApplyRoPEFull).
+cudaError_t launch_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
+                             int32_t start_pos, int32_t rope_mode, const RopeFreqs& freqs, cudaStream_t st);
+
+// Append k_new/v_new [batch][n_new][Hkv][d] into cache rows [seq_len[b], seq_len[b]+n_new),
+// rotating K when rope_mode != NONE. Records kStatusBadLength when a row would exceed capacity.
+cudaError_t launch_kv_append(const void* k_new, const void* v_new, int32_t in_dtype, void* k_cache,
+                             void* v_cache, const KvLayout& kv, const int32_t* seq_len, int32_t batch,
+                             int32_t n_new, int32_t n_kv_heads, int32_t head_dim, int32_t rope_mode,
+                             const RopeFreqs& freqs, int32_t* status, cudaStream_t st);
+
+// ---------------------------------------------------------------- decode.cu
+struct DecodeArgs {
+  const void* q;            // [batch][Hq][d], q_dtype
+  int32_t q_dtype;
+  const void* k_cache;
+  const void* v_cache;
+  KvLayout kv;
+  const int32_t* seq_len;   // device; NULL -> every sequence starts at start_scalar
+  int32_t start_scalar;
+  int32_t len_offset;       // attended rows = start + len_offset
+  int32_t rope_pos_offset;  // q position = seq_len[b] + rope_pos_offset
+  int32_t batch, n_q_heads, n_kv_heads, head_dim;
+  float scale;
+  int32_t rope_mode;
+  RopeFreqs freqs;
+  int32_t chunk;            // tokens per split
+  int32_t max_splits;       // grid.x
+  float* part_o;            // [batch][Hq][max_splits][d]   (scratch)
+  float* part_ml;           // [batch][Hq][max_splits][2]   (scratch)
+  void* out;                // [batch][Hq][d], out_dtype
+  int32_t out_dtype;
+  int32_t* status;
+};
+size_t decode_scratch_bytes(int32_t batch, int32_t n_q_heads, int32_t head_dim, int32_t max_splits);
+// Split kernel; writes the output directly for sequences that fit in one split.
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t st);
+// Merge of the per-split partials (only needed when max_splits > 1).
+cudaError_t launch_decode_combine(const DecodeArgs& a, cudaStream_t st);
+
+// ---------------------------------------------------------------- prefill_sm100.cu
+struct PrefillArgs {
+  const void* q;            // [batch][S][Hq][d] fp16
+  CUtensorMap q_map;        // dims {d, Hq, S, batch}
+  CUtensorMap k_map;        // dims {d, Hkv, capacity, batch} over the cache
+  CUtensorMap v_map;
+  const int32_t* seq_len;   // device: rows cached before this call (start position)
+  int32_t start_scalar;     // used when seq_len is NULL
+  int32_t len_offset;       // attended rows = seq_len[b] + len_offset (n_new for forward, 0 for mha)
+  int32_t batch, n_new, n_q_heads, n_kv_heads, head_dim;
+  float scale;
+  int32_t rope_mode;        // applied to Q inside the kernel
+  RopeFreqs freqs;
+  void* out;                // [batch][S][Hq][d]
+  int32_t out_dtype;
+  int32_t* status;
+};
+bool prefill_supported(int32_t head_dim);
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st);
+
+}  // namespace aihost

@@ -1,0 +1,179 @@
+// rope_append.cu — RoPE and KV-cache append kernels.
+//
+// rope_full_kernel   : ComputeOps.ApplyRoPEFull (ComputeOps.cs:959-979, shader
+//                      ComputeShaders.cs:517-543), in place, one thread per rotation pair.
+// kv_append_kernel   : KVCache.Add (Inference/InferenceEngine.cs:598-622) into a preallocated
+//                      cache instead of a Concat copy of the whole cache per token; optionally
+//                      rotates K on the way (the ComputeOps.cs:1283 RoPE of the new K), and
+//                      converts to the cache dtype (fp32 copy, fp16 round-to-nearest-even, or
+//                      GGUF Q8_0 quantisation with ggml's reference rule d = amax/127,
+//                      q = roundf(x * (1/d)), d stored as fp16).
+// Rotation arithmetic uses explicitly rounded multiplies/adds (no FMA contraction), so a
+// kernel and a CPU restatement that see the same cos/sin produce the same bits.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace aihost {
+namespace {
+
+__device__ __forceinline__ void rotate_pair(float& x1, float& x2, float c, float s) {
+  const float a = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+  const float b = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+  x1 = a;
+  x2 = b;
+}
+
+template <typename T>
+__global__ void rope_full_kernel(T* __restrict__ x, int32_t seq, int32_t n_heads, int32_t head_dim,
+                                 int32_t start_pos, int32_t rope_mode, RopeFreqs freqs) {
+  const int32_t half = head_dim / 2;
+  const int64_t total = static_cast<int64_t>(seq) * n_heads * half;
+  for (int64_t gid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gid < total;
+       gid += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t pair = static_cast<int32_t>(gid % half);
+    const int64_t row = gid / half;  // = s * n_heads + h
+    const int32_t s = static_cast<int32_t>(row / n_heads);
+    const float angle = __fmul_rn(static_cast<float>(start_pos + s), freqs.f[pair]);
+    float sn, cs;
+    sincosf(angle, &sn, &cs);
+    const int32_t i1 = rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
+    const int32_t i2 = rope_mode == AIHOST_ROPE_NEOX ? pair + half : 2 * pair + 1;
+    T* base = x + row * head_dim;
+    float x1 = ld_as_float(base + i1), x2 = ld_as_float(base + i2);
+    rotate_pair(x1, x2, cs, sn);
+    st_from_float(base + i1, x1);
+    st_from_float(base + i2, x2);
+  }
+}
+
+__device__ __forceinline__ float load_in(const float* p) { return *p; }
+__device__ __forceinline__ float load_in(const __half* p) { return __half2float(*p); }
+
+// One warp per (batch, token, kv head) row; lane l holds elements [l*E, l*E+E), E = D/32.
+// blockIdx.y selects K (0, rotated) or V (1).
+template <typename Tin, int D>
+__global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __restrict__ v_new,
+                                 uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache, KvLayout kv,
+                                 const int32_t* __restrict__ seq_len, int32_t batch, int32_t n_new,
+                                 int32_t n_kv_heads, int32_t rope_mode, RopeFreqs freqs, int32_t* status) {
+  constexpr int E = D / 32;
+  const int32_t lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t rows = static_cast<int64_t>(batch) * n_new * n_kv_heads;
+  if (row >= rows) return;
+  const bool is_k = blockIdx.y == 0;
+  const int32_t h = static_cast<int32_t>(row % n_kv_heads);
+  const int32_t s = static_cast<int32_t>((row / n_kv_heads) % n_new);
+  const int32_t b = static_cast<int32_t>(row / (static_cast<int64_t>(n_kv_heads) * n_new));
+  const int32_t start = seq_len[b];
+  const int32_t t = start + s;
+  if (start < 0 || t >= kv.capacity) {
+    if (lane == 0 && is_k && s == 0 && h == 0) atomicOr(status, kStatusBadLength);
+    return;
+  }
+  const Tin* src = (is_k ? k_new : v_new) + row * D + lane * E;
+  float x[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = load_in(src + e);
+
+  if (is_k && rope_mode != AIHOST_ROPE_NONE) {
+    const float pos = static_cast<float>(t);
+    if (rope_mode == AIHOST_ROPE_INTERLEAVED) {
+#pragma unroll
+      for (int e = 0; e < E; e += 2) {
+        const int pair = (lane * E + e) >> 1;
+        float sn, cs;
+        sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
+        rotate_pair(x[e], x[e + 1], cs, sn);
+      }
+    } else {  // NEOX: element i pairs with i + D/2, which lives in lane ^ 16
+      const bool lo = lane < 16;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+        const int pair = (lane & 15) * E + e;
+        float sn, cs;
+        sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
+        float x1 = lo ? x[e] : other, x2 = lo ? other : x[e];
+        rotate_pair(x1, x2, cs, sn);
+        x[e] = lo ? x1 : x2;
+      }
+    }
+  }
+
+  uint8_t* dst = (is_k ? k_cache : v_cache) + b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride +
+                 static_cast<int64_t>(h) * kv.head_stride;
+  if (kv.dtype == AIHOST_F32) {
+    float* d = reinterpret_cast<float*>(dst) + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; ++e) d[e] = x[e];
+  } else if (kv.dtype == AIHOST_F16) {
+    __half* d = reinterpret_cast<__half*>(dst) + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; ++e) d[e] = __float2half_rn(x[e]);
+  } else {  // Q8_0: 32 values per block = 32/E lanes
+    constexpr int LPB = 32 / E;
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) amax = fmaxf(amax, fabsf(x[e]));
+#pragma unroll
+    for (int off = 1; off < LPB; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float dsc = __fdiv_rn(amax, 127.0f);
+    const float id = dsc != 0.0f ? __frcp_rn(dsc) : 0.0f;
+    const int blk = lane / LPB, sub = lane % LPB;
+    uint8_t* bp = dst + blk * 34;
+    if (sub == 0) {
+      const __half hd = __float2half_rn(dsc);
+      const uint16_t bits = __half_as_ushort(hd);
+      bp[0] = static_cast<uint8_t>(bits & 0xffu);
+      bp[1] = static_cast<uint8_t>(bits >> 8);
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) bp[2 + sub * E + e] = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[e], id))));
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
+                             int32_t start_pos, int32_t rope_mode, const RopeFreqs& freqs, cudaStream_t st) {
+  const int64_t total = static_cast<int64_t>(seq) * n_heads * (head_dim / 2);
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t want = (total + threads - 1) / threads;
+  const int blocks = static_cast<int>(want < 148 * 64 ? want : 148 * 64);
+  if (dtype == AIHOST_F32)
+    rope_full_kernel<float><<<blocks, threads, 0, st>>>(static_cast<float*>(x), seq, n_heads, head_dim, start_pos,
+                                                        rope_mode, freqs);
+  else
+    rope_full_kernel<__half><<<blocks, threads, 0, st>>>(static_cast<__half*>(x), seq, n_heads, head_dim, start_pos,
+                                                         rope_mode, freqs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_kv_append(const void* k_new, const void* v_new, int32_t in_dtype, void* k_cache,
+                             void* v_cache, const KvLayout& kv, const int32_t* seq_len, int32_t batch,
+                             int32_t n_new, int32_t n_kv_heads, int32_t head_dim, int32_t rope_mode,
+                             const RopeFreqs& freqs, int32_t* status, cudaStream_t st) {
+  const int64_t rows = static_cast<int64_t>(batch) * n_new * n_kv_heads;
+  if (rows == 0) return cudaSuccess;
+  const int warps = 8;
+  dim3 grid(static_cast<unsigned>((rows + warps - 1) / warps), 2);
+  auto* kc = static_cast<uint8_t*>(k_cache);
+  auto* vc = static_cast<uint8_t*>(v_cache);
+#define AIHOST_APPEND(TIN, DD)                                                                                   \
+  kv_append_kernel<TIN, DD><<<grid, warps * 32, 0, st>>>(static_cast<const TIN*>(k_new),                         \
+                                                         static_cast<const TIN*>(v_new), kc, vc, kv, seq_len, \
+                                                         batch, n_new, n_kv_heads, rope_mode, freqs, status)
+  if (in_dtype == AIHOST_F32) {
+    if (head_dim == 64) AIHOST_APPEND(float, 64);
+    else AIHOST_APPEND(float, 128);
+  } else {
+    if (head_dim == 64) AIHOST_APPEND(__half, 64);
+    else AIHOST_APPEND(__half, 128);
+  }
+#undef AIHOST_APPEND
+  return cudaGetLastError();
+}
+
+}  // namespace aihost

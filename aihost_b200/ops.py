@@ -1,0 +1,246 @@
+"""Reference-shaped operator surface over libaihost_attn.so.
+
+Mirrors the C# calls the reference's transformer formats make for attention
+(AIHost/AIHost/Compute/ComputeOps.cs and Inference/InferenceEngine.cs):
+
+  ComputeOps.ApplyRoPEFull(tensor, startPosition, numHeads, headDim, theta)  -> apply_rope_full
+  ComputeOps.MultiHeadAttention(Q, K, V, numHeads, startPosition)            -> multi_head_attention
+  ComputeOps.FusedMHAGenerate(Q, K, V, numQHeads, numKvHeads, headDim, scale) -> fused_mha_generate
+  KVCache.Add(layer, K, V) / KVCache.Get(layer) / KVCache.SequenceLength     -> KVCache
+  TransformerLayer's RoPE(Q), RoPE(K), Add, Get, MultiHeadAttention sequence
+  (ComputeOps.cs:1282-1304)                                                  -> attention_layer
+
+Tensors are torch CUDA tensors used only as device memory; every computation runs in the
+library's CUDA kernels. Argument errors surface as AttnError (the C# side throws
+ArgumentException / CudaException for the same cases).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import (F16, F32, Q8_0, ROPE_INTERLEAVED, ROPE_NONE, AttnDesc, AttnError, EINVAL, check, lib)
+
+_TORCH_CODES = {torch.float32: F32, torch.float16: F16}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _TORCH_CODES[t.dtype]
+    except KeyError:
+        raise AttnError(EINVAL, f"unsupported tensor dtype {t.dtype} (float32 or float16)") from None
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def row_bytes(kv_dtype: int, head_dim: int) -> int:
+    return {F32: 4 * head_dim, F16: 2 * head_dim, Q8_0: 34 * (head_dim // 32)}[kv_dtype]
+
+
+@dataclass
+class LayerSpec:
+    """One attention layer's description (aihost_attn_desc)."""
+
+    n_q_heads: int
+    n_kv_heads: int
+    head_dim: int
+    rope_theta: float = 10000.0
+    rope_mode: int = ROPE_INTERLEAVED
+    scale: float = 0.0
+    q_dtype: int = F16
+    kv_dtype: int = F16
+    out_dtype: int = F16
+    kv_capacity: int = 1
+    kv_seq_stride: int = 0
+    kv_token_stride: int = 0
+    kv_head_stride: int = 0
+
+    def desc(self) -> AttnDesc:
+        return AttnDesc(self.n_q_heads, self.n_kv_heads, self.head_dim, self.rope_theta, self.rope_mode, self.scale,
+                        self.q_dtype, self.kv_dtype, self.out_dtype, self.kv_capacity, self.kv_seq_stride,
+                        self.kv_token_stride, self.kv_head_stride)
+
+
+class Context:
+    """aihost_attn_ctx: device binding plus split-K scratch."""
+
+    def __init__(self, device: int = 0):
+        self._h = ctypes.c_void_p()
+        check(lib().aihost_attn_create(int(device), ctypes.byref(self._h)))
+        self.device = device
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if not self._h:
+            raise AttnError(EINVAL, "context is closed")
+        return self._h
+
+    def reserve_for(self, spec: LayerSpec, batch: int, n_new: int) -> None:
+        need = ctypes.c_size_t()
+        d = spec.desc()
+        check(lib().aihost_attn_workspace_size(ctypes.byref(d), batch, n_new, ctypes.byref(need)))
+        if need.value:
+            check(lib().aihost_attn_reserve(self.handle, need.value))
+
+    def sync_status(self) -> int:
+        bits = ctypes.c_int32()
+        check(lib().aihost_attn_sync_status(self.handle, ctypes.byref(bits)))
+        return bits.value
+
+    def profiler(self, enable: bool) -> None:
+        """Bracket every kernel launch with CUDA events (device time per kernel kind)."""
+        check(lib().aihost_attn_profiler_enable(self.handle, int(enable)))
+
+    def profiler_read(self, kernel: int) -> tuple[int, float]:
+        """(launches, total device ms) of one aihost_kernel kind since the last reset (synchronises)."""
+        n, ms = ctypes.c_int64(), ctypes.c_double()
+        check(lib().aihost_attn_profiler_read(self.handle, kernel, ctypes.byref(n), ctypes.byref(ms)))
+        return n.value, ms.value
+
+    def profiler_reset(self) -> None:
+        check(lib().aihost_attn_profiler_reset(self.handle))
+
+    def close(self) -> None:
+        if self._h:
+            lib().aihost_attn_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class KVCache:
+    """Preallocated KV cache for `n_layers` layers and `batch` sequences.
+
+    Layout per layer (the reference's token-major [rows, Hkv*d], InferenceEngine.cs:582-625):
+    [batch][capacity][n_kv_heads][head_dim] in `kv_dtype` (Q8_0: GGUF blocks, stored as bytes).
+    `add` copies new rows in place instead of the reference's Concat of old and new rows.
+    """
+
+    def __init__(self, ctx: Context, spec: LayerSpec, batch: int = 1, n_layers: int = 1, device=None):
+        self.ctx, self.spec, self.batch = ctx, spec, batch
+        dev = device if device is not None else torch.device("cuda", ctx.device)
+        nbytes = batch * spec.kv_capacity * spec.n_kv_heads * row_bytes(spec.kv_dtype, spec.head_dim)
+        self.k = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(n_layers)]
+        self.v = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(n_layers)]
+        self.seq_len = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.host_len = [0] * batch
+
+    @property
+    def sequence_length(self) -> int:
+        """KVCache.SequenceLength of sequence 0."""
+        return self.host_len[0]
+
+    def add(self, layer: int, k: torch.Tensor, v: torch.Tensor, stream=None) -> None:
+        """KVCache.Add: append k, v [batch, n_new, Hkv, d] (already rotated) after the cached rows."""
+        n_new = k.shape[1]
+        if any(n + n_new > self.spec.kv_capacity for n in self.host_len):
+            raise AttnError(EINVAL, "KV cache capacity exceeded")
+        spec = LayerSpec(**{**self.spec.__dict__, "q_dtype": dtype_code(k)})
+        d = spec.desc()
+        check(lib().aihost_kv_append(self.ctx.handle, ctypes.byref(d), self.batch, n_new, _ptr(k), _ptr(v),
+                                      _ptr(self.k[layer]), _ptr(self.v[layer]), _ptr(self.seq_len), _stream(stream)))
+
+    def advance(self, n_new: int) -> None:
+        """Commit n_new appended rows for every sequence (after the last layer of a step)."""
+        self.host_len = [n + n_new for n in self.host_len]
+        self.seq_len += n_new
+
+    def get(self, layer: int):
+        """KVCache.Get: the raw K and V byte buffers of one layer."""
+        return self.k[layer], self.v[layer]
+
+
+class ComputeOps:
+    """The attention subset of the reference's ComputeOps, executed by libaihost_attn."""
+
+    def __init__(self, ctx: Context, stream=None):
+        self.ctx, self.stream = ctx, stream
+
+    def apply_rope_full(self, tensor: torch.Tensor, start_position: int, num_heads: int, head_dim: int,
+                        theta: float = 10000.0, rope_mode: int = ROPE_INTERLEAVED) -> None:
+        """ApplyRoPEFull (ComputeOps.cs:959-979): rotate tensor [seq, num_heads*head_dim] in place."""
+        seq = tensor.shape[0]
+        check(lib().aihost_rope_full(_ptr(tensor), dtype_code(tensor), seq, num_heads, head_dim, int(start_position),
+                                     float(theta), rope_mode, _stream(self.stream)))
+
+    def multi_head_attention(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, num_heads: int,
+                             start_position: int = 0, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        """MultiHeadAttention (ComputeOps.cs:1055-1102) over rotated Q [S, Hq*d], K/V [Lk, Hkv*d]."""
+        seq, dq = Q.shape
+        head_dim = dq // num_heads
+        n_kv_heads = K.shape[1] // head_dim
+        out_dtype = out_dtype or Q.dtype
+        out = torch.empty(seq, dq, dtype=out_dtype, device=Q.device)
+        spec = LayerSpec(num_heads, n_kv_heads, head_dim, rope_mode=ROPE_NONE, q_dtype=dtype_code(Q),
+                         kv_dtype=dtype_code(K), out_dtype=dtype_code(out), kv_capacity=K.shape[0])
+        if seq == 1:
+            self.ctx.reserve_for(spec, 1, 1)
+        d = spec.desc()
+        check(lib().aihost_attn_mha(self.ctx.handle, ctypes.byref(d), seq, K.shape[0], int(start_position), _ptr(Q),
+                                    _ptr(K), _ptr(V), _ptr(out), _stream(self.stream)))
+        return out
+
+    def fused_mha_generate(self, Q, K, V, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                           scale: float) -> torch.Tensor:
+        """FusedMHAGenerate (ComputeOps.cs:1015-1043): one query row, every cached row visible."""
+        out = torch.empty(1, num_q_heads * head_dim, dtype=Q.dtype, device=Q.device)
+        spec = LayerSpec(num_q_heads, num_kv_heads, head_dim, rope_mode=ROPE_NONE, scale=scale, q_dtype=dtype_code(Q),
+                         kv_dtype=dtype_code(K), out_dtype=dtype_code(out), kv_capacity=K.shape[0])
+        self.ctx.reserve_for(spec, 1, 1)
+        d = spec.desc()
+        check(lib().aihost_attn_mha(self.ctx.handle, ctypes.byref(d), 1, K.shape[0], 0, _ptr(Q), _ptr(K), _ptr(V),
+                                    _ptr(out), _stream(self.stream)))
+        return out
+
+    def attention_layer(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, cache: KVCache,
+                        layer: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The fused layer step (ComputeOps.cs:1282-1304): RoPE(Q), RoPE(K), KVCache.Add, MultiHeadAttention.
+
+        q [B, S, Hq, d], k_new / v_new [B, S, Hkv, d]. Rows are appended to `cache` for this layer;
+        call cache.advance(S) once all layers of the step ran.
+        """
+        B, S = q.shape[0], q.shape[1]
+        spec = cache.spec
+        if out is None:
+            odt = torch.float32 if spec.out_dtype == F32 else torch.float16
+            out = torch.empty(B, S, spec.n_q_heads, spec.head_dim, dtype=odt, device=q.device)
+        if S == 1:
+            self.ctx.reserve_for(spec, B, 1)
+        d = spec.desc()
+        # host copy of the lengths (sizes the grid); None -> the library plans from kv_capacity
+        hl = (ctypes.c_int32 * B)(*cache.host_len) if cache.host_len is not None else None
+        check(lib().aihost_attn_forward(self.ctx.handle, ctypes.byref(d), B, S, _ptr(q), _ptr(k_new), _ptr(v_new),
+                                        _ptr(cache.k[layer]), _ptr(cache.v[layer]), _ptr(cache.seq_len),
+                                        ctypes.cast(hl, ctypes.c_void_p) if hl is not None else None, _ptr(out),
+                                        _stream(self.stream)))
+        return out
+
+
+def default_scale(head_dim: int) -> float:
+    """1.0f / MathF.Sqrt(headDim) in fp32 (ComputeOps.cs:1065)."""
+    import numpy as np
+
+    return float(np.float32(1.0) / np.sqrt(np.float32(head_dim)))
+
+
+__all__ = ["Context", "LayerSpec", "KVCache", "ComputeOps", "dtype_code", "row_bytes", "default_scale", "math"]

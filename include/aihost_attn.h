@@ -1,0 +1,163 @@
+/*
+ * aihost_attn.h — C ABI of libaihost_attn.so, the B200 (sm_100a) attention op for AIHost.
+ *
+ * This library replaces, for one hot path, what AIHost's C# compute layer does through
+ * `ComputeOps` on a GPU backend:
+ *
+ *   ApplyRoPEFull(Q) ; ApplyRoPEFull(K) ; KVCache.Add(layer, K, V) ; KVCache.Get(layer) ;
+ *   MultiHeadAttention(Q, cachedK, cachedV, numHeads, position)
+ *
+ * (AIHost/AIHost/Compute/ComputeOps.cs:1279-1304, Formats/CombinedQKVFormat.cs:52-67,
+ *  Formats/QwenHybridFormat.cs:141-145). The reference dispatches these as GLSL compute shaders
+ * through Vulkan; its CUDA backend (ICompute/CUDA/CudaComputeCommandQueue.cs:56-61) cannot
+ * dispatch at all. A C# host binds the functions below with [DllImport("aihost_attn")]; the
+ * binding is listed in INTEGRATION.md.
+ *
+ * Conventions (mirroring ICompute/CUDA/CudaApi.cs:11-92, where every native call returns an
+ * error enum that the caller checks):
+ *   - every function returns an aihost_status; no exception or abort crosses the ABI;
+ *   - aihost_attn_last_error() gives a thread-local message for the last failure;
+ *   - all tensor pointers are raw device pointers (CUdeviceptr, IComputeBuffer.GetPointer()),
+ *     owned by the caller; the library never frees or retains them past the call;
+ *   - work is enqueued on the caller's cudaStream_t (passed as void*, NULL = legacy stream);
+ *     calls are asynchronous with respect to the host, like Dispatch() before Flush();
+ *   - the library allocates nothing inside the attention calls: split-K scratch is owned by
+ *     the context and sized once by aihost_attn_reserve().
+ *
+ * Layouts (reference KVCache, Inference/InferenceEngine.cs:582-625, is one fp32 tensor
+ * [rows, n_kv_heads*head_dim] per layer for K and one for V, token-major):
+ *   q, out          [batch][n_new][n_q_heads][head_dim]      (= reference [S, Hq*d] per sequence)
+ *   k_new, v_new    [batch][n_new][n_kv_heads][head_dim]
+ *   k_cache,v_cache element (b, t, h, i) at byte offset
+ *                     b*kv_seq_stride + t*kv_token_stride + h*kv_head_stride + bytes(i)
+ *                   defaults (strides 0): token-major, kv_capacity rows per sequence.
+ *   Q8_0 caches hold GGUF blocks {fp16 d; int8 qs[32]} (34 bytes per 32 values,
+ *   GGUF/GGUFTensorInfo.cs:64), head_dim/32 blocks per (token, head).
+ */
+#ifndef AIHOST_ATTN_H
+#define AIHOST_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AIHOST_ATTN_ABI_VERSION 1
+
+typedef enum {
+  AIHOST_OK = 0,
+  AIHOST_EINVAL = 1,        /* bad argument: null pointer, bad dims, misaligned pointer, ... */
+  AIHOST_ENOMEM = 2,        /* context reservation failed, or scratch too small for a call */
+  AIHOST_ECUDA = 3,         /* a CUDA runtime/driver call failed */
+  AIHOST_ETIMEOUT = 4,      /* a bounded device-side wait expired (status word set by a kernel) */
+  AIHOST_EUNSUPPORTED = 5,  /* valid request this build does not implement (e.g. head_dim 96) */
+  AIHOST_ENCCL = 6          /* a collective failed */
+} aihost_status;
+
+/* Element types; the numeric values are AIHost's DataType ordinals
+ * (ICompute/IComputeBuffer.cs:57-76: F32=0, F16=1, Q8_0=6). */
+typedef enum { AIHOST_F32 = 0, AIHOST_F16 = 1, AIHOST_Q8_0 = 6 } aihost_dtype;
+
+/* RoPE pairing. INTERLEAVED is the reference's (x[2i], x[2i+1]) pairing used by every
+ * architecture in AIHost (Compute/ComputeShaders.cs:517-543). NEOX pairs (x[i], x[i+d/2]).
+ * NONE skips rotation (inputs already rotated). */
+typedef enum { AIHOST_ROPE_INTERLEAVED = 0, AIHOST_ROPE_NEOX = 1, AIHOST_ROPE_NONE = 2 } aihost_rope_mode;
+
+/* One attention layer's static description. The fields are the GGUF metadata the reference
+ * reads in Compute/TransformerBase.cs:72-80 (head_count, head_count_kv, rope.freq_base). */
+typedef struct {
+  int32_t n_q_heads;        /* Hq */
+  int32_t n_kv_heads;       /* Hkv; Hq % Hkv == 0, Q head h uses KV head h / (Hq/Hkv) */
+  int32_t head_dim;         /* d: 64 or 128 in this build */
+  float rope_theta;         /* frequency base; LlamaFormat passes none and gets 10000 */
+  int32_t rope_mode;        /* aihost_rope_mode */
+  float scale;              /* 0 -> 1/sqrtf(head_dim), as ComputeOps.cs:1065 */
+  int32_t q_dtype;          /* dtype of q, k_new, v_new: F32 or F16 */
+  int32_t kv_dtype;         /* cache dtype: F32, F16 or Q8_0 */
+  int32_t out_dtype;        /* F32 or F16 */
+  int32_t kv_capacity;      /* rows allocated per sequence in the cache */
+  int64_t kv_seq_stride;    /* bytes between sequences; 0 -> kv_capacity * kv_token_stride */
+  int64_t kv_token_stride;  /* bytes between tokens;    0 -> n_kv_heads * kv_head_stride */
+  int64_t kv_head_stride;   /* bytes between heads;     0 -> bytes of one head row */
+} aihost_attn_desc;
+
+typedef struct aihost_attn_ctx aihost_attn_ctx;
+
+/* Library version and the thread-local message of the last failing call on this thread. */
+int32_t aihost_attn_abi_version(void);
+const char* aihost_attn_last_error(void);
+
+/* Context: binds a CUDA device, owns split-K scratch and cached TMA descriptors.
+ * Replaces the per-call buffer creation of ComputeOps.FusedMHAGenerate (ComputeOps.cs:1015-1043). */
+aihost_status aihost_attn_create(int32_t device, aihost_attn_ctx** out_ctx);
+aihost_status aihost_attn_destroy(aihost_attn_ctx* ctx);
+
+/* Bytes of device scratch a forward call with these arguments needs (0 if none). */
+aihost_status aihost_attn_workspace_size(const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
+                                         size_t* out_bytes);
+/* Grow the context's scratch to at least `bytes` (the only allocating call besides create). */
+aihost_status aihost_attn_reserve(aihost_attn_ctx* ctx, size_t bytes);
+
+/* The fused op: RoPE(q) and RoPE(k_new) at positions seq_len[b] + s, append the rotated k_new
+ * and v_new into cache rows [seq_len[b], seq_len[b] + n_new), then attention of the n_new
+ * query rows over cache rows [0, seq_len[b] + n_new) with the causal rule j <= seq_len[b] + i
+ * (ComputeShaders.cs:545-561). n_new == 1 is decode (ComputeOps.cs:1069-1073, split-K kernel);
+ * n_new > 1 is prefill (ComputeOps.cs:1076-1101, tcgen05 kernel).
+ *   seq_len     device int32[batch]: rows already cached per sequence (= start position).
+ *   h_seq_len   optional host copy of seq_len (NULL allowed): only used to size the grid.
+ * q, k_new, v_new are not modified (the reference rotates Q and K in place; here the rotated
+ * values live only in registers and in the cache). */
+aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
+                                  int32_t n_new, const void* q, const void* k_new, const void* v_new,
+                                  void* k_cache, void* v_cache, const int32_t* seq_len,
+                                  const int32_t* h_seq_len, void* out, void* stream);
+
+/* ComputeOps.MultiHeadAttention(Q, K, V, numHeads, startPosition) (ComputeOps.cs:1055-1102):
+ * attention only, for one sequence, over K/V rows [0, n_kv) that are already rotated.
+ * q/out [n_q, Hq*d]; k/v laid out as desc (kv_capacity >= n_kv). rope_mode is ignored.
+ * n_q == 1 -> FusedMHAGenerate semantics (no mask); n_q > 1 -> causal j <= start_pos + i. */
+aihost_status aihost_attn_mha(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t n_q,
+                              int32_t n_kv, int32_t start_pos, const void* q, const void* k,
+                              const void* v, void* out, void* stream);
+
+/* ComputeOps.ApplyRoPEFull(tensor, startPosition, numHeads, headDim, theta)
+ * (ComputeOps.cs:959-979): in-place rotation of x [seq, n_heads*head_dim] (F32 or F16). */
+aihost_status aihost_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads,
+                               int32_t head_dim, int32_t start_pos, float theta, int32_t rope_mode,
+                               void* stream);
+
+/* KVCache.Add(layer, K, V) (Inference/InferenceEngine.cs:598-622) without the per-token
+ * reallocation: copies (and converts / Q8_0-quantises) k_new, v_new [batch][n_new][Hkv][d]
+ * into cache rows [seq_len[b], seq_len[b] + n_new). No rotation. */
+aihost_status aihost_kv_append(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
+                               const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                               const int32_t* seq_len, void* stream);
+
+/* Device-time profiler, the GPU-side counterpart of the reference's GlobalProfiler
+ * (AIHost/Compute/ComputeProfiler.cs:16-97, host Stopwatch totals by name). While enabled,
+ * every kernel the context launches is bracketed by CUDA events on the caller's stream;
+ * aihost_attn_profiler_read synchronises those events and returns the launch count and
+ * total device milliseconds of one kernel kind since the last reset. */
+typedef enum {
+  AIHOST_KERNEL_APPEND = 0,   /* RoPE(K) + cache append */
+  AIHOST_KERNEL_DECODE = 1,   /* split-K decode */
+  AIHOST_KERNEL_COMBINE = 2,  /* split merge */
+  AIHOST_KERNEL_PREFILL = 3,  /* tcgen05 prefill */
+  AIHOST_KERNEL_COUNT = 4
+} aihost_kernel;
+aihost_status aihost_attn_profiler_enable(aihost_attn_ctx* ctx, int32_t enable);
+aihost_status aihost_attn_profiler_read(aihost_attn_ctx* ctx, int32_t kernel, int64_t* launches, double* total_ms);
+aihost_status aihost_attn_profiler_reset(aihost_attn_ctx* ctx);
+
+/* Synchronise the context's device and read-and-clear the device status word that kernels
+ * set when a bounded wait expired (AIHOST_ETIMEOUT) or a device-side length exceeded
+ * kv_capacity (AIHOST_EINVAL). *out_bits receives the raw bits (may be NULL). */
+aihost_status aihost_attn_sync_status(aihost_attn_ctx* ctx, int32_t* out_bits);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AIHOST_ATTN_H */

@@ -1,0 +1,236 @@
+"""GPU parity of the fused op (RoPE + KV append + attention) against the CPU oracle.
+
+Every case runs libaihost_attn.so through its C ABI on cuda:0 and the oracle
+(oracle/attn_oracle.c, ORACLE_EXACT: double accumulation) on the same seeded inputs.
+Tolerances (max |gpu - oracle| over every output element):
+  fp16 inputs / fp16 cache:  2e-3   (the north-star bound for fp16 inputs)
+  fp32 inputs / fp32 cache:  2e-4
+  Q8_0 cache:                2e-3   (against the dequantise-then-attend oracle)
+Appended cache rows: V rows are bit-exact (fp16 round-to-nearest-even, fp32 copy, Q8_0 bytes);
+K rows go through RoPE, whose cos/sin come from CUDA's sincosf on the GPU and glibc on the CPU
+(1-ulp differences), so they are compared within one unit of the stored format.
+"""
+import numpy as np
+import pytest
+import torch
+
+from aihost_b200 import F16, F32, Q8_0, ROPE_INTERLEAVED, ROPE_NEOX, ROPE_NONE
+from aihost_b200.configs import CONFIGS, make_inputs
+from helpers import cache_rows, gpu_forward, max_abs, oracle_forward
+
+pytestmark = pytest.mark.gpu
+
+TOL = {F16: 2e-3, F32: 2e-4, Q8_0: 2e-3}
+
+
+def tol_for(cfg):
+    return TOL[Q8_0] if cfg.kv_dtype == Q8_0 else TOL[cfg.q_dtype]
+
+
+def check_call(ctx, cfg, pass_host_len=True, part=None, inp=None, check_cache=True):
+    inp = inp or make_inputs(cfg)
+    out, kc, vc = gpu_forward(ctx, cfg, inp, pass_host_len=pass_host_len)
+    ref, rkc, rvc = oracle_forward(cfg, inp, part=part)
+    out = out.float().numpy()
+    if part is not None:
+        b0, b1, h0, h1 = part
+        out, ref = out[b0:b1, :, h0:h1], ref[b0:b1, :, h0:h1]
+    err = max_abs(out, ref)
+    assert np.isfinite(out).all()
+    assert err <= tol_for(cfg), f"max |gpu - oracle| = {err:.3g} > {tol_for(cfg)}"
+    if check_cache:
+        lengths = inp["lengths"]
+        rows = [list(range(n, n + cfg.n_new)) for n in lengths]
+        cap = inp["capacity"]
+        bl = slice(None) if part is None else slice(part[0], part[1])
+        gv, rv = cache_rows(vc.numpy(), cfg, cap, rows)[bl], cache_rows(rvc, cfg, cap, rows)[bl]
+        assert np.array_equal(gv, rv), "appended V rows differ from the oracle"
+        if cfg.kv_dtype == Q8_0:
+            gvb = vc.numpy().reshape(cfg.batch, cap, -1)
+            rvb = rvc.reshape(cfg.batch, cap, -1)
+            for b in range(cfg.batch)[bl]:
+                assert np.array_equal(gvb[b, rows[b]], rvb[b, rows[b]]), "Q8_0 V blocks differ byte-wise"
+        gk, rk = cache_rows(kc.numpy(), cfg, cap, rows)[bl], cache_rows(rkc, cfg, cap, rows)[bl]
+        unit = {F32: 1e-5, F16: 2e-3}.get(cfg.kv_dtype, 0.03)
+        assert max_abs(gk, rk) <= unit * max(1.0, float(np.abs(rk).max())), "appended K rows differ"
+        # rows outside the appended range are untouched
+        before = kc.numpy().reshape(cfg.batch, cap, -1)
+        orig = inp["k_cache"].numpy().reshape(cfg.batch, cap, -1)
+        for b in range(cfg.batch)[bl]:
+            assert np.array_equal(before[b, :lengths[b]], orig[b, :lengths[b]])
+    return err
+
+
+# ---------------------------------------------------------------- decode (n_new == 1)
+
+def test_decode_cfg1_fp32_full(ctx):
+    check_call(ctx, CONFIGS[1])
+
+
+@pytest.mark.parametrize("hq,hkv", [(4, 4), (8, 2), (16, 2), (32, 2), (12, 4)])
+def test_decode_f16_gqa_ratios(ctx, hq, hkv):
+    cfg = CONFIGS[3].scaled(batch=3, n_q_heads=hq, n_kv_heads=hkv, cached_range=None, cached_list=[0, 700, 1999])
+    check_call(ctx, cfg)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("kv", [F32, F16, Q8_0])
+def test_decode_dtypes_dims(ctx, d, kv):
+    qd = F32 if kv == F32 else F16
+    cfg = CONFIGS[3].scaled(batch=2, n_q_heads=16, n_kv_heads=2, head_dim=d, q_dtype=qd, kv_dtype=kv, out_dtype=qd,
+                            cached_range=None, cached_list=[33, 1500])
+    check_call(ctx, cfg)
+
+
+@pytest.mark.parametrize("mode", [ROPE_NEOX, ROPE_NONE])
+def test_decode_rope_modes(ctx, mode):
+    cfg = CONFIGS[3].scaled(batch=2, rope_mode=mode, cached_range=None, cached_list=[100, 4097])
+    check_call(ctx, cfg)
+
+
+def test_decode_without_host_lengths(ctx):
+    cfg = CONFIGS[3].scaled(batch=4, cached_range=None, cached_list=[5, 300, 2048, 4095])
+    check_call(ctx, cfg, pass_host_len=False)
+
+
+def test_decode_cfg3_full_sample(ctx):
+    # full 64-sequence call on the GPU; oracle on sequences 0-3 (all heads)
+    check_call(ctx, CONFIGS[3], part=(0, 4, 0, 32))
+
+
+def test_decode_cfg5_q8_full_sample(ctx):
+    check_call(ctx, CONFIGS[5], part=(0, 2, 0, 64))
+
+
+def test_decode_stale_nan_rows_ignored(ctx):
+    """Cache rows past each sequence's length hold NaN bit patterns; they must not leak."""
+    cfg = CONFIGS[3].scaled(batch=2, n_q_heads=8, n_kv_heads=2, cached_range=None, cached_list=[40, 300])
+    inp = make_inputs(cfg, capacity=512)
+    for name in ("k_cache", "v_cache"):
+        c = inp[name].view(torch.float16).reshape(cfg.batch, 512, cfg.n_kv_heads, cfg.head_dim)
+        for b, n in enumerate(inp["lengths"]):
+            c[b, n + 1:] = float("nan")
+    check_call(ctx, cfg, inp=inp, check_cache=False)
+
+
+# ---------------------------------------------------------------- prefill (n_new > 1)
+
+def test_prefill_cfg2_full(ctx):
+    check_call(ctx, CONFIGS[2], part=(0, 1, 0, 14))
+
+
+@pytest.mark.parametrize("s", [2, 37, 128, 129, 300])
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_ragged(ctx, s, d):
+    cfg = CONFIGS[2].scaled(n_new=s, head_dim=d, n_q_heads=4, n_kv_heads=2, cached=0)
+    check_call(ctx, cfg)
+
+
+@pytest.mark.parametrize("cached", [[100], [1, 257]])
+def test_prefill_chunked(ctx, cached):
+    """Prefill after cached rows (chunked prefill): causal rule j <= P + i with P > 0."""
+    cfg = CONFIGS[2].scaled(batch=len(cached), n_new=150, n_q_heads=6, n_kv_heads=2, head_dim=128, cached=None,
+                            cached_list=cached)
+    check_call(ctx, cfg)
+
+
+@pytest.mark.parametrize("mode", [ROPE_NEOX, ROPE_NONE])
+def test_prefill_rope_modes(ctx, mode):
+    cfg = CONFIGS[2].scaled(n_new=200, n_q_heads=4, n_kv_heads=1, rope_mode=mode)
+    check_call(ctx, cfg)
+
+
+def test_prefill_f32_out(ctx):
+    cfg = CONFIGS[2].scaled(n_new=130, n_q_heads=2, n_kv_heads=1, out_dtype=F32)
+    check_call(ctx, cfg)
+
+
+def test_prefill_stale_nan_rows_ignored(ctx):
+    cfg = CONFIGS[2].scaled(n_new=100, n_q_heads=2, n_kv_heads=1, head_dim=128)
+    inp = make_inputs(cfg, capacity=256)
+    for name in ("k_cache", "v_cache"):
+        c = inp[name].view(torch.float16).reshape(1, 256, 1, 128)
+        c[0, 100:] = float("nan")
+    check_call(ctx, cfg, inp=inp, check_cache=False)
+
+
+# ---------------------------------------------------------------- reference-shaped ops
+
+def test_multi_head_attention_matches_reference_shapes(ctx):
+    """ComputeOps.MultiHeadAttention(Q, K, V, numHeads, startPosition) with already-rotated inputs."""
+    from aihost_b200 import gen
+    from aihost_b200.ops import ComputeOps
+    from oracle import oracle as orc
+
+    ops = ComputeOps(ctx)
+    for S, Lk, P, hq, hkv, d in [(1, 513, 512, 32, 4, 64), (96, 96, 0, 8, 2, 64), (64, 200, 136, 4, 4, 128)]:
+        q = gen.normal((S, hq * d), 7, "mq", dtype=torch.float16)
+        k = gen.normal((Lk, hkv * d), 7, "mk", dtype=torch.float16)
+        v = gen.normal((Lk, hkv * d), 7, "mv", dtype=torch.float16)
+        out = ops.multi_head_attention(q.cuda(), k.cuda(), v.cuda(), hq, P).cpu().float().numpy()
+        ref = orc.mha(q.float().numpy(), k.float().numpy(), v.float().numpy(), hq, P)
+        assert max_abs(out, ref) <= 2e-3
+
+
+def test_fused_mha_generate_fp32(ctx):
+    from aihost_b200 import gen
+    from aihost_b200.ops import ComputeOps, default_scale
+    from oracle import oracle as orc
+
+    ops = ComputeOps(ctx)
+    q = gen.normal((1, 32 * 64), 9, "gq", std=0.5)
+    k = gen.normal((513, 4 * 64), 9, "gk", std=0.5)
+    v = gen.normal((513, 4 * 64), 9, "gv", std=0.5)
+    out = ops.fused_mha_generate(q.cuda(), k.cuda(), v.cuda(), 32, 4, 64, default_scale(64)).cpu().numpy()
+    ref = orc.mha(q.numpy(), k.numpy(), v.numpy(), 32, 512)
+    assert max_abs(out, ref) <= 2e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("mode", [ROPE_INTERLEAVED, ROPE_NEOX])
+def test_apply_rope_full(ctx, dtype, mode):
+    from aihost_b200 import gen
+    from aihost_b200.ops import ComputeOps
+    from oracle import oracle as orc
+
+    x = gen.normal((33, 6 * 128), 11, "rope", dtype=dtype)
+    y = x.cuda()
+    ComputeOps(ctx).apply_rope_full(y, 4000, 6, 128, theta=5e5, rope_mode=mode)
+    ref = orc.rope_full(x.float().numpy(), 4000, 6, 128, 5e5, mode)
+    tol = 2e-5 if dtype == torch.float32 else 4e-3
+    assert max_abs(y.cpu().float().numpy(), ref) <= tol
+
+
+@pytest.mark.parametrize("kv", [F32, F16, Q8_0])
+def test_kv_append_exact(ctx, kv):
+    """KVCache.Add without rotation: the stored bytes equal the oracle's conversion / quantiser."""
+    from aihost_b200.ops import KVCache
+    from oracle import oracle as orc
+
+    cfg = CONFIGS[3].scaled(batch=2, n_new=5, n_q_heads=8, n_kv_heads=2, q_dtype=F32 if kv == F32 else F16,
+                            kv_dtype=kv, cached_range=None, cached_list=[3, 10], rope_mode=ROPE_NONE)
+    inp = make_inputs(cfg, capacity=32)
+    spec = cfg.spec(32)
+    cache = KVCache(ctx, spec, batch=2, device=torch.device("cuda", 0))
+    cache.k[0].copy_(inp["k_cache"])
+    cache.v[0].copy_(inp["v_cache"])
+    cache.seq_len.copy_(inp["seq_len"])
+    cache.host_len = list(inp["lengths"])
+    cache.add(0, inp["k_new"].cuda(), inp["v_new"].cuda())
+    torch.cuda.synchronize()
+    ctx.sync_status()
+    _, rk, rv = oracle_forward(cfg, inp)
+    assert np.array_equal(cache.k[0].cpu().numpy(), rk)
+    assert np.array_equal(cache.v[0].cpu().numpy(), rv)
+
+
+def test_device_length_over_capacity_reports_status(ctx):
+    """A device-side seq_len past kv_capacity is refused by the kernels and reported on sync."""
+    from aihost_b200 import AttnError, EINVAL
+
+    cfg = CONFIGS[3].scaled(batch=2, n_q_heads=8, n_kv_heads=2, cached_range=None, cached_list=[10, 20])
+    inp = make_inputs(cfg, capacity=64)
+    inp["seq_len"] = torch.tensor([10, 64], dtype=torch.int32)  # 64 + 1 > 64 rows
+    with pytest.raises(AttnError) as ei:
+        gpu_forward(ctx, cfg, inp, pass_host_len=False)
+    assert ei.value.status == EINVAL

@@ -121,15 +121,16 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
     const float dsc = __fdiv_rn(amax, 127.0f);
     const float id = dsc != 0.0f ? __frcp_rn(dsc) : 0.0f;
     const int blk = lane / LPB, sub = lane % LPB;
-    uint8_t* bp = dst + blk * 34;
-    if (sub == 0) {
-      const __half hd = __float2half_rn(dsc);
-      const uint16_t bits = __half_as_ushort(hd);
-      bp[0] = static_cast<uint8_t>(bits & 0xffu);
-      bp[1] = static_cast<uint8_t>(bits >> 8);
-    }
+    // Every field is stored with 16-bit stores: the row base, the 34-byte block stride and the
+    // 2-byte scale are all even, so each pair of bytes is 2-byte aligned.
+    uint16_t* bp = reinterpret_cast<uint16_t*>(dst + blk * 34);
+    if (sub == 0) bp[0] = __half_as_ushort(__float2half_rn(dsc));
 #pragma unroll
-    for (int e = 0; e < E; ++e) bp[2 + sub * E + e] = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[e], id))));
+    for (int e = 0; e < E; e += 2) {
+      const uint32_t q0 = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[e], id))));
+      const uint32_t q1 = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[e + 1], id))));
+      bp[1 + (sub * E + e) / 2] = static_cast<uint16_t>(q0 | (q1 << 8));
+    }
   }
 }
 

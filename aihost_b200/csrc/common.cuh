@@ -119,6 +119,17 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16. A (M x 16 per instruction, K-major) lives in
+// tensor memory: row m in lane m, 16-bit element k in column k/2 (two per 32-bit column).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on `bar` once every tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -149,6 +160,40 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// 2^x on the SFU (ex2.approx.ftz: relative error ~2^-22, flushes subnormal results to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// sin and cos of a non-negative fp32 angle of up to ~1e5 rad: Cody-Waite reduction by 2*pi
+// (W. J. Cody and W. Waite, Software Manual for the Elementary Functions, 1980) with a
+// three-part split of 2*pi whose first part has 8 significant bits, so k * C1 is exact for
+// k < 2^16; the reduced |r| <= pi then goes to the SFU sin/cos. Absolute error ~5e-7, well
+// under the fp16 rounding that follows in the callers.
+__device__ __forceinline__ void sincos_reduced(float a, float* s, float* c) {
+  constexpr float kInv2Pi = 0.159154943091895336f;
+  constexpr float kC1 = 6.28125f;                      // 2*pi, first 8 bits
+  constexpr float kC2 = 1.9353071693331003e-3f;        // float nearest to 2*pi - kC1
+  constexpr float kC3 = 1.0253376273028358e-11f;       // float nearest to 2*pi - kC1 - kC2
+  const float k = rintf(a * kInv2Pi);
+  float r = fmaf(-k, kC1, a);
+  r = fmaf(-k, kC2, r);
+  r = fmaf(-k, kC3, r);
+  __sincosf(r, s, c);
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

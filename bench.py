@@ -42,6 +42,8 @@ def parse_args():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode object")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="run N untimed fused calls of --config and exit (the command profiled with ncu)")
     return ap.parse_args()
 
 
@@ -272,6 +274,25 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on):
                 lengths=lengths, flushed=need_flush)
 
 
+def profile_steps(cfg, n, device):
+    """n fused calls of `cfg` on device inputs, no timing: the target of ncu captures."""
+    import torch
+
+    from aihost_b200.ops import ComputeOps, Context, KVCache
+
+    with Context(device.index) as ctx:
+        inp = device_inputs(cfg, device, 0)
+        cache = KVCache(ctx, cfg.spec(inp["capacity"]), batch=cfg.batch, n_layers=1, device=device)
+        cache.k[0], cache.v[0] = inp["k_cache"], inp["v_cache"]
+        cache.seq_len, cache.host_len = inp["seq_len"], list(inp["lengths"])
+        ops = ComputeOps(ctx)
+        for _ in range(n):
+            out = ops.attention_layer(inp["q"], inp["k_new"], inp["v_new"], cache)
+        torch.cuda.synchronize()
+        ctx.sync_status()
+        print(f"profiled config {cfg.number}: {n} calls, mean |out| {out.float().abs().mean().item():.4f}")
+
+
 def max_over_ranks(x: float, dist_on: bool) -> float:
     if not dist_on:
         return x
@@ -444,6 +465,9 @@ def main():
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if args.profile_steps:
+        profile_steps(CONFIGS[args.config], args.profile_steps, device)
+        return
     pk, pk_kind = peaks()
     ctx = Context(local)
     clocks = ClockSampler(local).start()

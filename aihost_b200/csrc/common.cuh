@@ -172,6 +172,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+// Warpgroup register budget changes (every warp of the warpgroup executes the same one).
+template <uint32_t N>
+__device__ __forceinline__ void regs_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // 2^x on the SFU (ex2.approx.ftz: relative error ~2^-22, flushes subnormal results to zero).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;

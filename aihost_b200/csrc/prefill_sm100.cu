@@ -14,14 +14,16 @@
 //               softmax group's exponentials overlap the other group's matrix products
 //               (ping-pong). S and O accumulate in TMEM (fp32); P (fp16) is written back over
 //               its own S columns and read by the P.V MMA straight from TMEM.
-//   warps 2-5   softmax group A (query tile A), warps 6-9 group B: one thread per query row.
+//   warps 4-7   softmax group A (query tile A), warps 8-11 group B: one thread per query row.
 //               RoPE of the Q tile in shared memory; per tile tcgen05.ld of S, row max, lazy
 //               rescale of O (only when the running max grows by more than 2^8), exp2 on the
 //               SFU, fp16 P via tcgen05.st; causal masking only on tiles that cross the
 //               diagonal or the end of the sequence; final O / l epilogue.
-// Tile pairing: CTA x takes query tiles x and n-1-x, so every CTA of a causal prefill does the
-// same number of tile products (n + 1); cache tiles above a tile's diagonal are never loaded
-// or multiplied.
+// Tile pairing: a CTA takes adjacent query tiles 2x and 2x+1, so both softmax groups stay busy
+// for the CTA's whole life (the ping-pong needs two live groups); CTAs with the longest causal
+// ranges launch first. Cache tiles above a tile's diagonal are never loaded or multiplied.
+// For head_dim 64, P goes through shared memory (SS-form P.V MMA at full rate); for 128 it stays
+// in TMEM (no room for two P tiles next to the K/V rings).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -30,7 +32,12 @@ namespace {
 
 constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // cache rows per tile
-constexpr int kThreads = 320;
+// Three warpgroups: WG0 = producer warp, MMA warp, two spare warps (56 registers each after
+// setmaxnreg); WG1 / WG2 = softmax groups A / B (224 registers: a full 128-column score row
+// stays in registers). 128*56 + 256*224 = 384*168 = the launch's register file.
+constexpr int kThreads = 384;
+constexpr uint32_t kRegsWG0 = 56;
+constexpr uint32_t kRegsSoftmax = 224;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -43,7 +50,12 @@ struct PrefillCfg {
   static constexpr int QB_OFF = QA_OFF + TILE_BYTES;
   static constexpr int K_OFF = QB_OFF + TILE_BYTES;
   static constexpr int V_OFF = K_OFF + NS * TILE_BYTES;
-  static constexpr int BAR_OFF = V_OFF + NS * TILE_BYTES;
+  // P.V from shared memory (both operands SS) runs at full rate; with P in TMEM (TS form) the
+  // MMA costs ~116 cycles per 16 keys whatever N is. D = 64 has room for two 32 KB P tiles.
+  static constexpr bool P_SMEM = D == 64;
+  static constexpr int P_BYTES = kBM * kBN * 2;  // [128 rows x 128 keys] fp16, two 64-key blocks
+  static constexpr int P_OFF = V_OFF + NS * TILE_BYTES;
+  static constexpr int BAR_OFF = P_OFF + (P_SMEM ? 2 * P_BYTES : 0);
   static constexpr int SMEM = BAR_OFF + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;
   // TMEM columns: S_A, S_B (fp32, P fp16 aliased onto their first 64 columns), O_A, O_B
@@ -82,14 +94,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   uint8_t* q_s[2] = {smem + C::QA_OFF, smem + C::QB_OFF};
   uint8_t* k_s = smem + C::K_OFF;
   uint8_t* v_s = smem + C::V_OFF;
+  uint8_t* p_s[2] = {smem + C::P_OFF, smem + C::P_OFF + C::P_BYTES};
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (a.n_new + kBM - 1) / kBM;
   const int h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (a.n_q_heads / a.n_kv_heads);
-  // tile A = x (shorter causal range), tile B = n_qt - 1 - x (absent for the middle of an odd n_qt)
-  const int qt[2] = {static_cast<int>(blockIdx.x), n_qt - 1 - static_cast<int>(blockIdx.x)};
-  const bool has_b = qt[1] > qt[0];
+  // adjacent query tiles 2x and 2x+1 (B absent past the end); the longest pairs launch first
+  const int x = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
+  const int qt[2] = {2 * x, 2 * x + 1};
+  const bool has_b = qt[1] < n_qt;
   const int32_t start = a.seq_len ? a.seq_len[b] : a.start_scalar;
   const int32_t Lk = start + a.len_offset;
   const bool bad = Lk < 1 || start < 0;
@@ -126,8 +140,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   const uint32_t tmem = bar.tmem_base;
 
   if (bad) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && h == 0) atomicOr(status, kStatusBadLength);
-  } else if (warp == 0) {
+    if (threadIdx.x == 0 && x == 0 && h == 0) atomicOr(status, kStatusBadLength);
+  } else if (warp < 4) {
+    regs_dealloc<kRegsWG0>();
+    if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&a.q_map);
@@ -169,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.v_fix);
     }
-  } else if (warp == 1) {
+    } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = make_idesc_f16(kBM, kBN, 0, 0);
@@ -189,13 +205,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
         umma_commit(&bar.s_full[t]);
       };
+      const uint32_t p_addr[2] = {smem_u32(p_s[0]), smem_u32(p_s[1])};
       auto issue_pv = [&](int t, int j) {
         const int s = j % C::NS;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          umma_f16_ts(tmem + C::o_col(t), tmem + C::s_col(t) + kk * 8,
-                      make_sw128_desc(v_addr + s * C::TILE_BYTES + kk * 2048, kBN * 128, 1024), idesc_pv,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t vd = make_sw128_desc(v_addr + s * C::TILE_BYTES + kk * 2048, kBN * 128, 1024);
+          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+          if constexpr (C::P_SMEM)
+            umma_f16_ss(tmem + C::o_col(t),
+                        make_sw128_desc(p_addr[t] + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024), vd, idesc_pv,
+                        acc);
+          else
+            umma_f16_ts(tmem + C::o_col(t), tmem + C::s_col(t) + kk * 8, vd, idesc_pv, acc);
+        }
       };
       if (ok && n_load > 0) {
         ok = mbar_wait(&bar.k_full[0], 0, status);
@@ -207,39 +230,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       for (int j = 0; ok && j < n_load; ++j) {
         const int s = j % C::NS;
         const int s1 = (j + 1) % C::NS;
-        const uint32_t par = (j / C::NS) & 1, par1 = ((j + 1) / C::NS) & 1;
-        bool v_ready = false, k1_ready = false;
+        // operands first (normally long resident), then the softmax hand-offs
+        if (!mbar_wait(&bar.v_full[s], (j / C::NS) & 1, status)) { ok = false; break; }
+        if (j == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
+        if (j + 1 < n_load && !mbar_wait(&bar.k_full[s1], ((j + 1) / C::NS) & 1, status)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (j >= n_kv[t]) continue;
           if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
           tc_fence_after();
-          if (!v_ready) {
-            if (!mbar_wait(&bar.v_full[s], par, status)) { ok = false; break; }
-            if (j == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
-            tc_fence_after();
-            v_ready = true;
-          }
           issue_pv(t, j);
-          if (j + 1 < n_kv[t]) {
-            if (!k1_ready) {
-              if (!mbar_wait(&bar.k_full[s1], par1, status)) { ok = false; break; }
-              tc_fence_after();
-              k1_ready = true;
-            }
-            issue_qk(t, j + 1);
-          } else {
-            umma_commit(&bar.o_full[t]);
-          }
+          if (j + 1 < n_kv[t]) issue_qk(t, j + 1);
+          else umma_commit(&bar.o_full[t]);
         }
         if (!ok) break;
         umma_commit(&bar.v_empty[s]);
         if (j + 1 < n_load) umma_commit(&bar.k_empty[s1]);
       }
     }
+    }
   } else {
+    regs_alloc<kRegsSoftmax>();
     // ------------------------------------------------------------------ softmax groups
-    const int t = warp >= 6 ? 1 : 0;
+    const int t = warp >= 8 ? 1 : 0;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -253,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       ok = mbar_wait(&bar.q_full, 0, status);
       if (ok && a.rope_mode != AIHOST_ROPE_NONE) {
         const float pos = static_cast<float>(qpos);
-#pragma unroll 4
+#pragma unroll
         for (int pair = 0; pair < D / 2; ++pair) {
           const int c1 = a.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
           const int c2 = a.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
@@ -277,24 +291,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     for (int j = 0; active && ok && j < nk; ++j) {
       if (!mbar_wait(&bar.s_full[t], j & 1, status)) { ok = false; break; }
       tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, sr[c]);
+      tmem_wait_ld();
       const int kv0 = j * kBN;
       const bool need_mask = __any_sync(0xffffffffu, kv0 + kBN - 1 > limit);
-      // pass 1: row max of the raw scores (masked entries excluded)
-      float mx = -INFINITY;
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(s_tmem + c * 32, sr);
-        tmem_wait_ld();
-        if (need_mask) {
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i)
-            if (kv0 + c * 32 + i <= limit) mx = fmaxf(mx, __uint_as_float(sr[i]));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-        }
+            if (kv0 + c * 32 + i > limit) sr[c][i] = __float_as_uint(-INFINITY);
       }
+      // row max with independent partial maxima (instruction-level parallelism)
+      float mxp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sr[c][i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       const float m_new = fmaxf(m, mx * sl2);
       const bool resc = m_new > m + kRescaleThreshold;
       const float f = resc ? ex2_approx(m - m_new) : 1.0f;
@@ -315,32 +334,39 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         l *= f;
         m = m_new;
       }
-      // pass 2: P = 2^(s*scale*log2e - m) in fp16, written over the first 64 columns of S.
-      // Chunk c's P columns [16c, 16c+16) lie below its own S columns [32c, 32c+32), so every
-      // chunk is read before any later chunk's P overwrites it.
+      // P = 2^(s*scale*log2e - m) in fp16 (masked entries: 2^-inf = 0), written over the first
+      // 64 columns of this tile's S, which are already in registers.
       const float neg_m = -m;
-      float rs = 0.0f;
+      float rsp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(s_tmem + c * 32, sr);
-        tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), sl2, neg_m));
-          float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), sl2, neg_m));
-          if (need_mask) {
-            p0 = kv0 + c * 32 + 2 * i <= limit ? p0 : 0.0f;
-            p1 = kv0 + c * 32 + 2 * i + 1 <= limit ? p1 : 0.0f;
-          }
-          rs += p0 + p1;
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), sl2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), sl2, neg_m));
+          rsp[i & 3] += p0 + p1;
           pk[i] = pack_half2(p0, p1);
         }
-        tmem_st16(s_tmem + c * 16, pk);
+        if constexpr (C::P_SMEM) {
+          // row r of the K-major SW128 P tile: 16-byte chunk (c*2 + q) of key block c/2
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int ch = (c & 1) * 4 + q * 2;  // 16-byte chunk index within the 128-byte row
+            uint8_t* row = p_s[t] + (c >> 1) * (kBM * 128) + r * 128;
+            *reinterpret_cast<uint4*>(row + (((ch) ^ (r & 7)) << 4)) =
+                make_uint4(pk[8 * q], pk[8 * q + 1], pk[8 * q + 2], pk[8 * q + 3]);
+            *reinterpret_cast<uint4*>(row + (((ch + 1) ^ (r & 7)) << 4)) =
+                make_uint4(pk[8 * q + 4], pk[8 * q + 5], pk[8 * q + 6], pk[8 * q + 7]);
+          }
+        } else {
+          tmem_st16(s_tmem + c * 16, pk);
+        }
       }
+      const float rs = (rsp[0] + rsp[1]) + (rsp[2] + rsp[3]);
       l += rs;
-      tmem_wait_st();
+      if constexpr (C::P_SMEM) fence_proxy_async_smem();
+      else tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar.p_full[t]);
     }

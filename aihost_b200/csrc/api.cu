@@ -39,16 +39,23 @@ struct aihost_attn_ctx {
 };
 
 namespace {
-
 thread_local char g_err[512] = "";
+}  // namespace
 
-aihost_status fail(aihost_status st, const char* fmt, ...) {
+namespace aihost {
+// Records the thread-local message returned by aihost_attn_last_error().
+aihost_status api_fail(aihost_status st, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
   vsnprintf(g_err, sizeof(g_err), fmt, ap);
   va_end(ap);
   return st;
 }
+}  // namespace aihost
+
+namespace {
+
+#define fail api_fail
 
 aihost_status cuda_fail(cudaError_t e, const char* what) {
   return fail(AIHOST_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
@@ -297,6 +304,21 @@ aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const
 }
 
 }  // namespace
+
+namespace aihost {
+// Validation, split plan and RoPE table of a one-token decode, for aihost_attn_decode_noalloc.
+aihost_status noalloc_prepare(const aihost_attn_desc* desc, int32_t batch, KvLayout* kv, float* scale,
+                              int32_t* chunk, int32_t* max_splits, RopeFreqs* freqs, int32_t num_sms) {
+  aihost_status s = check_desc(desc, kv, scale);
+  if (s != AIHOST_OK) return s;
+  if (batch < 1) return fail(AIHOST_EINVAL, "batch (%d) must be >= 1", batch);
+  const DecodePlan p = plan_decode(desc, batch, num_sms);
+  *chunk = p.chunk;
+  *max_splits = p.max_splits;
+  *freqs = make_freqs(desc->rope_mode != AIHOST_ROPE_NONE ? desc->rope_theta : 1.0f, desc->head_dim);
+  return AIHOST_OK;
+}
+}  // namespace aihost
 
 extern "C" {
 

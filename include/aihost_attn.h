@@ -151,6 +151,20 @@ aihost_status aihost_attn_profiler_enable(aihost_attn_ctx* ctx, int32_t enable);
 aihost_status aihost_attn_profiler_read(aihost_attn_ctx* ctx, int32_t kernel, int64_t* launches, double* total_ms);
 aihost_status aihost_attn_profiler_reset(aihost_attn_ctx* ctx);
 
+/* No counterpart in the reference. The one-token decode step of aihost_attn_forward
+ * (n_new == 1: RoPE, KV append, split-K attention, split merge) for hosts that cannot allocate
+ * device memory when they decode (their allocator is taken by a pool, or may not be entered on
+ * the token path). It needs no context and allocates nothing: the split scratch is a static
+ * 8 MiB array that every GPU loading this library holds until the process exits. Calls whose
+ * split scratch, batch * n_q_heads * splits * (head_dim + 2) * 4 bytes, exceeds 8 MiB return
+ * AIHOST_ENOMEM. Runs on the current CUDA device. The first call on each device looks up the
+ * array's device address: make it before any stream capture. All calls share the array, so
+ * calls that overlap on the GPU race; serialise them. Results equal aihost_attn_forward's. */
+aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc, int32_t batch, const void* q,
+                                         const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                                         const int32_t* seq_len, const int32_t* h_seq_len, void* out,
+                                         void* stream);
+
 /* Synchronise the context's device and read-and-clear the device status word that kernels
  * set when a bounded wait expired (AIHOST_ETIMEOUT) or a device-side length exceeded
  * kv_capacity (AIHOST_EINVAL). *out_bits receives the raw bits (may be NULL). */

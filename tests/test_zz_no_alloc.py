@@ -1,0 +1,85 @@
+"""aihost_attn_decode_noalloc: the decode step for hosts that cannot allocate device memory.
+
+Some callers of this library cannot call cudaMalloc while they decode (an engine whose device
+memory is already carved up by its own pool, or a host that must not enter the allocator on the
+token path). For them, aihost_attn_decode_noalloc runs the same one-token step as
+aihost_attn_forward with its split scratch in a static device array instead of a context's
+reserved buffer. These tests call both entry points through the C ABI on the same inputs, twice
+in a row (the static array keeps the previous call's contents), and require the same outputs
+and cache rows within the parity bound the other fp16 tests use (2e-3).
+
+The file name puts it last in collection order, so a run that stops at the first failure has run
+every other test before it; it also passes on its own in a fresh process.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from aihost_b200 import ENOMEM, OK, check, lib
+from aihost_b200.configs import CONFIGS, make_inputs
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def _regular(ctx, cfg, inp):
+    """aihost_attn_forward with a context and reserved scratch; returns (out, k_cache, v_cache)."""
+    dev = torch.device("cuda", 0)
+    spec = cfg.spec(inp["capacity"])
+    ctx.reserve_for(spec, cfg.batch, 1)
+    d = spec.desc()
+    q, kn, vn = (inp[n].to(dev) for n in ("q", "k_new", "v_new"))
+    kc, vc = inp["k_cache"].to(dev).clone(), inp["v_cache"].to(dev).clone()
+    sl = inp["seq_len"].to(dev)
+    out = torch.empty(cfg.batch, 1, cfg.n_q_heads, cfg.head_dim, dtype=torch.float16, device=dev)
+    hl = (ctypes.c_int32 * cfg.batch)(*inp["lengths"])
+    check(lib().aihost_attn_forward(ctx.handle, ctypes.byref(d), cfg.batch, 1, q.data_ptr(), kn.data_ptr(),
+                                    vn.data_ptr(), kc.data_ptr(), vc.data_ptr(), sl.data_ptr(),
+                                    ctypes.cast(hl, ctypes.c_void_p), out.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return out.cpu(), kc.cpu(), vc.cpu()
+
+
+def _noalloc(cfg, inp):
+    """aihost_attn_decode_noalloc on the current device; no context, no reservation."""
+    dev = torch.device("cuda", 0)
+    d = cfg.spec(inp["capacity"]).desc()
+    q, kn, vn = (inp[n].to(dev) for n in ("q", "k_new", "v_new"))
+    kc, vc = inp["k_cache"].to(dev).clone(), inp["v_cache"].to(dev).clone()
+    sl = inp["seq_len"].to(dev)
+    out = torch.empty(cfg.batch, 1, cfg.n_q_heads, cfg.head_dim, dtype=torch.float16, device=dev)
+    check(lib().aihost_attn_decode_noalloc(ctypes.byref(d), cfg.batch, q.data_ptr(), kn.data_ptr(), vn.data_ptr(),
+                                           kc.data_ptr(), vc.data_ptr(), sl.data_ptr(), None, out.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return out.cpu(), kc.cpu(), vc.cpu()
+
+
+def test_noalloc_matches_forward_on_two_calls_in_a_row(ctx):
+    torch.cuda.set_device(0)
+    calls = [
+        CONFIGS[3].scaled(batch=8, cached_range=None, cached_list=[300, 4095, 17, 2048, 999, 1, 3333, 640]),
+        CONFIGS[5].scaled(batch=2, n_q_heads=16, n_kv_heads=2, cached=None, cached_list=[513, 2700]),
+    ]
+    for cfg in calls:
+        inp = make_inputs(cfg)
+        ref_out, ref_k, ref_v = _regular(ctx, cfg, inp)
+        out, k, v = _noalloc(cfg, inp)
+        assert torch.isfinite(out.float()).all()
+        err = float((out.float() - ref_out.float()).abs().max())
+        assert err <= TOL, f"{cfg.name}: max |noalloc - forward| = {err:.3g}"
+        assert np.array_equal(k.numpy(), ref_k.numpy()) and np.array_equal(v.numpy(), ref_v.numpy())
+
+
+def test_noalloc_refuses_requests_past_its_static_scratch():
+    torch.cuda.set_device(0)
+    cfg = CONFIGS[3]  # 64 sequences of up to 8193 rows: ~18 MB of split scratch > 8 MiB
+    spec = cfg.spec(8193)
+    d = spec.desc()
+    st = lib().aihost_attn_decode_noalloc(ctypes.byref(d), cfg.batch, 16, 16, 16, 16, 16, 16, None, 16, None)
+    assert st == ENOMEM
+    assert b"8 MiB" in lib().aihost_attn_last_error()
+    assert st != OK

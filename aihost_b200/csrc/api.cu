@@ -168,10 +168,10 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// fp16 tensor [d3][d2][d1][d0 = head_dim] with byte strides s1, s2, s3; box {64, 1, 128, 1},
+// fp16 tensor [d3][d2][d1][d0 = head_dim] with byte strides s1, s2, s3; box {64, 1, box_rows, 1},
 // 128-byte swizzle (the canonical tcgen05 K-major / MN-major operand layout).
 aihost_status encode_f16_map(CUtensorMap* map, const void* base, int32_t d0, int64_t d1, int64_t d2, int64_t d3,
-                             int64_t s1, int64_t s2, int64_t s3, const char* what) {
+                             int64_t s1, int64_t s2, int64_t s3, const char* what, uint32_t box_rows = 128) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
   if (!aligned(base, 16)) return fail(AIHOST_EINVAL, "%s must be 16-byte aligned", what);
@@ -179,7 +179,7 @@ aihost_status encode_f16_map(CUtensorMap* map, const void* base, int32_t d0, int
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2),
                         static_cast<cuuint64_t>(d3)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(s1), static_cast<cuuint64_t>(s2), static_cast<cuuint64_t>(s3)};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, 1, box_rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -255,12 +255,8 @@ aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const 
   a.out = out;
   a.out_dtype = d->out_dtype;
   a.status = ctx->d_status;
-  cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_DECODE, st, [&] { return launch_decode(a, st); });
+  cudaError_t e = launch_decode_any(a, st, ctx);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
-  if (a.max_splits > 1) {
-    e = timed_launch(ctx, AIHOST_KERNEL_COMBINE, st, [&] { return launch_decode_combine(a, st); });
-    if (e != cudaSuccess) return cuda_fail(e, "decode combine launch");
-  }
   return AIHOST_OK;
 }
 
@@ -306,6 +302,32 @@ aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const
 }  // namespace
 
 namespace aihost {
+cudaError_t launch_decode_any(const DecodeArgs& a, cudaStream_t st, aihost_attn_ctx* ctx) {
+  auto run = [&](int kind, auto&& fn) -> cudaError_t { return ctx ? timed_launch(ctx, kind, st, fn) : fn(); };
+  cudaError_t e = cudaSuccess;
+  bool done = false;
+  if (a.kv.dtype == AIHOST_F16) {
+    DecodeMmaArgs m;
+    memset(&m, 0, sizeof(m));
+    m.base = a;
+    const int64_t seq_stride = a.kv.seq_stride ? a.kv.seq_stride : a.kv.token_stride * a.kv.capacity;
+    char saved[sizeof(g_err)];
+    memcpy(saved, g_err, sizeof(g_err));
+    if (encode_f16_map(&m.k_map, a.k_cache, a.head_dim, a.n_kv_heads, a.kv.capacity, a.batch, a.kv.head_stride,
+                       a.kv.token_stride, seq_stride, "k_cache", 64) == AIHOST_OK &&
+        encode_f16_map(&m.v_map, a.v_cache, a.head_dim, a.n_kv_heads, a.kv.capacity, a.batch, a.kv.head_stride,
+                       a.kv.token_stride, seq_stride, "v_cache", 64) == AIHOST_OK) {
+      e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode_mma(m, st); });
+      done = true;
+    } else {
+      memcpy(g_err, saved, sizeof(g_err));  // strides TMA cannot describe: CUDA-core kernel instead
+    }
+  }
+  if (!done) e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode(a, st); });
+  if (e != cudaSuccess || a.max_splits <= 1) return e;
+  return run(AIHOST_KERNEL_COMBINE, [&] { return launch_decode_combine(a, st); });
+}
+
 // Validation, split plan and RoPE table of a one-token decode, for aihost_attn_decode_noalloc.
 aihost_status noalloc_prepare(const aihost_attn_desc* desc, int32_t batch, KvLayout* kv, float* scale,
                               int32_t* chunk, int32_t* max_splits, RopeFreqs* freqs, int32_t num_sms) {

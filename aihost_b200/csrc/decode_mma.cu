@@ -1,0 +1,344 @@
+// decode_mma.cu — split-K flash decoding for fp16 caches on the tensor cores.
+//
+// Replaces FusedMHAGenerate (ComputeShaders.cs:656-733) for fp16 KV caches. One CTA handles one
+// (sequence, KV head, group of up to 16 Q heads, split of `chunk` cache rows):
+//   warp 4      TMA producer: K and V tiles of 64 rows (128-byte swizzled, no multicast) into a
+//               multi-stage shared-memory ring, completion on mbarriers;
+//   warps 0-3   each takes 16 rows of every tile: S = Q K^T with m16n8k16 MMAs (the group's Q
+//               heads are the 16 MMA rows, rotated by RoPE once per CTA and kept as A fragments
+//               in registers), online softmax in the exp2 domain with quad-shuffle row
+//               reductions, O += P V with P re-used from the S accumulators as A fragments;
+//               the four warps' (max, sum, O) are merged through shared memory at the end.
+// The per-split (max, sum, unnormalised O) go to the same scratch / combine kernel as the fp32
+// path, or straight to the output when a sequence fits in one split.
+// Decode moves ~2 bytes of cache per multiply-add pair and has only G <= 16 query rows per KV
+// head, so it is bound by HBM bandwidth: the design goal is many bytes in flight per SM
+// (ring depth x 2 x 64 x head_dim x 2 bytes) and few instructions per byte.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace aihost {
+namespace {
+
+constexpr int kTileRows = 64;     // cache rows per pipeline stage
+constexpr int kComputeWarps = 4;  // 16 rows of each tile per warp
+constexpr int kThreads = (kComputeWarps + 1) * 32;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct DecodeCfg {
+  static constexpr int KB = D / 64;                         // 128-byte column blocks
+  static constexpr int TILE_BYTES = KB * kTileRows * 128;   // one K or V tile
+  static constexpr int NS = D == 64 ? 6 : 3;                // ring depth
+  static constexpr int QROW = D + 8;                        // padded Q row (fp16 elements)
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = NS * TILE_BYTES;
+  static constexpr int Q_OFF = 2 * NS * TILE_BYTES;
+  static constexpr int Q_BYTES = 16 * QROW * 2;
+  static constexpr int BAR_OFF = Q_OFF + Q_BYTES;
+  static constexpr int SMEM = BAR_OFF + 128 + 1024;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.x4.m8n8.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.x4.trans.m8n8.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Shared-memory byte address of fp16 element (row, col) of a 64-row tile written by TMA with
+// 128-byte swizzle (16-byte chunk index XOR row % 8; 64-column blocks of 64 * 128 bytes).
+__device__ __forceinline__ uint32_t sw_addr(uint32_t tile, int row, int col) {
+  return tile + (col >> 6) * (kTileRows * 128) + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4);
+}
+
+struct DecBars {
+  uint64_t full[6], empty[6];
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_constant__ DecodeMmaArgs a) {
+  using C = DecodeCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DecBars& bar = *reinterpret_cast<DecBars*>(smem + C::BAR_OFF);
+  __half* q_s = reinterpret_cast<__half*>(smem + C::Q_OFF);
+  const uint32_t k_base = smem_u32(smem + C::K_OFF), v_base = smem_u32(smem + C::V_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const DecodeArgs& p = a.base;
+  const int split = blockIdx.x;
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int n_sub = (G + 15) / 16;
+  const int kvh = blockIdx.y / n_sub, sub = blockIdx.y % n_sub;
+  const int b = blockIdx.z;
+  const int g_count = min(16, G - sub * 16);
+  const int h0 = kvh * G + sub * 16;
+  const int32_t start = p.seq_len ? p.seq_len[b] : p.start_scalar;
+  const int32_t Lk = start + p.len_offset;
+  if (Lk > p.kv.capacity || Lk < 1) {
+    if (threadIdx.x == 0 && split == 0 && blockIdx.y == 0) atomicOr(p.status, kStatusBadLength);
+    return;
+  }
+  const int32_t t0 = split * p.chunk;
+  if (t0 >= Lk) return;
+  const int32_t n = min(p.chunk, Lk - t0);
+  const int n_tiles = (n + kTileRows - 1) / kTileRows;
+  const int n_splits = (Lk + p.chunk - 1) / p.chunk;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NS; ++i) {
+      mbar_init(&bar.full[i], 1);
+      mbar_init(&bar.empty[i], kComputeWarps);
+    }
+    fence_mbar_init();
+  }
+  // Q rows of the group, rotated at the new token's position, as fp16 (rows >= g_count zero)
+  const float pos = static_cast<float>(start + p.rope_pos_offset);
+  for (int idx = threadIdx.x; idx < 16 * (D / 2); idx += kThreads) {
+    const int g = idx / (D / 2), pair = idx % (D / 2);
+    const int i1 = p.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
+    const int i2 = p.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
+    float x1 = 0.0f, x2 = 0.0f;
+    if (g < g_count) {
+      const int64_t qoff = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D;
+      if (p.q_dtype == AIHOST_F32) {
+        x1 = static_cast<const float*>(p.q)[qoff + i1];
+        x2 = static_cast<const float*>(p.q)[qoff + i2];
+      } else {
+        x1 = __half2float(static_cast<const __half*>(p.q)[qoff + i1]);
+        x2 = __half2float(static_cast<const __half*>(p.q)[qoff + i2]);
+      }
+      if (p.rope_mode != AIHOST_ROPE_NONE) {
+        float sn, cs;
+        sincosf(__fmul_rn(pos, p.freqs.f[pair]), &sn, &cs);
+        const float r1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+        const float r2 = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
+        x1 = r1;
+        x2 = r2;
+      }
+    }
+    q_s[g * C::QROW + i1] = __float2half_rn(x1);
+    q_s[g * C::QROW + i2] = __float2half_rn(x2);
+  }
+  __syncthreads();
+
+  if (warp == kComputeWarps) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&a.k_map);
+      tma_prefetch_desc(&a.v_map);
+      for (int i = 0; i < n_tiles; ++i) {
+        const int s = i % C::NS;
+        if (!mbar_wait(&bar.empty[s], ((i / C::NS) & 1) ^ 1, p.status)) break;
+        mbar_arrive_expect_tx(&bar.full[s], 2 * C::TILE_BYTES);
+        const int row = t0 + i * kTileRows;
+        for (int kb = 0; kb < C::KB; ++kb) {
+          tma_load_4d(smem + C::K_OFF + s * C::TILE_BYTES + kb * kTileRows * 128, &a.k_map, &bar.full[s], kb * 64,
+                      kvh, row, b);
+          tma_load_4d(smem + C::V_OFF + s * C::TILE_BYTES + kb * kTileRows * 128, &a.v_map, &bar.full[s], kb * 64,
+                      kvh, row, b);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ compute warps
+  const int grp = lane >> 2, tig = lane & 3;
+  // Q as A fragments: k-step kk covers dims [16kk, 16kk + 16)
+  uint32_t qa[D / 16][4];
+  {
+    const uint32_t qb = smem_u32(q_s);
+    const int mi = lane >> 3, r = lane & 7;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      ldsm_x4(qb + ((r + 8 * (mi & 1)) * C::QROW + kk * 16 + 8 * (mi >> 1)) * 2, qa[kk][0], qa[kk][1], qa[kk][2],
+              qa[kk][3]);
+  }
+  const float sl2 = p.scale * kLog2e;
+  float m_run[2] = {-1e30f, -1e30f}, l_run[2] = {0.0f, 0.0f};
+  float o[D / 8][4];
+#pragma unroll
+  for (int nb = 0; nb < D / 8; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
+
+  bool ok = true;
+  for (int i = 0; i < n_tiles && ok; ++i) {
+    const int s = i % C::NS;
+    if (!mbar_wait(&bar.full[s], (i / C::NS) & 1, p.status)) { ok = false; break; }
+    const uint32_t kt = k_base + s * C::TILE_BYTES, vt = v_base + s * C::TILE_BYTES;
+    const int r0 = warp * 16;  // this warp's 16 rows of the tile
+    // ---- S = Q K^T for the warp's rows: two n8 blocks
+    float sacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+    {
+      const int mi = lane >> 3, r = lane & 7;
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+        for (int kk = 0; kk < D / 16; kk += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(sw_addr(kt, r0 + nb * 8 + r, kk * 16 + 8 * mi), b0, b1, b2, b3);
+          mma16816(sacc[nb], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+          mma16816(sacc[nb], qa[kk + 1][0], qa[kk + 1][1], qa[kk + 1][2], qa[kk + 1][3], b2, b3);
+        }
+    }
+    // ---- mask rows past the split's end, then the online softmax (rows grp and grp + 8)
+    const int base_row = i * kTileRows + r0;
+    float mt[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = base_row + nb * 8 + 2 * tig + (e & 1);
+        float v = sacc[nb][e] * sl2;
+        v = row < n ? v : -INFINITY;
+        sacc[nb][e] = v;
+        mt[e >> 1] = fmaxf(mt[e >> 1], v);
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 1));
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 2));
+    }
+    float f[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float m_new = fmaxf(m_run[h], mt[h]);
+      f[h] = ex2_approx(m_run[h] - m_new);
+      m_run[h] = m_new;
+      l_run[h] *= f[h];
+    }
+#pragma unroll
+    for (int nb = 0; nb < D / 8; ++nb) {
+      o[nb][0] *= f[0];
+      o[nb][1] *= f[0];
+      o[nb][2] *= f[1];
+      o[nb][3] *= f[1];
+    }
+    float pv[2][4];
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pv[nb][e] = ex2_approx(sacc[nb][e] - m_run[e >> 1]);
+        l_run[e >> 1] += pv[nb][e];
+      }
+    const uint32_t pa0 = pack_h2(pv[0][0], pv[0][1]), pa1 = pack_h2(pv[0][2], pv[0][3]);
+    const uint32_t pa2 = pack_h2(pv[1][0], pv[1][1]), pa3 = pack_h2(pv[1][2], pv[1][3]);
+    // ---- rows past the split's end may hold stale bits (NaN patterns included); P is 0 there,
+    // but 0 * NaN is NaN, so the warp zeroes its own V rows beyond n before reading them
+    if (base_row + 16 > n) {
+      uint8_t* vrow0 = smem + C::V_OFF + s * C::TILE_BYTES;
+      for (int c = lane; c < 16 * C::KB * 8; c += 32) {
+        const int rr = c / (C::KB * 8), ch = c % (C::KB * 8);
+        if (base_row + rr >= n)
+          *reinterpret_cast<uint4*>(vrow0 + (ch >> 3) * (kTileRows * 128) + (r0 + rr) * 128 + (ch & 7) * 16) =
+              make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+    }
+    // ---- O += P V: V rows r0..r0+15 of the tile, all D columns (ldmatrix.trans gives B frags)
+    {
+      const int mi = lane >> 3, r = lane & 7;
+#pragma unroll
+      for (int nb = 0; nb < D / 8; nb += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(sw_addr(vt, r0 + r + 8 * (mi & 1), nb * 8 + 8 * (mi >> 1)), b0, b1, b2, b3);
+        mma16816(o[nb], pa0, pa1, pa2, pa3, b0, b1);
+        mma16816(o[nb + 1], pa0, pa1, pa2, pa3, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (base_row + 16 > n) fence_proxy_async_smem();  // zeroed rows are rewritten by TMA later
+    if (lane == 0) mbar_arrive(&bar.empty[s]);
+  }
+
+  // ---- merge the four warps: row sums over the quad, then through shared memory
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+  }
+  // all tiles consumed: the K ring is reused for the merge (no TMA can target it any more)
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  float* ml_s = reinterpret_cast<float*>(smem + C::K_OFF);      // [4 warps][16 rows][2]
+  float* o_s = ml_s + kComputeWarps * 16 * 2;                     // [4 warps][16 rows][D]
+  if (tig == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ml_s[(warp * 16 + grp + 8 * h) * 2] = m_run[h];
+      ml_s[(warp * 16 + grp + 8 * h) * 2 + 1] = l_run[h];
+    }
+  }
+#pragma unroll
+  for (int nb = 0; nb < D / 8; ++nb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = grp + 8 * (e >> 1), col = nb * 8 + 2 * tig + (e & 1);
+      o_s[(warp * 16 + row) * D + col] = o[nb][e];
+    }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (int idx = threadIdx.x; idx < g_count * D; idx += kComputeWarps * 32) {
+    const int g = idx / D, d = idx % D;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kComputeWarps; ++w) m = fmaxf(m, ml_s[(w * 16 + g) * 2]);
+    float l = 0.0f, acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kComputeWarps; ++w) {
+      const float wt = ex2_approx(ml_s[(w * 16 + g) * 2] - m);
+      l = fmaf(ml_s[(w * 16 + g) * 2 + 1], wt, l);
+      acc = fmaf(o_s[(w * 16 + g) * D + d], wt, acc);
+    }
+    const int h = h0 + g;
+    if (n_splits == 1) {
+      const float v = acc / l;
+      const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * D + d;
+      if (p.out_dtype == AIHOST_F32) static_cast<float*>(p.out)[oidx] = v;
+      else static_cast<__half*>(p.out)[oidx] = __float2half_rn(v);
+    } else {
+      const int64_t pidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * p.max_splits + split;
+      p.part_o[pidx * D + d] = acc;
+      if (d == 0) {
+        p.part_ml[pidx * 2] = m;
+        p.part_ml[pidx * 2 + 1] = l;
+      }
+    }
+  }
+}
+
+template <int D>
+cudaError_t launch_d(const DecodeMmaArgs& a, cudaStream_t st) {
+  using C = DecodeCfg<D>;
+  auto kern = decode_mma_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int G = a.base.n_q_heads / a.base.n_kv_heads;
+  dim3 grid(a.base.max_splits, a.base.n_kv_heads * ((G + 15) / 16), a.base.batch);
+  kern<<<grid, kThreads, C::SMEM, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_decode_mma(const DecodeMmaArgs& a, cudaStream_t st) {
+  return a.base.head_dim == 64 ? launch_d<64>(a, st) : launch_d<128>(a, st);
+}
+
+}  // namespace aihost

@@ -63,6 +63,23 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t st);
 // Merge of the per-split partials (only needed when max_splits > 1).
 cudaError_t launch_decode_combine(const DecodeArgs& a, cudaStream_t st);
 
+// ---------------------------------------------------------------- decode_mma.cu
+// fp16-cache decode on the tensor cores: K/V maps over the cache with 64-row boxes.
+struct DecodeMmaArgs {
+  DecodeArgs base;
+  CUtensorMap k_map;  // dims {d, Hkv, capacity, batch}, box {64, 1, 64, 1}, 128-byte swizzle
+  CUtensorMap v_map;
+};
+cudaError_t launch_decode_mma(const DecodeMmaArgs& a, cudaStream_t st);
+
+}  // namespace aihost
+struct aihost_attn_ctx;
+namespace aihost {
+// Decode kernel for the cache dtype (tensor-core path for fp16 caches with TMA-compatible
+// strides, CUDA-core path otherwise) followed by the split merge; launches are timed by the
+// context's profiler when ctx is non-NULL. Defined in api.cu.
+cudaError_t launch_decode_any(const DecodeArgs& a, cudaStream_t st, aihost_attn_ctx* ctx);
+
 // ---------------------------------------------------------------- prefill_sm100.cu
 struct PrefillArgs {
   const void* q;            // [batch][S][Hq][d] fp16

@@ -136,8 +136,7 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   a.out = out;
   a.out_dtype = desc->out_dtype;
   a.status = status;
-  e = launch_decode(a, st);
-  if (e == cudaSuccess) e = launch_decode_combine(a, st);
+  e = launch_decode_any(a, st, nullptr);
   if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "decode launch: %s", cudaGetErrorString(e));
   return AIHOST_OK;
 }

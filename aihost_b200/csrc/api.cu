@@ -188,6 +188,28 @@ aihost_status encode_f16_map(CUtensorMap* map, const void* base, int32_t d0, int
   return AIHOST_OK;
 }
 
+// Q8_0 cache viewed as 32-bit words: dims {words per token row, capacity, batch, 1}, box
+// {box_words, 64 rows, 1, 1}, no swizzle. Needs 16-byte token/sequence strides and 4-byte heads.
+aihost_status encode_q8_map(CUtensorMap* map, const void* base, const KvLayout& kv, int32_t batch,
+                            uint32_t box_words) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int64_t seq_stride = kv.seq_stride ? kv.seq_stride : kv.token_stride * kv.capacity;
+  if (!aligned(base, 16) || kv.token_stride % 16 || seq_stride % 16 || kv.head_stride % 4)
+    return fail(AIHOST_EINVAL, "Q8_0 cache strides are not TMA-compatible");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kv.token_stride / 4), static_cast<cuuint64_t>(kv.capacity),
+                        static_cast<cuuint64_t>(batch), 1};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(kv.token_stride), static_cast<cuuint64_t>(seq_stride),
+                           static_cast<cuuint64_t>(seq_stride) * static_cast<cuuint64_t>(batch)};
+  cuuint32_t box[4] = {box_words, 64, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled(q8 cache) failed with %d", static_cast<int>(r));
+  return AIHOST_OK;
+}
+
 aihost_status check_ctx(aihost_attn_ctx* ctx) {
   if (!ctx) return fail(AIHOST_EINVAL, "ctx is NULL");
   return AIHOST_OK;
@@ -321,6 +343,20 @@ cudaError_t launch_decode_any(const DecodeArgs& a, cudaStream_t st, aihost_attn_
       done = true;
     } else {
       memcpy(g_err, saved, sizeof(g_err));  // strides TMA cannot describe: CUDA-core kernel instead
+    }
+  } else if (a.kv.dtype == AIHOST_Q8_0) {
+    DecodeMmaArgs m;
+    memset(&m, 0, sizeof(m));
+    m.base = a;
+    char saved[sizeof(g_err)];
+    memcpy(saved, g_err, sizeof(g_err));
+    const uint32_t bw = q8_box_words(a.head_dim);
+    if (encode_q8_map(&m.k_map, a.k_cache, a.kv, a.batch, bw) == AIHOST_OK &&
+        encode_q8_map(&m.v_map, a.v_cache, a.kv, a.batch, bw) == AIHOST_OK) {
+      e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode_mma(m, st); });
+      done = true;
+    } else {
+      memcpy(g_err, saved, sizeof(g_err));
     }
   }
   if (!done) e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode(a, st); });

@@ -323,6 +323,327 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
   }
 }
 
+// ------------------------------------------------------------------ GGUF Q8_0 caches
+// Eight compute warps: warps w and w + 4 take the same 16 rows of each tile (both compute the
+// scores, which are cheap) and each accumulates half of the output columns, which halves the
+// accumulator registers and doubles the warps available to hide shared-memory latency.
+constexpr int kQ8ComputeWarps = 8;
+constexpr int kQ8Threads = (kQ8ComputeWarps + 1) * 32;
+// Tiles hold raw 34-byte blocks: each cache row's head slice is read by TMA as a box of 32-bit
+// words that starts at the 16-byte boundary at or below the slice (GGUF blocks are only 2-byte
+// aligned), `q8_box_words` wide; the slice then begins `q8_off` words into every tile row.
+template <int D>
+struct Q8Cfg {
+  static constexpr int NB = D / 32;                   // blocks per head row
+  static constexpr int HEAD_WORDS = NB * 34 / 4;      // 17 (D=64) or 34 (D=128) words
+  static constexpr int BOX_WORDS = (HEAD_WORDS + 3 + 3) / 4 * 4;  // room for a 0..3-word start offset
+  static constexpr int ROW_BYTES = BOX_WORDS * 4;
+  static constexpr int TILE_BYTES = kTileRows * ROW_BYTES;
+  static constexpr int NS = 4;
+  static constexpr int QROW = D + 8;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = NS * TILE_BYTES;
+  static constexpr int Q_OFF = (2 * NS * TILE_BYTES + 1023) / 1024 * 1024;
+  static constexpr int Q_BYTES = 16 * QROW * 2;
+  static constexpr int MERGE_BYTES = kComputeWarps * 16 * (D + 2) * 4;
+  static constexpr int BAR_OFF = Q_OFF + Q_BYTES;
+  static constexpr int SMEM = BAR_OFF + 128 + 1024;
+  static_assert(2 * NS * TILE_BYTES >= MERGE_BYTES, "merge buffer reuses the K/V rings");
+};
+
+// Two int8 values (low byte = first) to an exact fp16 pair: 0x64xx is 1024 + xx in fp16, so
+// (1024 + (b ^ 0x80)) - 1152 = signed b.
+__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t w) {
+  const uint32_t x = __byte_perm(w ^ 0x8080u, 0x64646464u, 0x4140);
+  __half2 h = *reinterpret_cast<const __half2*>(&x);
+  h = __hsub2(h, __floats2half2_rn(1152.0f, 1152.0f));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_constant__ DecodeMmaArgs a) {
+  using C = Q8Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DecBars& bar = *reinterpret_cast<DecBars*>(smem + C::BAR_OFF);
+  __half* q_s = reinterpret_cast<__half*>(smem + C::Q_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const DecodeArgs& p = a.base;
+  const int split = blockIdx.x;
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int n_sub = (G + 15) / 16;
+  const int kvh = blockIdx.y / n_sub, sub = blockIdx.y % n_sub;
+  const int b = blockIdx.z;
+  const int g_count = min(16, G - sub * 16);
+  const int h0 = kvh * G + sub * 16;
+  const int32_t start = p.seq_len ? p.seq_len[b] : p.start_scalar;
+  const int32_t Lk = start + p.len_offset;
+  if (Lk > p.kv.capacity || Lk < 1) {
+    if (threadIdx.x == 0 && split == 0 && blockIdx.y == 0) atomicOr(p.status, kStatusBadLength);
+    return;
+  }
+  const int32_t t0 = split * p.chunk;
+  if (t0 >= Lk) return;
+  const int32_t n = min(p.chunk, Lk - t0);
+  const int n_tiles = (n + kTileRows - 1) / kTileRows;
+  const int n_splits = (Lk + p.chunk - 1) / p.chunk;
+  const int head_word = static_cast<int>(kvh * (p.kv.head_stride / 4));
+  const int box_x = head_word & ~3;
+  const int off = (head_word - box_x) * 4;  // byte offset of the head slice in a tile row
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NS; ++i) {
+      mbar_init(&bar.full[i], 1);
+      mbar_init(&bar.empty[i], kQ8ComputeWarps);
+    }
+    fence_mbar_init();
+  }
+  const float pos = static_cast<float>(start + p.rope_pos_offset);
+  for (int idx = threadIdx.x; idx < 16 * (D / 2); idx += kQ8Threads) {
+    const int g = idx / (D / 2), pair = idx % (D / 2);
+    const int i1 = p.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
+    const int i2 = p.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
+    float x1 = 0.0f, x2 = 0.0f;
+    if (g < g_count) {
+      const int64_t qoff = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D;
+      if (p.q_dtype == AIHOST_F32) {
+        x1 = static_cast<const float*>(p.q)[qoff + i1];
+        x2 = static_cast<const float*>(p.q)[qoff + i2];
+      } else {
+        x1 = __half2float(static_cast<const __half*>(p.q)[qoff + i1]);
+        x2 = __half2float(static_cast<const __half*>(p.q)[qoff + i2]);
+      }
+      if (p.rope_mode != AIHOST_ROPE_NONE) {
+        float sn, cs;
+        sincosf(__fmul_rn(pos, p.freqs.f[pair]), &sn, &cs);
+        const float r1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+        const float r2 = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
+        x1 = r1;
+        x2 = r2;
+      }
+    }
+    q_s[g * C::QROW + i1] = __float2half_rn(x1);
+    q_s[g * C::QROW + i2] = __float2half_rn(x2);
+  }
+  __syncthreads();
+
+  if (warp == kQ8ComputeWarps) {
+    if (lane == 0) {
+      tma_prefetch_desc(&a.k_map);
+      tma_prefetch_desc(&a.v_map);
+      for (int i = 0; i < n_tiles; ++i) {
+        const int s = i % C::NS;
+        if (!mbar_wait(&bar.empty[s], ((i / C::NS) & 1) ^ 1, p.status)) break;
+        mbar_arrive_expect_tx(&bar.full[s], 2 * C::TILE_BYTES);
+        const int row = t0 + i * kTileRows;
+        tma_load_4d(smem + C::K_OFF + s * C::TILE_BYTES, &a.k_map, &bar.full[s], box_x, row, b, 0);
+        tma_load_4d(smem + C::V_OFF + s * C::TILE_BYTES, &a.v_map, &bar.full[s], box_x, row, b, 0);
+      }
+    }
+    return;
+  }
+
+  const int grp = lane >> 2, tig = lane & 3;
+  uint32_t qa[D / 16][4];
+  {
+    const uint32_t qb = smem_u32(q_s);
+    const int mi = lane >> 3, r = lane & 7;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      ldsm_x4(qb + ((r + 8 * (mi & 1)) * C::QROW + kk * 16 + 8 * (mi >> 1)) * 2, qa[kk][0], qa[kk][1], qa[kk][2],
+              qa[kk][3]);
+  }
+  const float sl2 = p.scale * kLog2e;
+  float m_run[2] = {-1e30f, -1e30f}, l_run[2] = {0.0f, 0.0f};
+  constexpr int NBH = D / 16;  // n8 blocks of output columns per warp (half of D)
+  float o[NBH][4];
+#pragma unroll
+  for (int nb = 0; nb < NBH; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
+
+  bool ok = true;
+  for (int i = 0; i < n_tiles && ok; ++i) {
+    const int s = i % C::NS;
+    if (!mbar_wait(&bar.full[s], (i / C::NS) & 1, p.status)) { ok = false; break; }
+    const uint8_t* kt = smem + C::K_OFF + s * C::TILE_BYTES + off;
+    uint8_t* vt = smem + C::V_OFF + s * C::TILE_BYTES + off;
+    const int r0 = (warp & 3) * 16;  // rows of the tile (shared by warps w and w + 4)
+    const int dh = warp >> 2;         // half of the output columns this warp accumulates
+    const int base_row = i * kTileRows + r0;
+    // rows past the split's end may hold stale bytes (their fp16 scales may be NaN): the
+    // row-group's first warp zeroes them (named barrier per row group before anyone reads)
+    if (base_row + 16 > n && dh == 0) {
+      for (int c = lane; c < 16 * C::NB; c += 32) {
+        const int rr = c / C::NB, blk = c % C::NB;
+        if (base_row + rr >= n) {
+          *reinterpret_cast<uint16_t*>(vt + (r0 + rr) * C::ROW_BYTES + blk * 34) = 0;
+          *reinterpret_cast<uint16_t*>(const_cast<uint8_t*>(kt) + (r0 + rr) * C::ROW_BYTES + blk * 34) = 0;
+        }
+      }
+    }
+    if (base_row + 16 > n) asm volatile("bar.sync %0, 64;" ::"r"(2 + (warp & 3)) : "memory");
+    // ---- S = Q K^T per 32-column block (integer K values are exact in fp16), then the block
+    // scales of each row: S = sum_blk d_blk * S_blk
+    float sacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll
+    for (int blk = 0; blk < C::NB; ++blk) {
+      float sb[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        const uint8_t* krow = kt + (r0 + nb * 8 + grp) * C::ROW_BYTES + blk * 34 + 2;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // the block's two 16-column k-steps
+          const int kk = blk * 2 + h;
+          const uint32_t b0 = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(krow + h * 16 + 2 * tig));
+          const uint32_t b1 = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(krow + h * 16 + 8 + 2 * tig));
+          mma16816(sb[nb], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+        }
+      }
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        const int row = r0 + nb * 8 + 2 * tig;
+        const float d0 = __half2float(*reinterpret_cast<const __half*>(kt + row * C::ROW_BYTES + blk * 34));
+        const float d1 = __half2float(*reinterpret_cast<const __half*>(kt + (row + 1) * C::ROW_BYTES + blk * 34));
+        sacc[nb][0] = fmaf(d0, sb[nb][0], sacc[nb][0]);
+        sacc[nb][1] = fmaf(d1, sb[nb][1], sacc[nb][1]);
+        sacc[nb][2] = fmaf(d0, sb[nb][2], sacc[nb][2]);
+        sacc[nb][3] = fmaf(d1, sb[nb][3], sacc[nb][3]);
+      }
+    }
+    float mt[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = base_row + nb * 8 + 2 * tig + (e & 1);
+        float v = sacc[nb][e] * sl2;
+        v = row < n ? v : -INFINITY;
+        sacc[nb][e] = v;
+        mt[e >> 1] = fmaxf(mt[e >> 1], v);
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 1));
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 2));
+    }
+    float f[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float m_new = fmaxf(m_run[h], mt[h]);
+      f[h] = ex2_approx(m_run[h] - m_new);
+      m_run[h] = m_new;
+      l_run[h] *= f[h];
+    }
+#pragma unroll
+    for (int nb = 0; nb < NBH; ++nb) {
+      o[nb][0] *= f[0];
+      o[nb][1] *= f[0];
+      o[nb][2] *= f[1];
+      o[nb][3] *= f[1];
+    }
+    float pv[2][4];
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pv[nb][e] = ex2_approx(sacc[nb][e] - m_run[e >> 1]);
+        l_run[e >> 1] += pv[nb][e];
+      }
+    // ---- O += (P * d_v) V per 32-column block of V: the block scale of row t multiplies P[., t]
+#pragma unroll
+    for (int bh = 0; bh < C::NB / 2; ++bh) {
+      const int blk = dh * (C::NB / 2) + bh;
+      float dv[2][2];
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        const int row = r0 + nb * 8 + 2 * tig;
+        dv[nb][0] = __half2float(*reinterpret_cast<const __half*>(vt + row * C::ROW_BYTES + blk * 34));
+        dv[nb][1] = __half2float(*reinterpret_cast<const __half*>(vt + (row + 1) * C::ROW_BYTES + blk * 34));
+      }
+      const uint32_t pa0 = pack_h2(pv[0][0] * dv[0][0], pv[0][1] * dv[0][1]);
+      const uint32_t pa1 = pack_h2(pv[0][2] * dv[0][0], pv[0][3] * dv[0][1]);
+      const uint32_t pa2 = pack_h2(pv[1][0] * dv[1][0], pv[1][1] * dv[1][1]);
+      const uint32_t pa3 = pack_h2(pv[1][2] * dv[1][0], pv[1][3] * dv[1][1]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // four 8-column n-blocks per 32-column block
+        const int nb = bh * 4 + q;
+        const int col = q * 8 + grp;  // this thread's column within the block
+        const uint8_t* v0 = vt + (r0 + 2 * tig) * C::ROW_BYTES + blk * 34 + 2 + col;
+        const uint32_t w0 = static_cast<uint32_t>(v0[0]) | (static_cast<uint32_t>(v0[C::ROW_BYTES]) << 8);
+        const uint32_t w1 =
+            static_cast<uint32_t>(v0[8 * C::ROW_BYTES]) | (static_cast<uint32_t>(v0[9 * C::ROW_BYTES]) << 8);
+        mma16816(o[nb], pa0, pa1, pa2, pa3, i8x2_to_h2(w0), i8x2_to_h2(w1));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar.empty[s]);
+  }
+
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+  }
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+  float* ml_s = reinterpret_cast<float*>(smem + C::K_OFF);
+  float* o_s = ml_s + kComputeWarps * 16 * 2;
+  const int rg = warp & 3;  // row group; warps rg and rg + 4 hold the same (max, sum)
+  if (tig == 0 && (warp >> 2) == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ml_s[(rg * 16 + grp + 8 * h) * 2] = m_run[h];
+      ml_s[(rg * 16 + grp + 8 * h) * 2 + 1] = l_run[h];
+    }
+  }
+#pragma unroll
+  for (int nb = 0; nb < NBH; ++nb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = grp + 8 * (e >> 1), col = (warp >> 2) * (D / 2) + nb * 8 + 2 * tig + (e & 1);
+      o_s[(rg * 16 + row) * D + col] = o[nb][e];
+    }
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+  for (int idx = threadIdx.x; idx < g_count * D; idx += kQ8ComputeWarps * 32) {
+    const int g = idx / D, d = idx % D;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kComputeWarps; ++w) m = fmaxf(m, ml_s[(w * 16 + g) * 2]);
+    float l = 0.0f, acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kComputeWarps; ++w) {
+      const float wt = ex2_approx(ml_s[(w * 16 + g) * 2] - m);
+      l = fmaf(ml_s[(w * 16 + g) * 2 + 1], wt, l);
+      acc = fmaf(o_s[(w * 16 + g) * D + d], wt, acc);
+    }
+    const int h = h0 + g;
+    if (n_splits == 1) {
+      const float v = acc / l;
+      const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * D + d;
+      if (p.out_dtype == AIHOST_F32) static_cast<float*>(p.out)[oidx] = v;
+      else static_cast<__half*>(p.out)[oidx] = __float2half_rn(v);
+    } else {
+      const int64_t pidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * p.max_splits + split;
+      p.part_o[pidx * D + d] = acc;
+      if (d == 0) {
+        p.part_ml[pidx * 2] = m;
+        p.part_ml[pidx * 2 + 1] = l;
+      }
+    }
+  }
+}
+
+template <int D>
+cudaError_t launch_q8(const DecodeMmaArgs& a, cudaStream_t st) {
+  using C = Q8Cfg<D>;
+  auto kern = decode_q8_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int G = a.base.n_q_heads / a.base.n_kv_heads;
+  dim3 grid(a.base.max_splits, a.base.n_kv_heads * ((G + 15) / 16), a.base.batch);
+  kern<<<grid, kQ8Threads, C::SMEM, st>>>(a);
+  return cudaGetLastError();
+}
+
 template <int D>
 cudaError_t launch_d(const DecodeMmaArgs& a, cudaStream_t st) {
   using C = DecodeCfg<D>;
@@ -338,7 +659,10 @@ cudaError_t launch_d(const DecodeMmaArgs& a, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_decode_mma(const DecodeMmaArgs& a, cudaStream_t st) {
+  if (a.base.kv.dtype == AIHOST_Q8_0) return a.base.head_dim == 64 ? launch_q8<64>(a, st) : launch_q8<128>(a, st);
   return a.base.head_dim == 64 ? launch_d<64>(a, st) : launch_d<128>(a, st);
 }
+
+uint32_t q8_box_words(int32_t head_dim) { return head_dim == 64 ? Q8Cfg<64>::BOX_WORDS : Q8Cfg<128>::BOX_WORDS; }
 
 }  // namespace aihost

@@ -71,6 +71,8 @@ struct DecodeMmaArgs {
   CUtensorMap v_map;
 };
 cudaError_t launch_decode_mma(const DecodeMmaArgs& a, cudaStream_t st);
+// Width in 32-bit words of the TMA box that holds one (token, head) slice of a Q8_0 cache.
+uint32_t q8_box_words(int32_t head_dim);
 
 }  // namespace aihost
 struct aihost_attn_ctx;

@@ -350,8 +350,9 @@ cudaError_t launch_decode_any(const DecodeArgs& a, cudaStream_t st, aihost_attn_
     m.base = a;
     char saved[sizeof(g_err)];
     memcpy(saved, g_err, sizeof(g_err));
-    const uint32_t bw = q8_box_words(a.head_dim);
-    if (encode_q8_map(&m.k_map, a.k_cache, a.kv, a.batch, bw) == AIHOST_OK &&
+    const uint32_t bw = q8_box_words(a.head_dim, a.kv.head_stride);
+    m.q8_row_bytes = static_cast<int32_t>(bw * 4);
+    if (bw && encode_q8_map(&m.k_map, a.k_cache, a.kv, a.batch, bw) == AIHOST_OK &&
         encode_q8_map(&m.v_map, a.v_cache, a.kv, a.batch, bw) == AIHOST_OK) {
       e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode_mma(m, st); });
       done = true;

@@ -331,12 +331,17 @@ constexpr int kQ8ComputeWarps = 8;
 constexpr int kQ8Threads = (kQ8ComputeWarps + 1) * 32;
 // Tiles hold raw 34-byte blocks: each cache row's head slice is read by TMA as a box of 32-bit
 // words that starts at the 16-byte boundary at or below the slice (GGUF blocks are only 2-byte
-// aligned), `q8_box_words` wide; the slice then begins `q8_off` words into every tile row.
+// aligned); the slice then begins `off` bytes into every tile row. The box is as narrow as the
+// head offsets allow: with the default 136-byte heads (d = 128) it is 144 bytes, an odd number
+// of 16-byte units, which keeps the row-strided shared loads below free of bank conflicts.
 template <int D>
 struct Q8Cfg {
   static constexpr int NB = D / 32;                   // blocks per head row
   static constexpr int HEAD_WORDS = NB * 34 / 4;      // 17 (D=64) or 34 (D=128) words
-  static constexpr int BOX_WORDS = (HEAD_WORDS + 3 + 3) / 4 * 4;  // room for a 0..3-word start offset
+  // box: the head slice plus up to 2 (d = 128) or 3 (d = 64) words of start offset, which
+  // covers every head of the default GGUF layout (136- / 68-byte heads). 36 and 20 words are odd
+  // multiples of 16 bytes, so row-strided shared loads hit distinct banks.
+  static constexpr int BOX_WORDS = (HEAD_WORDS + 2 + 3) / 4 * 4;
   static constexpr int ROW_BYTES = BOX_WORDS * 4;
   static constexpr int TILE_BYTES = kTileRows * ROW_BYTES;
   static constexpr int NS = 4;
@@ -391,6 +396,7 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
   const int head_word = static_cast<int>(kvh * (p.kv.head_stride / 4));
   const int box_x = head_word & ~3;
   const int off = (head_word - box_x) * 4;  // byte offset of the head slice in a tile row
+  constexpr int ROW = C::ROW_BYTES;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NS; ++i) {
@@ -435,7 +441,7 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
       for (int i = 0; i < n_tiles; ++i) {
         const int s = i % C::NS;
         if (!mbar_wait(&bar.empty[s], ((i / C::NS) & 1) ^ 1, p.status)) break;
-        mbar_arrive_expect_tx(&bar.full[s], 2 * C::TILE_BYTES);
+        mbar_arrive_expect_tx(&bar.full[s], 2 * kTileRows * ROW);  // bytes the two boxes deliver
         const int row = t0 + i * kTileRows;
         tma_load_4d(smem + C::K_OFF + s * C::TILE_BYTES, &a.k_map, &bar.full[s], box_x, row, b, 0);
         tma_load_4d(smem + C::V_OFF + s * C::TILE_BYTES, &a.v_map, &bar.full[s], box_x, row, b, 0);
@@ -476,8 +482,8 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
       for (int c = lane; c < 16 * C::NB; c += 32) {
         const int rr = c / C::NB, blk = c % C::NB;
         if (base_row + rr >= n) {
-          *reinterpret_cast<uint16_t*>(vt + (r0 + rr) * C::ROW_BYTES + blk * 34) = 0;
-          *reinterpret_cast<uint16_t*>(const_cast<uint8_t*>(kt) + (r0 + rr) * C::ROW_BYTES + blk * 34) = 0;
+          *reinterpret_cast<uint16_t*>(vt + (r0 + rr) * ROW + blk * 34) = 0;
+          *reinterpret_cast<uint16_t*>(const_cast<uint8_t*>(kt) + (r0 + rr) * ROW + blk * 34) = 0;
         }
       }
     }
@@ -490,7 +496,7 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
       float sb[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb) {
-        const uint8_t* krow = kt + (r0 + nb * 8 + grp) * C::ROW_BYTES + blk * 34 + 2;
+        const uint8_t* krow = kt + (r0 + nb * 8 + grp) * ROW + blk * 34 + 2;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {  // the block's two 16-column k-steps
           const int kk = blk * 2 + h;
@@ -502,8 +508,8 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb) {
         const int row = r0 + nb * 8 + 2 * tig;
-        const float d0 = __half2float(*reinterpret_cast<const __half*>(kt + row * C::ROW_BYTES + blk * 34));
-        const float d1 = __half2float(*reinterpret_cast<const __half*>(kt + (row + 1) * C::ROW_BYTES + blk * 34));
+        const float d0 = __half2float(*reinterpret_cast<const __half*>(kt + row * ROW + blk * 34));
+        const float d1 = __half2float(*reinterpret_cast<const __half*>(kt + (row + 1) * ROW + blk * 34));
         sacc[nb][0] = fmaf(d0, sb[nb][0], sacc[nb][0]);
         sacc[nb][1] = fmaf(d1, sb[nb][1], sacc[nb][1]);
         sacc[nb][2] = fmaf(d0, sb[nb][2], sacc[nb][2]);
@@ -557,8 +563,8 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb) {
         const int row = r0 + nb * 8 + 2 * tig;
-        dv[nb][0] = __half2float(*reinterpret_cast<const __half*>(vt + row * C::ROW_BYTES + blk * 34));
-        dv[nb][1] = __half2float(*reinterpret_cast<const __half*>(vt + (row + 1) * C::ROW_BYTES + blk * 34));
+        dv[nb][0] = __half2float(*reinterpret_cast<const __half*>(vt + row * ROW + blk * 34));
+        dv[nb][1] = __half2float(*reinterpret_cast<const __half*>(vt + (row + 1) * ROW + blk * 34));
       }
       const uint32_t pa0 = pack_h2(pv[0][0] * dv[0][0], pv[0][1] * dv[0][1]);
       const uint32_t pa1 = pack_h2(pv[0][2] * dv[0][0], pv[0][3] * dv[0][1]);
@@ -568,10 +574,10 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
       for (int q = 0; q < 4; ++q) {  // four 8-column n-blocks per 32-column block
         const int nb = bh * 4 + q;
         const int col = q * 8 + grp;  // this thread's column within the block
-        const uint8_t* v0 = vt + (r0 + 2 * tig) * C::ROW_BYTES + blk * 34 + 2 + col;
-        const uint32_t w0 = static_cast<uint32_t>(v0[0]) | (static_cast<uint32_t>(v0[C::ROW_BYTES]) << 8);
+        const uint8_t* v0 = vt + (r0 + 2 * tig) * ROW + blk * 34 + 2 + col;
+        const uint32_t w0 = static_cast<uint32_t>(v0[0]) | (static_cast<uint32_t>(v0[ROW]) << 8);
         const uint32_t w1 =
-            static_cast<uint32_t>(v0[8 * C::ROW_BYTES]) | (static_cast<uint32_t>(v0[9 * C::ROW_BYTES]) << 8);
+            static_cast<uint32_t>(v0[8 * ROW]) | (static_cast<uint32_t>(v0[9 * ROW]) << 8);
         mma16816(o[nb], pa0, pa1, pa2, pa3, i8x2_to_h2(w0), i8x2_to_h2(w1));
       }
     }
@@ -663,6 +669,13 @@ cudaError_t launch_decode_mma(const DecodeMmaArgs& a, cudaStream_t st) {
   return a.base.head_dim == 64 ? launch_d<64>(a, st) : launch_d<128>(a, st);
 }
 
-uint32_t q8_box_words(int32_t head_dim) { return head_dim == 64 ? Q8Cfg<64>::BOX_WORDS : Q8Cfg<128>::BOX_WORDS; }
+uint32_t q8_box_words(int32_t head_dim, int64_t head_stride) {
+  // 0 when some head would start further past its 16-byte boundary than the box allows
+  const int64_t hs = head_stride / 4;
+  const int max_off = hs % 4 == 0 ? 0 : hs % 2 == 0 ? 2 : 3;
+  const int head_words = head_dim / 32 * 34 / 4;
+  const int box = head_dim == 64 ? Q8Cfg<64>::BOX_WORDS : Q8Cfg<128>::BOX_WORDS;
+  return head_words + max_off <= box ? static_cast<uint32_t>(box) : 0u;
+}
 
 }  // namespace aihost

@@ -67,12 +67,14 @@ cudaError_t launch_decode_combine(const DecodeArgs& a, cudaStream_t st);
 // fp16-cache decode on the tensor cores: K/V maps over the cache with 64-row boxes.
 struct DecodeMmaArgs {
   DecodeArgs base;
+  int32_t q8_row_bytes;  // Q8_0 only: bytes per tile row (the TMA box width), 16-byte multiple
   CUtensorMap k_map;  // dims {d, Hkv, capacity, batch}, box {64, 1, 64, 1}, 128-byte swizzle
   CUtensorMap v_map;
 };
 cudaError_t launch_decode_mma(const DecodeMmaArgs& a, cudaStream_t st);
-// Width in 32-bit words of the TMA box that holds one (token, head) slice of a Q8_0 cache.
-uint32_t q8_box_words(int32_t head_dim);
+// Width in 32-bit words of the TMA box that holds one (token, head) slice of a Q8_0 cache whose
+// heads are head_stride bytes apart (the narrowest 16-byte multiple every head offset fits).
+uint32_t q8_box_words(int32_t head_dim, int64_t head_stride);
 
 }  // namespace aihost
 struct aihost_attn_ctx;

@@ -42,6 +42,9 @@ def parse_args():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode object")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time")
+    ap.add_argument("--shard", default="seq", choices=["seq", "heads"],
+                    help="N>1: seq = every rank runs its own sequences (weak scaling); heads = the KV heads "
+                         "of one problem are split over the ranks and the head outputs all-gathered (strong)")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N untimed fused calls of --config and exit (the command profiled with ncu)")
     return ap.parse_args()
@@ -193,28 +196,60 @@ def device_inputs(cfg, device, rank):
     return inp
 
 
-def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on):
+def shard_inputs(cfg, device, rank, world):
+    """This rank's share of `cfg` under KV-head sharding: its Q / new K / V heads and its local
+    cache slice (seeded per rank), laid out with the shard's (16-byte padded) token stride."""
+    import torch
+
+    from aihost_b200.configs import make_inputs
+    from aihost_b200.ops import row_bytes
+    from aihost_b200.shard import HeadShard
+
+    shard = HeadShard(cfg.spec(cfg.capacity()), rank, world)
+    local = cfg.scaled(number=cfg.number + 1000 * rank, n_q_heads=shard.q_per_rank, n_kv_heads=shard.kv_per_rank)
+    inp = make_inputs(local, device=device)
+    spec = shard.local_spec()
+    spec.kv_capacity = inp["capacity"]
+    rb = row_bytes(cfg.kv_dtype, cfg.head_dim) * shard.kv_per_rank
+    if spec.kv_token_stride != rb:  # pad each token row (one Q8_0 head: 136 -> 144 bytes)
+        for name in ("k_cache", "v_cache"):
+            src = inp[name].view(cfg.batch, inp["capacity"], rb)
+            dst = torch.zeros(cfg.batch, inp["capacity"], spec.kv_token_stride, dtype=torch.uint8, device=device)
+            dst[:, :, :rb] = src
+            inp[name] = dst.reshape(-1)
+    inp["lengths"] = cfg.lengths()
+    inp["seq_len"] = torch.tensor(inp["lengths"], dtype=torch.int32, device=device)
+    return inp, spec, shard, local
+
+
+def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_heads=False):
     import torch
 
     import aihost_b200 as A
     from aihost_b200.ops import ComputeOps, KVCache
 
     rank = int(os.environ.get("RANK", "0"))
-    inp = device_inputs(cfg, device, rank)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if shard_heads:
+        inp, spec, shard, local_cfg = shard_inputs(cfg, device, rank, world)
+    else:
+        inp = device_inputs(cfg, device, rank)
+        spec, shard, local_cfg = cfg.spec(inp["capacity"]), None, cfg
     lengths = inp["lengths"]
-    spec = cfg.spec(inp["capacity"])
     cache = KVCache(ctx, spec, batch=cfg.batch, n_layers=1, device=device)
     cache.k[0], cache.v[0] = inp["k_cache"], inp["v_cache"]
     cache.seq_len, cache.host_len = inp["seq_len"], list(lengths)
     q, kn, vn = inp["q"], inp["k_new"], inp["v_new"]
     ops = ComputeOps(ctx)
     out = ops.attention_layer(q, kn, vn, cache)  # also reserves scratch
-    w = work(cfg, lengths)
+    w = work(local_cfg, lengths)  # this rank's work
     need_flush = w["bytes"] < 2 * 126e6  # L2 is 126 MB: flush unless the step streams more than 2x that
     flush = torch.empty(flush_bytes, dtype=torch.uint8, device=device) if need_flush else None
 
     def step():
         ops.attention_layer(q, kn, vn, cache, out=out)
+        if shard is not None and world > 1:
+            shard.gather(out)  # NCCL all-gather of every rank's head outputs (rank-major)
 
     for _ in range(warmup):
         if flush is not None:
@@ -271,7 +306,7 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on):
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
     return dict(ms=ms, wall=wall, kern=kern, launches=launches, e2e_ms=e_ms, h2d=h2d, d2h=d2h, work=w,
-                lengths=lengths, flushed=need_flush)
+                lengths=lengths, flushed=need_flush, sharded=shard is not None)
 
 
 def profile_steps(cfg, n, device):
@@ -312,8 +347,10 @@ def summarize(cfg, r, n_gpus, dist_on, pk, pk_kind):
         unit, per_step = "TFLOP/s", w["flops"] * 1e-12
     else:
         unit, per_step = "tokens/s", float(w["tokens"])
-    value = n_gpus * per_step / (ms_step * 1e-3)
-    e2e_value = n_gpus * per_step / (e2e_ms * 1e-3)
+    # FLOPs and bytes add up over ranks; under head sharding every rank serves the same tokens
+    ranks = 1 if (r.get("sharded") and not prefill) else n_gpus
+    value = ranks * per_step / (ms_step * 1e-3)
+    e2e_value = ranks * per_step / (e2e_ms * 1e-3)
     kname = "prefill" if prefill else "decode"
     n_k, tot = r["kern"][kname]
     k_ms = max_over_ranks(tot / max(n_k, 1), dist_on)
@@ -473,7 +510,8 @@ def main():
     clocks = ClockSampler(local).start()
     cfg = CONFIGS[args.config]
     flush_bytes = 512 << 20
-    r = bench_ours(cfg, args.steps, args.warmup, device, ctx, flush_bytes, dist_on)
+    heads = args.shard == "heads"
+    r = bench_ours(cfg, args.steps, args.warmup, device, ctx, flush_bytes, dist_on, shard_heads=heads)
     main_res = summarize(cfg, r, ws, dist_on, pk, pk_kind)
     dec = None
     if args.config == 2 and not args.no_decode:
@@ -489,11 +527,13 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": main_res["value"], "unit": main_res["unit"], "n_gpus": ws,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": main_res["ms_per_step"],
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "higher_is_better": True, "scaling": "strong" if heads else "weak", "vs_baseline": None,
                 "dtype": "f16 (fp32 accumulate)" if cfg.q_dtype == 1 else "f32",
                 "data": "synthetic (seeded SplitMix64 + Box-Muller, no model weights)",
                 "config": {**cfg_desc(cfg, r["lengths"], r["flushed"]),
-                           "parallelism": "one independent sequence per rank" if ws > 1 else "single GPU"},
+                           "parallelism": (f"KV heads split over {ws} ranks + NCCL all-gather of head outputs"
+                                           if heads else "one independent sequence set per rank")
+                           if ws > 1 else "single GPU"},
                 "roofline": main_res["roofline"], "cpu_baseline": cpu, "e2e": main_res["e2e"],
                 "gpu_launches": main_res["gpu_launches"], "clocks": clk, "kernels": main_res["kernels"],
                 "wall_s_timed_region": r["wall"]}

@@ -1,0 +1,86 @@
+"""KV-head sharding host logic on CPU: two gloo ranks each compute their heads (with the CPU
+oracle standing in for the GPU kernels) and the all-gather must rebuild the unsharded result."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from aihost_b200 import F16, F32, Q8_0, ROPE_INTERLEAVED
+from aihost_b200.configs import CONFIGS, make_inputs
+from aihost_b200.ops import row_bytes
+from aihost_b200.shard import HeadShard
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _local_cache(full_cache: torch.Tensor, cfg, shard: HeadShard, capacity: int) -> torch.Tensor:
+    """The rank's slice of a full token-major cache, re-laid with the local token stride."""
+    rb = row_bytes(cfg.kv_dtype, cfg.head_dim)
+    full = full_cache.view(cfg.batch, capacity, cfg.n_kv_heads * rb)
+    part = full[:, :, shard.kv0 * rb:(shard.kv0 + shard.kv_per_rank) * rb]
+    tok = shard.local_spec().kv_token_stride
+    out = torch.zeros(cfg.batch, capacity, tok, dtype=torch.uint8)
+    out[:, :, :part.shape[2]] = part
+    return out.reshape(-1)
+
+
+def _worker(rank, world, port, cfg_num, kv, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as orc
+
+        cfg = CONFIGS[cfg_num].scaled(batch=2, n_q_heads=8, n_kv_heads=4, head_dim=64, kv_dtype=kv,
+                                      q_dtype=F32 if kv == F32 else F16, out_dtype=F32, cached_range=None,
+                                      cached=None, cached_list=[37, 90], rope_mode=ROPE_INTERLEAVED)
+        inp = make_inputs(cfg, capacity=96)
+        shard = HeadShard(cfg.spec(96), rank, world)
+        ls = shard.local_spec()
+        kc = _local_cache(inp["k_cache"], cfg, shard, 96).numpy()
+        vc = _local_cache(inp["v_cache"], cfg, shard, 96).numpy()
+        out_l = orc.attn_forward(ls.desc(), shard.slice_q(inp["q"]).numpy(), shard.slice_kv(inp["k_new"]).numpy(),
+                                 shard.slice_kv(inp["v_new"]).numpy(), kc, vc, inp["seq_len"].numpy())
+        gathered = shard.gather(torch.from_numpy(out_l))
+        full = HeadShard.to_reference_layout(gathered)
+        if rank == 0:
+            ref = orc.attn_forward(cfg.spec(96).desc(), inp["q"].numpy(), inp["k_new"].numpy(),
+                                   inp["v_new"].numpy(), inp["k_cache"].numpy().copy(),
+                                   inp["v_cache"].numpy().copy(), inp["seq_len"].numpy())
+            result_q.put(float(np.abs(full.numpy() - ref).max()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kv", [F32, Q8_0])
+def test_head_sharded_gather_matches_unsharded(kv):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, 3, kv, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    err = q.get(timeout=5)
+    assert err == 0.0, err
+
+
+def test_local_spec_pads_q8_token_stride():
+    spec = CONFIGS[5].spec(16385)
+    sh = HeadShard(spec, 3, 8)
+    ls = sh.local_spec()
+    assert (ls.n_q_heads, ls.n_kv_heads) == (8, 1)
+    assert ls.kv_head_stride == 136 and ls.kv_token_stride == 144
+    with pytest.raises(ValueError):
+        HeadShard(CONFIGS[2].spec(2048), 0, 4)  # 2 KV heads over 4 ranks

@@ -27,7 +27,7 @@ EXPORTS = (
     "aihost_attn_profiler_read", "aihost_attn_profiler_reset", "aihost_attn_decode_noalloc",
 )
 # aihost_kernel ids of the device-time profiler
-KERNEL_APPEND, KERNEL_DECODE, KERNEL_COMBINE, KERNEL_PREFILL = range(4)
+KERNEL_APPEND, KERNEL_DECODE, KERNEL_COMBINE, KERNEL_PREFILL, KERNEL_CONVERT = range(5)
 
 
 class AttnDesc(ctypes.Structure):

@@ -282,13 +282,67 @@ aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const 
   return AIHOST_OK;
 }
 
-aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const KvLayout& kv, float scale,
+size_t round256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Scratch for the fp16 copies the prefill kernel reads when q is fp32 or the cache is fp32 /
+// Q8_0 (zero for fp16 operands): q [batch][n_q][Hq][d], K and V [batch][kv_rows][Hkv][d].
+size_t prefill_stage_bytes(const aihost_attn_desc* d, int32_t batch, int32_t n_q, int32_t kv_rows) {
+  size_t bytes = 0;
+  if (d->q_dtype != AIHOST_F16)
+    bytes += round256(static_cast<size_t>(batch) * n_q * d->n_q_heads * d->head_dim * 2);
+  if (d->kv_dtype != AIHOST_F16)
+    bytes += 2 * round256(static_cast<size_t>(batch) * kv_rows * d->n_kv_heads * d->head_dim * 2);
+  return bytes;
+}
+
+// Prefill of n_q query rows per sequence over cache rows [0, start_b + len_offset), where
+// start_b = seq_len[b] (or start_scalar) and at most kv_rows rows are attended by any sequence.
+// fp32 q and fp32 / Q8_0 caches are first converted to fp16 in the context's scratch (q rotated
+// in fp32 on the way), then the same tensor-core kernel runs on the copies.
+aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const KvLayout& kv_in, float scale,
                           int32_t batch, int32_t n_q, const void* q, const void* kc, const void* vc,
-                          const int32_t* seq_len, int32_t start_scalar, int32_t len_offset, int32_t rope_mode,
-                          void* out, cudaStream_t st) {
-  if (d->q_dtype != AIHOST_F16 || d->kv_dtype != AIHOST_F16)
-    return fail(AIHOST_EUNSUPPORTED, "prefill (n_new > 1) needs F16 q and F16 cache in this build");
+                          const int32_t* seq_len, int32_t start_scalar, int32_t len_offset, int32_t kv_rows,
+                          int32_t rope_mode, void* out, cudaStream_t st) {
   if (!prefill_supported(d->head_dim)) return fail(AIHOST_EUNSUPPORTED, "prefill head_dim %d", d->head_dim);
+  KvLayout kv = kv_in;
+  if (d->q_dtype != AIHOST_F16 || d->kv_dtype != AIHOST_F16) {
+    const size_t need = prefill_stage_bytes(d, batch, n_q, kv_rows);
+    if (need > ctx->scratch_bytes)
+      return fail(AIHOST_ENOMEM,
+                  "prefill with fp32 / Q8_0 operands needs %zu bytes of scratch, context has %zu "
+                  "(call aihost_attn_reserve with aihost_attn_workspace_size)",
+                  need, ctx->scratch_bytes);
+    uint8_t* sp = static_cast<uint8_t*>(ctx->scratch);
+    if (d->q_dtype != AIHOST_F16) {
+      __half* qh = reinterpret_cast<__half*>(sp);
+      sp += round256(static_cast<size_t>(batch) * n_q * d->n_q_heads * d->head_dim * 2);
+      const RopeFreqs fr = make_freqs(rope_mode != AIHOST_ROPE_NONE ? d->rope_theta : 1.0f, d->head_dim);
+      cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_CONVERT, st, [&] {
+        return launch_stage_q(static_cast<const float*>(q), qh, seq_len, start_scalar, batch, n_q, d->n_q_heads,
+                              d->head_dim, rope_mode, fr, st);
+      });
+      if (e != cudaSuccess) return cuda_fail(e, "q staging launch");
+      q = qh;
+      rope_mode = AIHOST_ROPE_NONE;
+    }
+    if (d->kv_dtype != AIHOST_F16) {
+      const size_t part = round256(static_cast<size_t>(batch) * kv_rows * d->n_kv_heads * d->head_dim * 2);
+      __half* kh = reinterpret_cast<__half*>(sp);
+      __half* vh = reinterpret_cast<__half*>(sp + part);
+      cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_CONVERT, st, [&] {
+        return launch_stage_kv(kc, vc, kv, kh, vh, kv_rows, seq_len, start_scalar, len_offset, batch, d->n_kv_heads,
+                               d->head_dim, st);
+      });
+      if (e != cudaSuccess) return cuda_fail(e, "cache staging launch");
+      kc = kh;
+      vc = vh;
+      kv.head_stride = 2LL * d->head_dim;
+      kv.token_stride = kv.head_stride * d->n_kv_heads;
+      kv.seq_stride = kv.token_stride * kv_rows;
+      kv.capacity = kv_rows;
+      kv.dtype = AIHOST_F16;
+    }
+  }
   PrefillArgs a;
   memset(&a, 0, sizeof(a));
   const int64_t D = d->head_dim, Hq = d->n_q_heads;
@@ -440,7 +494,7 @@ aihost_status aihost_attn_workspace_size(const aihost_attn_desc* desc, int32_t b
   aihost_status s = check_desc(desc, &kv, &scale);
   if (s != AIHOST_OK) return s;
   if (batch < 1 || n_new < 1) return fail(AIHOST_EINVAL, "batch (%d) and n_new (%d) must be >= 1", batch, n_new);
-  *out_bytes = 0;
+  *out_bytes = prefill_stage_bytes(desc, batch, n_new, desc->kv_capacity);
   if (n_new == 1) {
     int sms = 148;
     int dev = 0;
@@ -497,8 +551,6 @@ aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* 
   DeviceGuard g(ctx->device);
   if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (n_new > 1 && (desc->q_dtype != AIHOST_F16 || desc->kv_dtype != AIHOST_F16))
-    return fail(AIHOST_EUNSUPPORTED, "prefill (n_new > 1) needs F16 q and F16 cache in this build");
   const RopeFreqs freqs = make_freqs(desc->rope_mode != AIHOST_ROPE_NONE ? desc->rope_theta : 1.0f, desc->head_dim);
   cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_APPEND, st, [&] {
     return launch_kv_append(k_new, v_new, desc->q_dtype, k_cache, v_cache, kv, seq_len, batch, n_new,
@@ -507,8 +559,13 @@ aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* 
   if (e != cudaSuccess) return cuda_fail(e, "kv append launch");
   if (n_new == 1)
     return run_decode(ctx, desc, kv, scale, batch, q, k_cache, v_cache, seq_len, 0, 1, desc->rope_mode, out, st);
-  return run_prefill(ctx, desc, kv, scale, batch, n_new, q, k_cache, v_cache, seq_len, 0, n_new, desc->rope_mode, out,
-                     st);
+  int32_t kv_rows = desc->kv_capacity;
+  if (h_seq_len) {
+    kv_rows = 0;
+    for (int32_t b = 0; b < batch; ++b) kv_rows = h_seq_len[b] + n_new > kv_rows ? h_seq_len[b] + n_new : kv_rows;
+  }
+  return run_prefill(ctx, desc, kv, scale, batch, n_new, q, k_cache, v_cache, seq_len, 0, n_new, kv_rows,
+                     desc->rope_mode, out, st);
 }
 
 aihost_status aihost_attn_mha(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t n_q, int32_t n_kv,
@@ -532,8 +589,8 @@ aihost_status aihost_attn_mha(aihost_attn_ctx* ctx, const aihost_attn_desc* desc
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (n_q == 1)  // FusedMHAGenerate: every row visible, no mask
     return run_decode(ctx, desc, kv, scale, 1, q, k, v, nullptr, 0, n_kv, AIHOST_ROPE_NONE, out, st);
-  return run_prefill(ctx, desc, kv, scale, 1, n_q, q, k, v, nullptr, start_pos, n_kv - start_pos, AIHOST_ROPE_NONE,
-                     out, st);
+  return run_prefill(ctx, desc, kv, scale, 1, n_q, q, k, v, nullptr, start_pos, n_kv - start_pos, n_kv,
+                     AIHOST_ROPE_NONE, out, st);
 }
 
 aihost_status aihost_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,

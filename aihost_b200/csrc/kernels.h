@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -33,6 +34,17 @@ cudaError_t launch_kv_append(const void* k_new, const void* v_new, int32_t in_dt
                              void* v_cache, const KvLayout& kv, const int32_t* seq_len, int32_t batch,
                              int32_t n_new, int32_t n_kv_heads, int32_t head_dim, int32_t rope_mode,
                              const RopeFreqs& freqs, int32_t* status, cudaStream_t st);
+
+// fp16 staging for the prefill: q [batch][n_q][Hq][d] fp32 -> fp16, rotated at start_b + s
+// (start_b = seq_len[b], or start_scalar when seq_len is NULL) unless rope_mode is NONE.
+cudaError_t launch_stage_q(const float* q, __half* dst, const int32_t* seq_len, int32_t start_scalar, int32_t batch,
+                           int32_t n_q, int32_t n_heads, int32_t head_dim, int32_t rope_mode, const RopeFreqs& freqs,
+                           cudaStream_t st);
+// Cache rows [0, start_b + len_offset) (at most `rows`) of an fp32 / Q8_0 cache -> dense fp16
+// [batch][rows][Hkv][d] copies of K and V.
+cudaError_t launch_stage_kv(const void* k_cache, const void* v_cache, const KvLayout& kv, __half* k_dst,
+                            __half* v_dst, int32_t rows, const int32_t* seq_len, int32_t start_scalar,
+                            int32_t len_offset, int32_t batch, int32_t n_kv_heads, int32_t head_dim, cudaStream_t st);
 
 // ---------------------------------------------------------------- decode.cu
 struct DecodeArgs {

@@ -8,6 +8,8 @@
 //                      converts to the cache dtype (fp32 copy, fp16 round-to-nearest-even, or
 //                      GGUF Q8_0 quantisation with ggml's reference rule d = amax/127,
 //                      q = roundf(x * (1/d)), d stored as fp16).
+// stage_q_kernel / stage_kv_kernel: fp32 Q and fp32 / Q8_0 cache rows converted to fp16 for
+//                      the tensor-core prefill (the reference computes those in fp32 shaders).
 // Rotation arithmetic uses explicitly rounded multiplies/adds (no FMA contraction), so a
 // kernel and a CPU restatement that see the same cos/sin produce the same bits.
 #include "common.cuh"
@@ -46,6 +48,35 @@ __global__ void rope_full_kernel(T* __restrict__ x, int32_t seq, int32_t n_heads
   }
 }
 
+// RoPE of one head row held by a warp (lane l holds elements [l*E, l*E+E), E = D/32) at
+// position `pos`. Interleaved pairs (2i, 2i+1) sit in one lane; NEOX pairs (i, i + D/2) sit in
+// lanes l and l ^ 16.
+template <int E>
+__device__ __forceinline__ void rope_row_warp(float (&x)[E], int32_t lane, float pos, int32_t rope_mode,
+                                              const RopeFreqs& freqs) {
+  if (rope_mode == AIHOST_ROPE_INTERLEAVED) {
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      const int pair = (lane * E + e) >> 1;
+      float sn, cs;
+      sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
+      rotate_pair(x[e], x[e + 1], cs, sn);
+    }
+  } else if (rope_mode == AIHOST_ROPE_NEOX) {
+    const bool lo = lane < 16;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+      const int pair = (lane & 15) * E + e;
+      float sn, cs;
+      sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
+      float x1 = lo ? x[e] : other, x2 = lo ? other : x[e];
+      rotate_pair(x1, x2, cs, sn);
+      x[e] = lo ? x1 : x2;
+    }
+  }
+}
+
 __device__ __forceinline__ float load_in(const float* p) { return *p; }
 __device__ __forceinline__ float load_in(const __half* p) { return __half2float(*p); }
 
@@ -76,30 +107,7 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
 #pragma unroll
   for (int e = 0; e < E; ++e) x[e] = load_in(src + e);
 
-  if (is_k && rope_mode != AIHOST_ROPE_NONE) {
-    const float pos = static_cast<float>(t);
-    if (rope_mode == AIHOST_ROPE_INTERLEAVED) {
-#pragma unroll
-      for (int e = 0; e < E; e += 2) {
-        const int pair = (lane * E + e) >> 1;
-        float sn, cs;
-        sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
-        rotate_pair(x[e], x[e + 1], cs, sn);
-      }
-    } else {  // NEOX: element i pairs with i + D/2, which lives in lane ^ 16
-      const bool lo = lane < 16;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
-        const int pair = (lane & 15) * E + e;
-        float sn, cs;
-        sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
-        float x1 = lo ? x[e] : other, x2 = lo ? other : x[e];
-        rotate_pair(x1, x2, cs, sn);
-        x[e] = lo ? x1 : x2;
-      }
-    }
-  }
+  if (is_k && rope_mode != AIHOST_ROPE_NONE) rope_row_warp<E>(x, lane, static_cast<float>(t), rope_mode, freqs);
 
   uint8_t* dst = (is_k ? k_cache : v_cache) + b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride +
                  static_cast<int64_t>(h) * kv.head_stride;
@@ -132,6 +140,75 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
       bp[1 + (sub * E + e) / 2] = static_cast<uint16_t>(q0 | (q1 << 8));
     }
   }
+}
+
+
+// fp16 staging for the tensor-core prefill, whose operands are fp16 (fp32 accumulation).
+// stage_q_kernel: q [B][S][Hq][D] fp32 -> fp16, rotated at position start_b + s on the way (one
+// rounding to fp16, after the fp32 rotation). One warp per head row.
+template <int D>
+__global__ void stage_q_kernel(const float* __restrict__ q, __half* __restrict__ dst, const int32_t* __restrict__ seq_len,
+                               int32_t start_scalar, int32_t batch, int32_t n_q, int32_t n_heads, int32_t rope_mode,
+                               RopeFreqs freqs) {
+  constexpr int E = D / 32;
+  const int32_t lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= static_cast<int64_t>(batch) * n_q * n_heads) return;
+  const int32_t s = static_cast<int32_t>((row / n_heads) % n_q);
+  const int32_t b = static_cast<int32_t>(row / (static_cast<int64_t>(n_heads) * n_q));
+  float x[E];
+  const float* src = q + row * D + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = src[e];
+  if (rope_mode != AIHOST_ROPE_NONE) {
+    const int32_t start = seq_len ? seq_len[b] : start_scalar;
+    rope_row_warp<E>(x, lane, static_cast<float>(start + s), rope_mode, freqs);
+  }
+  __half2* d2 = reinterpret_cast<__half2*>(dst + row * D + lane * E);
+#pragma unroll
+  for (int e = 0; e < E; e += 2) d2[e / 2] = __floats2half2_rn(x[e], x[e + 1]);
+}
+
+// stage_kv_kernel: cache rows [0, start_b + len_offset) of an fp32 or Q8_0 cache -> a dense fp16
+// [B][rows][Hkv][D] copy (rows past a sequence's length are left as they are: the prefill kernel
+// masks them). Q8_0 values are d * q in fp32, then rounded once to fp16. blockIdx.y: 0 = K, 1 = V.
+template <int D>
+__global__ void stage_kv_kernel(const uint8_t* __restrict__ k_cache, const uint8_t* __restrict__ v_cache, KvLayout kv,
+                                __half* __restrict__ k_dst, __half* __restrict__ v_dst, int32_t rows,
+                                const int32_t* __restrict__ seq_len, int32_t start_scalar, int32_t len_offset,
+                                int32_t batch, int32_t n_kv_heads) {
+  constexpr int E = D / 32;
+  const int32_t lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= static_cast<int64_t>(batch) * rows * n_kv_heads) return;
+  const int32_t h = static_cast<int32_t>(row % n_kv_heads);
+  const int32_t t = static_cast<int32_t>((row / n_kv_heads) % rows);
+  const int32_t b = static_cast<int32_t>(row / (static_cast<int64_t>(n_kv_heads) * rows));
+  const int32_t len = (seq_len ? seq_len[b] : start_scalar) + len_offset;
+  if (t >= len || t >= kv.capacity) return;
+  const bool is_k = blockIdx.y == 0;
+  const uint8_t* src = (is_k ? k_cache : v_cache) + b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride +
+                       static_cast<int64_t>(h) * kv.head_stride;
+  float x[E];
+  if (kv.dtype == AIHOST_F32) {
+    const float* f = reinterpret_cast<const float*>(src) + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = f[e];
+  } else {  // Q8_0: element i is in block i / 32 (34 bytes: fp16 d, then 32 int8)
+    const int i0 = lane * E;
+    const uint8_t* blk = src + (i0 / 32) * 34;
+    const float dsc = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
+    const uint16_t* qs = reinterpret_cast<const uint16_t*>(blk + 2 + (i0 % 32));  // even offset: 2-byte loads
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      const uint16_t w = qs[e / 2];
+      x[e] = __fmul_rn(dsc, static_cast<float>(static_cast<int8_t>(w & 0xff)));
+      x[e + 1] = __fmul_rn(dsc, static_cast<float>(static_cast<int8_t>(w >> 8)));
+    }
+  }
+  __half2* d2 = reinterpret_cast<__half2*>((is_k ? k_dst : v_dst) + row * D + lane * E);
+#pragma unroll
+  for (int e = 0; e < E; e += 2) d2[e / 2] = __floats2half2_rn(x[e], x[e + 1]);
 }
 
 }  // namespace
@@ -174,6 +251,41 @@ cudaError_t launch_kv_append(const void* k_new, const void* v_new, int32_t in_dt
     else AIHOST_APPEND(__half, 128);
   }
 #undef AIHOST_APPEND
+  return cudaGetLastError();
+}
+
+
+cudaError_t launch_stage_q(const float* q, __half* dst, const int32_t* seq_len, int32_t start_scalar, int32_t batch,
+                           int32_t n_q, int32_t n_heads, int32_t head_dim, int32_t rope_mode, const RopeFreqs& freqs,
+                           cudaStream_t st) {
+  const int64_t rows = static_cast<int64_t>(batch) * n_q * n_heads;
+  if (rows == 0) return cudaSuccess;
+  const int warps = 8;
+  const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
+  if (head_dim == 64)
+    stage_q_kernel<64><<<grid, warps * 32, 0, st>>>(q, dst, seq_len, start_scalar, batch, n_q, n_heads, rope_mode,
+                                                    freqs);
+  else
+    stage_q_kernel<128><<<grid, warps * 32, 0, st>>>(q, dst, seq_len, start_scalar, batch, n_q, n_heads, rope_mode,
+                                                     freqs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_stage_kv(const void* k_cache, const void* v_cache, const KvLayout& kv, __half* k_dst,
+                            __half* v_dst, int32_t rows, const int32_t* seq_len, int32_t start_scalar,
+                            int32_t len_offset, int32_t batch, int32_t n_kv_heads, int32_t head_dim, cudaStream_t st) {
+  const int64_t n = static_cast<int64_t>(batch) * rows * n_kv_heads;
+  if (n == 0) return cudaSuccess;
+  const int warps = 8;
+  dim3 grid(static_cast<unsigned>((n + warps - 1) / warps), 2);
+  auto* kc = static_cast<const uint8_t*>(k_cache);
+  auto* vc = static_cast<const uint8_t*>(v_cache);
+  if (head_dim == 64)
+    stage_kv_kernel<64><<<grid, warps * 32, 0, st>>>(kc, vc, kv, k_dst, v_dst, rows, seq_len, start_scalar,
+                                                     len_offset, batch, n_kv_heads);
+  else
+    stage_kv_kernel<128><<<grid, warps * 32, 0, st>>>(kc, vc, kv, k_dst, v_dst, rows, seq_len, start_scalar,
+                                                      len_offset, batch, n_kv_heads);
   return cudaGetLastError();
 }
 

@@ -193,8 +193,7 @@ class ComputeOps:
         out = torch.empty(seq, dq, dtype=out_dtype, device=Q.device)
         spec = LayerSpec(num_heads, n_kv_heads, head_dim, rope_mode=ROPE_NONE, q_dtype=dtype_code(Q),
                          kv_dtype=dtype_code(K), out_dtype=dtype_code(out), kv_capacity=K.shape[0])
-        if seq == 1:
-            self.ctx.reserve_for(spec, 1, 1)
+        self.ctx.reserve_for(spec, 1, seq)
         d = spec.desc()
         check(lib().aihost_attn_mha(self.ctx.handle, ctypes.byref(d), seq, K.shape[0], int(start_position), _ptr(Q),
                                     _ptr(K), _ptr(V), _ptr(out), _stream(self.stream)))
@@ -224,8 +223,7 @@ class ComputeOps:
         if out is None:
             odt = torch.float32 if spec.out_dtype == F32 else torch.float16
             out = torch.empty(B, S, spec.n_q_heads, spec.head_dim, dtype=odt, device=q.device)
-        if S == 1:
-            self.ctx.reserve_for(spec, B, 1)
+        self.ctx.reserve_for(spec, B, S)
         d = spec.desc()
         # host copy of the lengths (sizes the grid); None -> the library plans from kv_capacity
         hl = (ctypes.c_int32 * B)(*cache.host_len) if cache.host_len is not None else None

@@ -281,7 +281,7 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_head
     ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     kern = {name: ctx.profiler_read(k) for name, k in
             (("append", A.KERNEL_APPEND), ("decode", A.KERNEL_DECODE), ("combine", A.KERNEL_COMBINE),
-             ("prefill", A.KERNEL_PREFILL))}
+             ("prefill", A.KERNEL_PREFILL), ("convert", A.KERNEL_CONVERT))}
     ctx.sync_status()
     launches = sum(n for n, _ in kern.values())
 

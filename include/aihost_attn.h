@@ -94,7 +94,9 @@ const char* aihost_attn_last_error(void);
 aihost_status aihost_attn_create(int32_t device, aihost_attn_ctx** out_ctx);
 aihost_status aihost_attn_destroy(aihost_attn_ctx* ctx);
 
-/* Bytes of device scratch a forward call with these arguments needs (0 if none). */
+/* Bytes of device scratch a forward (or mha, with batch = 1 and n_new = n_q) call with these
+ * arguments needs (0 if none): split partials for decode; for prefill, fp16 copies of an fp32 q
+ * and of an fp32 / Q8_0 cache (kv_capacity rows), which the tensor-core kernel reads. */
 aihost_status aihost_attn_workspace_size(const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
                                          size_t* out_bytes);
 /* Grow the context's scratch to at least `bytes` (the only allocating call besides create). */
@@ -104,7 +106,8 @@ aihost_status aihost_attn_reserve(aihost_attn_ctx* ctx, size_t bytes);
  * and v_new into cache rows [seq_len[b], seq_len[b] + n_new), then attention of the n_new
  * query rows over cache rows [0, seq_len[b] + n_new) with the causal rule j <= seq_len[b] + i
  * (ComputeShaders.cs:545-561). n_new == 1 is decode (ComputeOps.cs:1069-1073, split-K kernel);
- * n_new > 1 is prefill (ComputeOps.cs:1076-1101, tcgen05 kernel).
+ * n_new > 1 is prefill (ComputeOps.cs:1076-1101, tcgen05 kernel; fp32 q and fp32 / Q8_0 caches
+ * are converted to fp16 in the context's scratch first, with fp32 accumulation throughout).
  *   seq_len     device int32[batch]: rows already cached per sequence (= start position).
  *   h_seq_len   optional host copy of seq_len (NULL allowed): only used to size the grid.
  * q, k_new, v_new are not modified (the reference rotates Q and K in place; here the rotated
@@ -145,7 +148,8 @@ typedef enum {
   AIHOST_KERNEL_DECODE = 1,   /* split-K decode */
   AIHOST_KERNEL_COMBINE = 2,  /* split merge */
   AIHOST_KERNEL_PREFILL = 3,  /* tcgen05 prefill */
-  AIHOST_KERNEL_COUNT = 4
+  AIHOST_KERNEL_CONVERT = 4,  /* fp16 staging of fp32 / Q8_0 prefill operands */
+  AIHOST_KERNEL_COUNT = 5
 } aihost_kernel;
 aihost_status aihost_attn_profiler_enable(aihost_attn_ctx* ctx, int32_t enable);
 aihost_status aihost_attn_profiler_read(aihost_attn_ctx* ctx, int32_t kernel, int64_t* launches, double* total_ms);

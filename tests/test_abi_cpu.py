@@ -55,7 +55,16 @@ def test_workspace_scales_with_capacity():
     small = _ws(LayerSpec(32, 8, 128, kv_capacity=1024), batch=4)[1]
     big = _ws(LayerSpec(32, 8, 128, kv_capacity=65536), batch=4)[1]
     assert big > small
-    assert _ws(LayerSpec(32, 8, 128, kv_capacity=1024), batch=4, n_new=16)[1] == 0  # prefill needs none
+    assert _ws(LayerSpec(32, 8, 128, kv_capacity=1024), batch=4, n_new=16)[1] == 0  # fp16 prefill needs none
+
+
+def test_workspace_covers_fp16_staging_of_fp32_and_q8_prefill():
+    """fp32 q -> fp16 copy of q; fp32 / Q8_0 cache -> fp16 copies of K and V (kv_capacity rows)."""
+    q_bytes = 4 * 16 * 32 * 128 * 2
+    kv_bytes = 2 * 4 * 1024 * 8 * 128 * 2
+    assert _ws(LayerSpec(32, 8, 128, kv_capacity=1024, q_dtype=A.F32, kv_dtype=A.F16), 4, 16)[1] == q_bytes
+    assert _ws(LayerSpec(32, 8, 128, kv_capacity=1024, q_dtype=A.F16, kv_dtype=A.Q8_0), 4, 16)[1] == kv_bytes
+    assert _ws(LayerSpec(32, 8, 128, kv_capacity=1024, q_dtype=A.F32, kv_dtype=A.F32), 4, 16)[1] == q_bytes + kv_bytes
 
 
 def test_null_context_and_pointers_rejected():

@@ -6,6 +6,8 @@ Tolerances (max |gpu - oracle| over every output element):
   fp16 inputs / fp16 cache:  2e-3   (the north-star bound for fp16 inputs)
   fp32 inputs / fp32 cache:  2e-4
   Q8_0 cache:                2e-3   (against the dequantise-then-attend oracle)
+  fp32 prefill:              1e-3   (the tensor-core prefill reads fp16 copies of fp32 operands
+                                     and rounds P to fp16; accumulation stays fp32)
 Appended cache rows: V rows are bit-exact (fp16 round-to-nearest-even, fp32 copy, Q8_0 bytes);
 K rows go through RoPE, whose cos/sin come from CUDA's sincosf on the GPU and glibc on the CPU
 (1-ulp differences), so they are compared within one unit of the stored format.
@@ -23,8 +25,15 @@ pytestmark = pytest.mark.gpu
 TOL = {F16: 2e-3, F32: 2e-4, Q8_0: 2e-3}
 
 
+TOL_F32_PREFILL = 1e-3
+
+
 def tol_for(cfg):
-    return TOL[Q8_0] if cfg.kv_dtype == Q8_0 else TOL[cfg.q_dtype]
+    if cfg.kv_dtype == Q8_0:
+        return TOL[Q8_0]
+    if cfg.n_new > 1 and (cfg.q_dtype == F32 or cfg.kv_dtype == F32):
+        return TOL_F32_PREFILL
+    return TOL[cfg.q_dtype]
 
 
 def check_call(ctx, cfg, pass_host_len=True, part=None, inp=None, check_cache=True):
@@ -145,6 +154,31 @@ def test_prefill_f32_out(ctx):
     check_call(ctx, cfg)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("cached", [[0], [100, 7]])
+def test_prefill_fp32_reference_dtypes(ctx, d, cached):
+    """The reference's own dtypes (fp32 q, cache and output) through prefill and chunked prefill."""
+    cfg = CONFIGS[1].scaled(batch=len(cached), n_new=150, head_dim=d, n_q_heads=8, n_kv_heads=2, cached=None,
+                            cached_list=cached)
+    check_call(ctx, cfg)
+
+
+@pytest.mark.parametrize("mode", [ROPE_INTERLEAVED, ROPE_NEOX])
+def test_prefill_fp32_rope_modes_without_host_lengths(ctx, mode):
+    cfg = CONFIGS[1].scaled(batch=2, n_new=130, n_q_heads=4, n_kv_heads=1, cached=None, cached_list=[0, 33],
+                            rope_mode=mode)
+    check_call(ctx, cfg, pass_host_len=False)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_q8_cache(ctx, d):
+    """Chunked prefill over a Q8_0 cache: the new rows are quantised into the cache and every row
+    is attended dequantised."""
+    cfg = CONFIGS[5].scaled(batch=2, n_new=140, n_q_heads=8, n_kv_heads=2, head_dim=d, cached=None,
+                            cached_list=[0, 300])
+    check_call(ctx, cfg)
+
+
 def test_prefill_stale_nan_rows_ignored(ctx):
     cfg = CONFIGS[2].scaled(n_new=100, n_q_heads=2, n_kv_heads=1, head_dim=128)
     inp = make_inputs(cfg, capacity=256)
@@ -170,6 +204,22 @@ def test_multi_head_attention_matches_reference_shapes(ctx):
         out = ops.multi_head_attention(q.cuda(), k.cuda(), v.cuda(), hq, P).cpu().float().numpy()
         ref = orc.mha(q.float().numpy(), k.float().numpy(), v.float().numpy(), hq, P)
         assert max_abs(out, ref) <= 2e-3
+
+
+def test_multi_head_attention_fp32_prefill(ctx):
+    """MultiHeadAttention with the reference's fp32 tensors (S > 1 goes through fp16 staging)."""
+    from aihost_b200 import gen
+    from aihost_b200.ops import ComputeOps
+    from oracle import oracle as orc
+
+    ops = ComputeOps(ctx)
+    for S, Lk, P, hq, hkv, d in [(96, 96, 0, 8, 2, 64), (64, 200, 136, 4, 4, 128)]:
+        q = gen.normal((S, hq * d), 8, "fq", std=0.5)
+        k = gen.normal((Lk, hkv * d), 8, "fk", std=0.5)
+        v = gen.normal((Lk, hkv * d), 8, "fv", std=0.5)
+        out = ops.multi_head_attention(q.cuda(), k.cuda(), v.cuda(), hq, P).cpu().numpy()
+        ref = orc.mha(q.numpy(), k.numpy(), v.numpy(), hq, P)
+        assert max_abs(out, ref) <= TOL_F32_PREFILL
 
 
 def test_fused_mha_generate_fp32(ctx):

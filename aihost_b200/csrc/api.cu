@@ -370,6 +370,7 @@ aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const
   a.out = out;
   a.out_dtype = d->out_dtype;
   a.status = ctx->d_status;
+  a.split_kv = prefill_split_kv(batch, n_q, d->n_q_heads, ctx->num_sms) ? 1 : 0;
   cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_PREFILL, st, [&] { return launch_prefill(a, st); });
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return AIHOST_OK;
@@ -405,7 +406,6 @@ cudaError_t launch_decode_any(const DecodeArgs& a, cudaStream_t st, aihost_attn_
     char saved[sizeof(g_err)];
     memcpy(saved, g_err, sizeof(g_err));
     const uint32_t bw = q8_box_words(a.head_dim, a.kv.head_stride);
-    m.q8_row_bytes = static_cast<int32_t>(bw * 4);
     if (bw && encode_q8_map(&m.k_map, a.k_cache, a.kv, a.batch, bw) == AIHOST_OK &&
         encode_q8_map(&m.v_map, a.v_cache, a.kv, a.batch, bw) == AIHOST_OK) {
       e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode_mma(m, st); });

@@ -1,10 +1,12 @@
-// decode_mma.cu — split-K flash decoding for fp16 caches on the tensor cores.
+// decode_mma.cu — split-K flash decoding for fp16 and GGUF Q8_0 caches on the tensor cores.
 //
-// Replaces FusedMHAGenerate (ComputeShaders.cs:656-733) for fp16 KV caches. One CTA handles one
-// (sequence, KV head, group of up to 16 Q heads, split of `chunk` cache rows):
-//   warp 4      TMA producer: K and V tiles of 64 rows (128-byte swizzled, no multicast) into a
-//               multi-stage shared-memory ring, completion on mbarriers;
-//   warps 0-3   each takes 16 rows of every tile: S = Q K^T with m16n8k16 MMAs (the group's Q
+// Replaces FusedMHAGenerate (ComputeShaders.cs:656-733) for fp16 / Q8_0 KV caches. One CTA handles
+// one (sequence, KV head, group of up to 16 Q heads, split of `chunk` cache rows):
+//   producer    TMA: K and V tiles of 64 rows into a multi-stage shared-memory ring (no
+//               multicast), completion on mbarriers. fp16 caches land as 128-byte swizzled fp16
+//               tiles; Q8_0 caches land as raw 34-byte blocks, which four converter warps turn
+//               into the same swizzled fp16 tiles (one cache row per thread);
+//   warps 0-3   each takes 16 rows of every fp16 tile: S = Q K^T with m16n8k16 MMAs (the group's Q
 //               heads are the 16 MMA rows, rotated by RoPE once per CTA and kept as A fragments
 //               in registers), online softmax in the exp2 domain with quad-shuffle row
 //               reductions, O += P V with P re-used from the S accumulators as A fragments;
@@ -72,95 +74,20 @@ struct DecBars {
   uint64_t full[6], empty[6];
 };
 
-template <int D>
-__global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_constant__ DecodeMmaArgs a) {
-  using C = DecodeCfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  DecBars& bar = *reinterpret_cast<DecBars*>(smem + C::BAR_OFF);
-  __half* q_s = reinterpret_cast<__half*>(smem + C::Q_OFF);
-  const uint32_t k_base = smem_u32(smem + C::K_OFF), v_base = smem_u32(smem + C::V_OFF);
-
+// Compute-warp half of both kernels (warps 0-3): streams the fp16 K/V tiles of ring `full` /
+// `empty` (NS stages of TILE_BYTES each at k_off / v_off), keeps (max, sum, O) per query row in
+// registers, then merges the four warps through `merge` and writes the output or the split's
+// partials. ZERO_V: rows past the split's end arrive as stale cache bytes and are zeroed here.
+template <int D, int NS, bool ZERO_V>
+__device__ __forceinline__ void decode_compute(const DecodeArgs& p, uint8_t* smem, int k_off, int v_off,
+                                               uint64_t* full, uint64_t* empty, const __half* q_s, float* merge,
+                                               int n, int n_tiles, int h0, int g_count, int b, int split,
+                                               int n_splits) {
+  constexpr int KB = D / 64;
+  constexpr int TILE_BYTES = KB * kTileRows * 128;
+  constexpr int QROW = D + 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const DecodeArgs& p = a.base;
-  const int split = blockIdx.x;
-  const int G = p.n_q_heads / p.n_kv_heads;
-  const int n_sub = (G + 15) / 16;
-  const int kvh = blockIdx.y / n_sub, sub = blockIdx.y % n_sub;
-  const int b = blockIdx.z;
-  const int g_count = min(16, G - sub * 16);
-  const int h0 = kvh * G + sub * 16;
-  const int32_t start = p.seq_len ? p.seq_len[b] : p.start_scalar;
-  const int32_t Lk = start + p.len_offset;
-  if (Lk > p.kv.capacity || Lk < 1) {
-    if (threadIdx.x == 0 && split == 0 && blockIdx.y == 0) atomicOr(p.status, kStatusBadLength);
-    return;
-  }
-  const int32_t t0 = split * p.chunk;
-  if (t0 >= Lk) return;
-  const int32_t n = min(p.chunk, Lk - t0);
-  const int n_tiles = (n + kTileRows - 1) / kTileRows;
-  const int n_splits = (Lk + p.chunk - 1) / p.chunk;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < C::NS; ++i) {
-      mbar_init(&bar.full[i], 1);
-      mbar_init(&bar.empty[i], kComputeWarps);
-    }
-    fence_mbar_init();
-  }
-  // Q rows of the group, rotated at the new token's position, as fp16 (rows >= g_count zero)
-  const float pos = static_cast<float>(start + p.rope_pos_offset);
-  for (int idx = threadIdx.x; idx < 16 * (D / 2); idx += kThreads) {
-    const int g = idx / (D / 2), pair = idx % (D / 2);
-    const int i1 = p.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
-    const int i2 = p.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
-    float x1 = 0.0f, x2 = 0.0f;
-    if (g < g_count) {
-      const int64_t qoff = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D;
-      if (p.q_dtype == AIHOST_F32) {
-        x1 = static_cast<const float*>(p.q)[qoff + i1];
-        x2 = static_cast<const float*>(p.q)[qoff + i2];
-      } else {
-        x1 = __half2float(static_cast<const __half*>(p.q)[qoff + i1]);
-        x2 = __half2float(static_cast<const __half*>(p.q)[qoff + i2]);
-      }
-      if (p.rope_mode != AIHOST_ROPE_NONE) {
-        float sn, cs;
-        sincosf(__fmul_rn(pos, p.freqs.f[pair]), &sn, &cs);
-        const float r1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
-        const float r2 = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
-        x1 = r1;
-        x2 = r2;
-      }
-    }
-    q_s[g * C::QROW + i1] = __float2half_rn(x1);
-    q_s[g * C::QROW + i2] = __float2half_rn(x2);
-  }
-  __syncthreads();
-
-  if (warp == kComputeWarps) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      tma_prefetch_desc(&a.k_map);
-      tma_prefetch_desc(&a.v_map);
-      for (int i = 0; i < n_tiles; ++i) {
-        const int s = i % C::NS;
-        if (!mbar_wait(&bar.empty[s], ((i / C::NS) & 1) ^ 1, p.status)) break;
-        mbar_arrive_expect_tx(&bar.full[s], 2 * C::TILE_BYTES);
-        const int row = t0 + i * kTileRows;
-        for (int kb = 0; kb < C::KB; ++kb) {
-          tma_load_4d(smem + C::K_OFF + s * C::TILE_BYTES + kb * kTileRows * 128, &a.k_map, &bar.full[s], kb * 64,
-                      kvh, row, b);
-          tma_load_4d(smem + C::V_OFF + s * C::TILE_BYTES + kb * kTileRows * 128, &a.v_map, &bar.full[s], kb * 64,
-                      kvh, row, b);
-        }
-      }
-    }
-    return;
-  }
-
-  // ------------------------------------------------------------------ compute warps
+  const uint32_t k_base = smem_u32(smem + k_off), v_base = smem_u32(smem + v_off);
   const int grp = lane >> 2, tig = lane & 3;
   // Q as A fragments: k-step kk covers dims [16kk, 16kk + 16)
   uint32_t qa[D / 16][4];
@@ -169,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
     const int mi = lane >> 3, r = lane & 7;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk)
-      ldsm_x4(qb + ((r + 8 * (mi & 1)) * C::QROW + kk * 16 + 8 * (mi >> 1)) * 2, qa[kk][0], qa[kk][1], qa[kk][2],
+      ldsm_x4(qb + ((r + 8 * (mi & 1)) * QROW + kk * 16 + 8 * (mi >> 1)) * 2, qa[kk][0], qa[kk][1], qa[kk][2],
               qa[kk][3]);
   }
   const float sl2 = p.scale * kLog2e;
@@ -180,9 +107,9 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
 
   bool ok = true;
   for (int i = 0; i < n_tiles && ok; ++i) {
-    const int s = i % C::NS;
-    if (!mbar_wait(&bar.full[s], (i / C::NS) & 1, p.status)) { ok = false; break; }
-    const uint32_t kt = k_base + s * C::TILE_BYTES, vt = v_base + s * C::TILE_BYTES;
+    const int s = i % NS;
+    if (!mbar_wait(&full[s], (i / NS) & 1, p.status)) { ok = false; break; }
+    const uint32_t kt = k_base + s * TILE_BYTES, vt = v_base + s * TILE_BYTES;
     const int r0 = warp * 16;  // this warp's 16 rows of the tile
     // ---- S = Q K^T for the warp's rows: two n8 blocks
     float sacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
@@ -243,10 +170,10 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
     const uint32_t pa2 = pack_h2(pv[1][0], pv[1][1]), pa3 = pack_h2(pv[1][2], pv[1][3]);
     // ---- rows past the split's end may hold stale bits (NaN patterns included); P is 0 there,
     // but 0 * NaN is NaN, so the warp zeroes its own V rows beyond n before reading them
-    if (base_row + 16 > n) {
-      uint8_t* vrow0 = smem + C::V_OFF + s * C::TILE_BYTES;
-      for (int c = lane; c < 16 * C::KB * 8; c += 32) {
-        const int rr = c / (C::KB * 8), ch = c % (C::KB * 8);
+    if (ZERO_V && base_row + 16 > n) {
+      uint8_t* vrow0 = smem + v_off + s * TILE_BYTES;
+      for (int c = lane; c < 16 * KB * 8; c += 32) {
+        const int rr = c / (KB * 8), ch = c % (KB * 8);
         if (base_row + rr >= n)
           *reinterpret_cast<uint4*>(vrow0 + (ch >> 3) * (kTileRows * 128) + (r0 + rr) * 128 + (ch & 7) * 16) =
               make_uint4(0, 0, 0, 0);
@@ -265,8 +192,8 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
       }
     }
     __syncwarp();
-    if (base_row + 16 > n) fence_proxy_async_smem();  // zeroed rows are rewritten by TMA later
-    if (lane == 0) mbar_arrive(&bar.empty[s]);
+    if (ZERO_V && base_row + 16 > n) fence_proxy_async_smem();  // zeroed rows are rewritten by TMA later
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
 
   // ---- merge the four warps: row sums over the quad, then through shared memory
@@ -275,10 +202,10 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
     l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
     l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
   }
-  // all tiles consumed: the K ring is reused for the merge (no TMA can target it any more)
+  // all tiles consumed: `merge` reuses ring memory no producer can target any more
   asm volatile("bar.sync 1, 128;" ::: "memory");
-  float* ml_s = reinterpret_cast<float*>(smem + C::K_OFF);      // [4 warps][16 rows][2]
-  float* o_s = ml_s + kComputeWarps * 16 * 2;                     // [4 warps][16 rows][D]
+  float* ml_s = merge;                           // [4 warps][16 rows][2]
+  float* o_s = ml_s + kComputeWarps * 16 * 2;    // [4 warps][16 rows][D]
   if (tig == 0) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -323,51 +250,44 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
   }
 }
 
-// ------------------------------------------------------------------ GGUF Q8_0 caches
-// Eight compute warps: warps w and w + 4 take the same 16 rows of each tile (both compute the
-// scores, which are cheap) and each accumulates half of the output columns, which halves the
-// accumulator registers and doubles the warps available to hide shared-memory latency.
-constexpr int kQ8ComputeWarps = 8;
-constexpr int kQ8Threads = (kQ8ComputeWarps + 1) * 32;
-// Tiles hold raw 34-byte blocks: each cache row's head slice is read by TMA as a box of 32-bit
-// words that starts at the 16-byte boundary at or below the slice (GGUF blocks are only 2-byte
-// aligned); the slice then begins `off` bytes into every tile row. The box is as narrow as the
-// head offsets allow: with the default 136-byte heads (d = 128) it is 144 bytes, an odd number
-// of 16-byte units, which keeps the row-strided shared loads below free of bank conflicts.
+// Q rows of the group, rotated at the new token's position, as fp16 rows of QROW elements
+// (rows >= g_count zero). All `nthreads` threads of the CTA take part.
 template <int D>
-struct Q8Cfg {
-  static constexpr int NB = D / 32;                   // blocks per head row
-  static constexpr int HEAD_WORDS = NB * 34 / 4;      // 17 (D=64) or 34 (D=128) words
-  // box: the head slice plus up to 2 (d = 128) or 3 (d = 64) words of start offset, which
-  // covers every head of the default GGUF layout (136- / 68-byte heads). 36 and 20 words are odd
-  // multiples of 16 bytes, so row-strided shared loads hit distinct banks.
-  static constexpr int BOX_WORDS = (HEAD_WORDS + 2 + 3) / 4 * 4;
-  static constexpr int ROW_BYTES = BOX_WORDS * 4;
-  static constexpr int TILE_BYTES = kTileRows * ROW_BYTES;
-  static constexpr int NS = 4;
-  static constexpr int QROW = D + 8;
-  static constexpr int K_OFF = 0;
-  static constexpr int V_OFF = NS * TILE_BYTES;
-  static constexpr int Q_OFF = (2 * NS * TILE_BYTES + 1023) / 1024 * 1024;
-  static constexpr int Q_BYTES = 16 * QROW * 2;
-  static constexpr int MERGE_BYTES = kComputeWarps * 16 * (D + 2) * 4;
-  static constexpr int BAR_OFF = Q_OFF + Q_BYTES;
-  static constexpr int SMEM = BAR_OFF + 128 + 1024;
-  static_assert(2 * NS * TILE_BYTES >= MERGE_BYTES, "merge buffer reuses the K/V rings");
-};
-
-// Two int8 values (low byte = first) to an exact fp16 pair: 0x64xx is 1024 + xx in fp16, so
-// (1024 + (b ^ 0x80)) - 1152 = signed b.
-__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t w) {
-  const uint32_t x = __byte_perm(w ^ 0x8080u, 0x64646464u, 0x4140);
-  __half2 h = *reinterpret_cast<const __half2*>(&x);
-  h = __hsub2(h, __floats2half2_rn(1152.0f, 1152.0f));
-  return *reinterpret_cast<const uint32_t*>(&h);
+__device__ __forceinline__ void load_q_rows(const DecodeArgs& p, __half* q_s, int b, int h0, int g_count,
+                                            int32_t start, int nthreads) {
+  constexpr int QROW = D + 8;
+  const float pos = static_cast<float>(start + p.rope_pos_offset);
+  for (int idx = threadIdx.x; idx < 16 * (D / 2); idx += nthreads) {
+    const int g = idx / (D / 2), pair = idx % (D / 2);
+    const int i1 = p.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
+    const int i2 = p.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
+    float x1 = 0.0f, x2 = 0.0f;
+    if (g < g_count) {
+      const int64_t qoff = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D;
+      if (p.q_dtype == AIHOST_F32) {
+        x1 = static_cast<const float*>(p.q)[qoff + i1];
+        x2 = static_cast<const float*>(p.q)[qoff + i2];
+      } else {
+        x1 = __half2float(static_cast<const __half*>(p.q)[qoff + i1]);
+        x2 = __half2float(static_cast<const __half*>(p.q)[qoff + i2]);
+      }
+      if (p.rope_mode != AIHOST_ROPE_NONE) {
+        float sn, cs;
+        sincosf(__fmul_rn(pos, p.freqs.f[pair]), &sn, &cs);
+        const float r1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+        const float r2 = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
+        x1 = r1;
+        x2 = r2;
+      }
+    }
+    q_s[g * QROW + i1] = __float2half_rn(x1);
+    q_s[g * QROW + i2] = __float2half_rn(x2);
+  }
 }
 
 template <int D>
-__global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_constant__ DecodeMmaArgs a) {
-  using C = Q8Cfg<D>;
+__global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_constant__ DecodeMmaArgs a) {
+  using C = DecodeCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   DecBars& bar = *reinterpret_cast<DecBars*>(smem + C::BAR_OFF);
@@ -393,249 +313,233 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
   const int32_t n = min(p.chunk, Lk - t0);
   const int n_tiles = (n + kTileRows - 1) / kTileRows;
   const int n_splits = (Lk + p.chunk - 1) / p.chunk;
-  const int head_word = static_cast<int>(kvh * (p.kv.head_stride / 4));
-  const int box_x = head_word & ~3;
-  const int off = (head_word - box_x) * 4;  // byte offset of the head slice in a tile row
-  constexpr int ROW = C::ROW_BYTES;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NS; ++i) {
       mbar_init(&bar.full[i], 1);
-      mbar_init(&bar.empty[i], kQ8ComputeWarps);
+      mbar_init(&bar.empty[i], kComputeWarps);
     }
     fence_mbar_init();
   }
-  const float pos = static_cast<float>(start + p.rope_pos_offset);
-  for (int idx = threadIdx.x; idx < 16 * (D / 2); idx += kQ8Threads) {
-    const int g = idx / (D / 2), pair = idx % (D / 2);
-    const int i1 = p.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
-    const int i2 = p.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
-    float x1 = 0.0f, x2 = 0.0f;
-    if (g < g_count) {
-      const int64_t qoff = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D;
-      if (p.q_dtype == AIHOST_F32) {
-        x1 = static_cast<const float*>(p.q)[qoff + i1];
-        x2 = static_cast<const float*>(p.q)[qoff + i2];
-      } else {
-        x1 = __half2float(static_cast<const __half*>(p.q)[qoff + i1]);
-        x2 = __half2float(static_cast<const __half*>(p.q)[qoff + i2]);
-      }
-      if (p.rope_mode != AIHOST_ROPE_NONE) {
-        float sn, cs;
-        sincosf(__fmul_rn(pos, p.freqs.f[pair]), &sn, &cs);
-        const float r1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
-        const float r2 = __fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs));
-        x1 = r1;
-        x2 = r2;
-      }
-    }
-    q_s[g * C::QROW + i1] = __float2half_rn(x1);
-    q_s[g * C::QROW + i2] = __float2half_rn(x2);
-  }
+  load_q_rows<D>(p, q_s, b, h0, g_count, start, kThreads);
   __syncthreads();
 
-  if (warp == kQ8ComputeWarps) {
+  if (warp == kComputeWarps) {
+    // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&a.k_map);
       tma_prefetch_desc(&a.v_map);
       for (int i = 0; i < n_tiles; ++i) {
         const int s = i % C::NS;
         if (!mbar_wait(&bar.empty[s], ((i / C::NS) & 1) ^ 1, p.status)) break;
-        mbar_arrive_expect_tx(&bar.full[s], 2 * kTileRows * ROW);  // bytes the two boxes deliver
+        mbar_arrive_expect_tx(&bar.full[s], 2 * C::TILE_BYTES);
         const int row = t0 + i * kTileRows;
-        tma_load_4d(smem + C::K_OFF + s * C::TILE_BYTES, &a.k_map, &bar.full[s], box_x, row, b, 0);
-        tma_load_4d(smem + C::V_OFF + s * C::TILE_BYTES, &a.v_map, &bar.full[s], box_x, row, b, 0);
+        for (int kb = 0; kb < C::KB; ++kb) {
+          tma_load_4d(smem + C::K_OFF + s * C::TILE_BYTES + kb * kTileRows * 128, &a.k_map, &bar.full[s], kb * 64,
+                      kvh, row, b);
+          tma_load_4d(smem + C::V_OFF + s * C::TILE_BYTES + kb * kTileRows * 128, &a.v_map, &bar.full[s], kb * 64,
+                      kvh, row, b);
+        }
       }
     }
     return;
   }
+  decode_compute<D, C::NS, true>(p, smem, C::K_OFF, C::V_OFF, bar.full, bar.empty, q_s,
+                                 reinterpret_cast<float*>(smem + C::K_OFF), n, n_tiles, h0, g_count, b, split,
+                                 n_splits);
+}
 
-  const int grp = lane >> 2, tig = lane & 3;
-  uint32_t qa[D / 16][4];
-  {
-    const uint32_t qb = smem_u32(q_s);
-    const int mi = lane >> 3, r = lane & 7;
+// ------------------------------------------------------------------ GGUF Q8_0 caches
+// Warps 0-3 compute (as above), warps 4-7 convert; the first converter thread also issues the
+// TMA loads (256 threads, so two CTAs per SM keep 128 registers per thread).
+// TMA reads each cache row's head slice as a box of 32-bit words that starts at the 16-byte
+// boundary at or below the slice (GGUF blocks are only 2-byte aligned); the slice then begins
+// `off` bytes into every raw tile row. The box is as narrow as the head offsets allow: with the
+// default 136-byte heads (d = 128) it is 144 bytes (68-byte heads, d = 64: 80 bytes), an odd
+// number of 16-byte units, so a quarter-warp reading 16 bytes from each of 8 consecutive rows
+// touches 8 distinct bank groups.
+// A converter thread owns one row of the K or V tile: it reads the raw row with 16-byte loads,
+// realigns the 2-byte-aligned blocks with byte permutes, turns each int8 exactly into fp16
+// (exponent 0x64 over q + 128, minus 1152), multiplies by the block's fp16 scale (one rounding:
+// fp16(d * q), the value an fp32 dequantise-then-round gives) and stores the row swizzled, so
+// the compute warps read the same fp16 tiles as for an fp16 cache. Rows past the split's end are
+// written as zeros.
+constexpr int kQ8ConvWarps = 4;
+constexpr int kQ8Threads = (kComputeWarps + kQ8ConvWarps) * 32;
+
+template <int D>
+struct Q8Cfg {
+  static constexpr int NB = D / 32;                   // blocks per head row
+  static constexpr int HEAD_WORDS = NB * 34 / 4;      // 17 (D=64) or 34 (D=128) words
+  // box: the head slice plus up to 2 (d = 128) or 3 (d = 64) words of start offset, which
+  // covers every head of the default GGUF layout (136- / 68-byte heads).
+  static constexpr int BOX_WORDS = (HEAD_WORDS + 2 + 3) / 4 * 4;
+  static constexpr int ROW_BYTES = BOX_WORDS * 4;
+  static constexpr int RAW_TILE = kTileRows * ROW_BYTES;   // one raw K or V tile
+  static constexpr int F_TILE = (D / 64) * kTileRows * 128;  // one fp16 K or V tile
+  static constexpr int NSR = D == 64 ? 4 : 2;              // raw ring depth
+  static constexpr int NSF = D == 64 ? 4 : 2;              // fp16 ring depth
+  static constexpr int QROW = D + 8;
+  static constexpr int RAW_OFF = 0;                        // K raw [NSR], then V raw [NSR]
+  static constexpr int F_OFF = (2 * NSR * RAW_TILE + 1023) / 1024 * 1024;  // K fp16 [NSF], V fp16
+  static constexpr int Q_OFF = F_OFF + 2 * NSF * F_TILE;
+  static constexpr int Q_BYTES = 16 * QROW * 2;
+  static constexpr int BAR_OFF = Q_OFF + Q_BYTES;
+  static constexpr int SMEM = BAR_OFF + 128 + 1024;
+  static constexpr int MERGE_BYTES = kComputeWarps * 16 * (D + 2) * 4;
+  static_assert(2 * NSF * F_TILE >= MERGE_BYTES, "merge buffer reuses the fp16 rings");
+  static_assert(NSR <= 4 && NSF <= 4, "barrier arrays hold four stages");
+};
+
+struct Q8Bars {
+  uint64_t raw_full[4], raw_empty[4], f_full[4], f_empty[4];
+};
+
+// Converts one raw row (words w, head slice starting OFFW words in) into 16-byte fp16 chunks
+// of the swizzled tile row `row` at `tile`.
+template <int D, int OFFW>
+__device__ __forceinline__ void q8_row_to_f16(const uint32_t (&w)[Q8Cfg<D>::BOX_WORDS], uint8_t* tile, int row) {
+  const __half2 k1152 = __floats2half2_rn(1152.0f, 1152.0f);
 #pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk)
-      ldsm_x4(qb + ((r + 8 * (mi & 1)) * C::QROW + kk * 16 + 8 * (mi >> 1)) * 2, qa[kk][0], qa[kk][1], qa[kk][2],
-              qa[kk][3]);
+  for (int blk = 0; blk < D / 32; ++blk) {
+    constexpr int kOff = 4 * OFFW;
+    const int b0 = kOff + 34 * blk;  // byte offset of the block's scale (even)
+    const uint32_t sw = w[b0 >> 2] >> ((b0 & 3) * 8);
+    const __half2 d2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(sw & 0xffffu)));
+    uint32_t hv[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int qb = b0 + 2 + 4 * j;  // bytes of dims 4j..4j+3 of the block
+      // (the clamp only keeps the index of the unused operand inside the array)
+      const int hi = (qb >> 2) + 1 < Q8Cfg<D>::BOX_WORDS ? (qb >> 2) + 1 : (qb >> 2);
+      const uint32_t q = (qb & 3) == 0 ? w[qb >> 2] : __byte_perm(w[qb >> 2], w[hi], 0x5432);
+      const uint32_t x = q ^ 0x80808080u;
+      const uint32_t e01 = __byte_perm(x, 0x64646464u, 0x4140);
+      const uint32_t e23 = __byte_perm(x, 0x64646464u, 0x4342);
+      const __half2 h01 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&e01), k1152), d2);
+      const __half2 h23 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&e23), k1152), d2);
+      hv[2 * j] = *reinterpret_cast<const uint32_t*>(&h01);
+      hv[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int col = blk * 32 + 8 * c;
+      uint8_t* dst = tile + (col >> 6) * (kTileRows * 128) + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4);
+      *reinterpret_cast<uint4*>(dst) = make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
+    }
   }
-  const float sl2 = p.scale * kLog2e;
-  float m_run[2] = {-1e30f, -1e30f}, l_run[2] = {0.0f, 0.0f};
-  constexpr int NBH = D / 16;  // n8 blocks of output columns per warp (half of D)
-  float o[NBH][4];
-#pragma unroll
-  for (int nb = 0; nb < NBH; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
+}
 
-  bool ok = true;
-  for (int i = 0; i < n_tiles && ok; ++i) {
-    const int s = i % C::NS;
-    if (!mbar_wait(&bar.full[s], (i / C::NS) & 1, p.status)) { ok = false; break; }
-    const uint8_t* kt = smem + C::K_OFF + s * C::TILE_BYTES + off;
-    uint8_t* vt = smem + C::V_OFF + s * C::TILE_BYTES + off;
-    const int r0 = (warp & 3) * 16;  // rows of the tile (shared by warps w and w + 4)
-    const int dh = warp >> 2;         // half of the output columns this warp accumulates
-    const int base_row = i * kTileRows + r0;
-    // rows past the split's end may hold stale bytes (their fp16 scales may be NaN): the
-    // row-group's first warp zeroes them (named barrier per row group before anyone reads)
-    if (base_row + 16 > n && dh == 0) {
-      for (int c = lane; c < 16 * C::NB; c += 32) {
-        const int rr = c / C::NB, blk = c % C::NB;
-        if (base_row + rr >= n) {
-          *reinterpret_cast<uint16_t*>(vt + (r0 + rr) * ROW + blk * 34) = 0;
-          *reinterpret_cast<uint16_t*>(const_cast<uint8_t*>(kt) + (r0 + rr) * ROW + blk * 34) = 0;
+template <int D>
+__global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_constant__ DecodeMmaArgs a) {
+  using C = Q8Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Q8Bars& bar = *reinterpret_cast<Q8Bars*>(smem + C::BAR_OFF);
+  __half* q_s = reinterpret_cast<__half*>(smem + C::Q_OFF);
+
+  const int warp = threadIdx.x >> 5;
+  const DecodeArgs& p = a.base;
+  const int split = blockIdx.x;
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int n_sub = (G + 15) / 16;
+  const int kvh = blockIdx.y / n_sub, sub = blockIdx.y % n_sub;
+  const int b = blockIdx.z;
+  const int g_count = min(16, G - sub * 16);
+  const int h0 = kvh * G + sub * 16;
+  const int32_t start = p.seq_len ? p.seq_len[b] : p.start_scalar;
+  const int32_t Lk = start + p.len_offset;
+  if (Lk > p.kv.capacity || Lk < 1) {
+    if (threadIdx.x == 0 && split == 0 && blockIdx.y == 0) atomicOr(p.status, kStatusBadLength);
+    return;
+  }
+  const int32_t t0 = split * p.chunk;
+  if (t0 >= Lk) return;
+  const int32_t n = min(p.chunk, Lk - t0);
+  const int n_tiles = (n + kTileRows - 1) / kTileRows;
+  const int n_splits = (Lk + p.chunk - 1) / p.chunk;
+  const int head_word = static_cast<int>(kvh * (p.kv.head_stride / 4));
+  const int box_x = head_word & ~3;
+  const int off_words = head_word - box_x;  // the head slice starts this many words into a row
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NSR; ++i) {
+      mbar_init(&bar.raw_full[i], 1);
+      mbar_init(&bar.raw_empty[i], kQ8ConvWarps * 32);
+    }
+    for (int i = 0; i < C::NSF; ++i) {
+      mbar_init(&bar.f_full[i], kQ8ConvWarps * 32);
+      mbar_init(&bar.f_empty[i], kComputeWarps);
+    }
+    fence_mbar_init();
+  }
+  load_q_rows<D>(p, q_s, b, h0, g_count, start, kQ8Threads);
+  __syncthreads();
+
+  if (warp >= kComputeWarps) {
+    // ------------------------------------------------------------------ converters
+    const int ct = threadIdx.x - kComputeWarps * 32;  // 0..127: K rows 0-63, V rows 0-63
+    const int is_v = ct >> 6, row = ct & 63;
+    const bool issuer = ct == 0;
+    // TMA of tile i into raw slot i % NSR, once every converter has read the slot's last tile
+    auto issue = [&](int i) -> bool {
+      const int s = i % C::NSR;
+      if (!mbar_wait(&bar.raw_empty[s], ((i / C::NSR) & 1) ^ 1, p.status)) return false;
+      mbar_arrive_expect_tx(&bar.raw_full[s], 2 * C::RAW_TILE);  // bytes the two boxes deliver
+      const int r = t0 + i * kTileRows;
+      tma_load_4d(smem + C::RAW_OFF + s * C::RAW_TILE, &a.k_map, &bar.raw_full[s], box_x, r, b, 0);
+      tma_load_4d(smem + C::RAW_OFF + (C::NSR + s) * C::RAW_TILE, &a.v_map, &bar.raw_full[s], box_x, r, b, 0);
+      return true;
+    };
+    bool feed = issuer;
+    if (issuer) {
+      tma_prefetch_desc(&a.k_map);
+      tma_prefetch_desc(&a.v_map);
+      for (int i = 0; feed && i < C::NSR && i < n_tiles; ++i) feed = issue(i);
+    }
+    for (int i = 0; i < n_tiles; ++i) {
+      const int sr = i % C::NSR, sf = i % C::NSF;
+      if (!mbar_wait(&bar.raw_full[sr], (i / C::NSR) & 1, p.status)) break;
+      uint32_t w[C::BOX_WORDS];
+      const uint4* src =
+          reinterpret_cast<const uint4*>(smem + C::RAW_OFF + (is_v * C::NSR + sr) * C::RAW_TILE + row * C::ROW_BYTES);
+#pragma unroll
+      for (int c = 0; c < C::BOX_WORDS / 4; ++c) {
+        const uint4 v = src[c];
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+      mbar_arrive(&bar.raw_empty[sr]);
+      if (feed && i + C::NSR < n_tiles) feed = issue(i + C::NSR);
+      if (!mbar_wait(&bar.f_empty[sf], ((i / C::NSF) & 1) ^ 1, p.status)) break;
+      uint8_t* tile = smem + C::F_OFF + (is_v * C::NSF + sf) * C::F_TILE;
+      if (i * kTileRows + row < n) {
+        if constexpr (D == 128) {
+          if (off_words == 0) q8_row_to_f16<D, 0>(w, tile, row);
+          else q8_row_to_f16<D, 2>(w, tile, row);
+        } else {
+          switch (off_words) {
+            case 0: q8_row_to_f16<D, 0>(w, tile, row); break;
+            case 1: q8_row_to_f16<D, 1>(w, tile, row); break;
+            case 2: q8_row_to_f16<D, 2>(w, tile, row); break;
+            default: q8_row_to_f16<D, 3>(w, tile, row); break;
+          }
         }
+      } else {
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c)
+          *reinterpret_cast<uint4*>(tile + (c >> 3) * (kTileRows * 128) + row * 128 + (((c & 7) ^ (row & 7)) << 4)) =
+              make_uint4(0, 0, 0, 0);
       }
+      mbar_arrive(&bar.f_full[sf]);
     }
-    if (base_row + 16 > n) asm volatile("bar.sync %0, 64;" ::"r"(2 + (warp & 3)) : "memory");
-    // ---- S = Q K^T per 32-column block (integer K values are exact in fp16), then the block
-    // scales of each row: S = sum_blk d_blk * S_blk
-    float sacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-#pragma unroll
-    for (int blk = 0; blk < C::NB; ++blk) {
-      float sb[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-#pragma unroll
-      for (int nb = 0; nb < 2; ++nb) {
-        const uint8_t* krow = kt + (r0 + nb * 8 + grp) * ROW + blk * 34 + 2;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {  // the block's two 16-column k-steps
-          const int kk = blk * 2 + h;
-          const uint32_t b0 = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(krow + h * 16 + 2 * tig));
-          const uint32_t b1 = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(krow + h * 16 + 8 + 2 * tig));
-          mma16816(sb[nb], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
-        }
-      }
-#pragma unroll
-      for (int nb = 0; nb < 2; ++nb) {
-        const int row = r0 + nb * 8 + 2 * tig;
-        const float d0 = __half2float(*reinterpret_cast<const __half*>(kt + row * ROW + blk * 34));
-        const float d1 = __half2float(*reinterpret_cast<const __half*>(kt + (row + 1) * ROW + blk * 34));
-        sacc[nb][0] = fmaf(d0, sb[nb][0], sacc[nb][0]);
-        sacc[nb][1] = fmaf(d1, sb[nb][1], sacc[nb][1]);
-        sacc[nb][2] = fmaf(d0, sb[nb][2], sacc[nb][2]);
-        sacc[nb][3] = fmaf(d1, sb[nb][3], sacc[nb][3]);
-      }
-    }
-    float mt[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nb = 0; nb < 2; ++nb)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int row = base_row + nb * 8 + 2 * tig + (e & 1);
-        float v = sacc[nb][e] * sl2;
-        v = row < n ? v : -INFINITY;
-        sacc[nb][e] = v;
-        mt[e >> 1] = fmaxf(mt[e >> 1], v);
-      }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 1));
-      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 2));
-    }
-    float f[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float m_new = fmaxf(m_run[h], mt[h]);
-      f[h] = ex2_approx(m_run[h] - m_new);
-      m_run[h] = m_new;
-      l_run[h] *= f[h];
-    }
-#pragma unroll
-    for (int nb = 0; nb < NBH; ++nb) {
-      o[nb][0] *= f[0];
-      o[nb][1] *= f[0];
-      o[nb][2] *= f[1];
-      o[nb][3] *= f[1];
-    }
-    float pv[2][4];
-#pragma unroll
-    for (int nb = 0; nb < 2; ++nb)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        pv[nb][e] = ex2_approx(sacc[nb][e] - m_run[e >> 1]);
-        l_run[e >> 1] += pv[nb][e];
-      }
-    // ---- O += (P * d_v) V per 32-column block of V: the block scale of row t multiplies P[., t]
-#pragma unroll
-    for (int bh = 0; bh < C::NB / 2; ++bh) {
-      const int blk = dh * (C::NB / 2) + bh;
-      float dv[2][2];
-#pragma unroll
-      for (int nb = 0; nb < 2; ++nb) {
-        const int row = r0 + nb * 8 + 2 * tig;
-        dv[nb][0] = __half2float(*reinterpret_cast<const __half*>(vt + row * ROW + blk * 34));
-        dv[nb][1] = __half2float(*reinterpret_cast<const __half*>(vt + (row + 1) * ROW + blk * 34));
-      }
-      const uint32_t pa0 = pack_h2(pv[0][0] * dv[0][0], pv[0][1] * dv[0][1]);
-      const uint32_t pa1 = pack_h2(pv[0][2] * dv[0][0], pv[0][3] * dv[0][1]);
-      const uint32_t pa2 = pack_h2(pv[1][0] * dv[1][0], pv[1][1] * dv[1][1]);
-      const uint32_t pa3 = pack_h2(pv[1][2] * dv[1][0], pv[1][3] * dv[1][1]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {  // four 8-column n-blocks per 32-column block
-        const int nb = bh * 4 + q;
-        const int col = q * 8 + grp;  // this thread's column within the block
-        const uint8_t* v0 = vt + (r0 + 2 * tig) * ROW + blk * 34 + 2 + col;
-        const uint32_t w0 = static_cast<uint32_t>(v0[0]) | (static_cast<uint32_t>(v0[ROW]) << 8);
-        const uint32_t w1 =
-            static_cast<uint32_t>(v0[8 * ROW]) | (static_cast<uint32_t>(v0[9 * ROW]) << 8);
-        mma16816(o[nb], pa0, pa1, pa2, pa3, i8x2_to_h2(w0), i8x2_to_h2(w1));
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&bar.empty[s]);
+    return;
   }
-
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
-    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
-  }
-  asm volatile("bar.sync 1, 256;" ::: "memory");
-  float* ml_s = reinterpret_cast<float*>(smem + C::K_OFF);
-  float* o_s = ml_s + kComputeWarps * 16 * 2;
-  const int rg = warp & 3;  // row group; warps rg and rg + 4 hold the same (max, sum)
-  if (tig == 0 && (warp >> 2) == 0) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      ml_s[(rg * 16 + grp + 8 * h) * 2] = m_run[h];
-      ml_s[(rg * 16 + grp + 8 * h) * 2 + 1] = l_run[h];
-    }
-  }
-#pragma unroll
-  for (int nb = 0; nb < NBH; ++nb)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int row = grp + 8 * (e >> 1), col = (warp >> 2) * (D / 2) + nb * 8 + 2 * tig + (e & 1);
-      o_s[(rg * 16 + row) * D + col] = o[nb][e];
-    }
-  asm volatile("bar.sync 1, 256;" ::: "memory");
-  for (int idx = threadIdx.x; idx < g_count * D; idx += kQ8ComputeWarps * 32) {
-    const int g = idx / D, d = idx % D;
-    float m = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kComputeWarps; ++w) m = fmaxf(m, ml_s[(w * 16 + g) * 2]);
-    float l = 0.0f, acc = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kComputeWarps; ++w) {
-      const float wt = ex2_approx(ml_s[(w * 16 + g) * 2] - m);
-      l = fmaf(ml_s[(w * 16 + g) * 2 + 1], wt, l);
-      acc = fmaf(o_s[(w * 16 + g) * D + d], wt, acc);
-    }
-    const int h = h0 + g;
-    if (n_splits == 1) {
-      const float v = acc / l;
-      const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * D + d;
-      if (p.out_dtype == AIHOST_F32) static_cast<float*>(p.out)[oidx] = v;
-      else static_cast<__half*>(p.out)[oidx] = __float2half_rn(v);
-    } else {
-      const int64_t pidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * p.max_splits + split;
-      p.part_o[pidx * D + d] = acc;
-      if (d == 0) {
-        p.part_ml[pidx * 2] = m;
-        p.part_ml[pidx * 2 + 1] = l;
-      }
-    }
-  }
+  decode_compute<D, C::NSF, false>(p, smem, C::F_OFF, C::F_OFF + C::NSF * C::F_TILE, bar.f_full, bar.f_empty, q_s,
+                                   reinterpret_cast<float*>(smem + C::F_OFF), n, n_tiles, h0, g_count, b, split,
+                                   n_splits);
 }
 
 template <int D>

@@ -79,7 +79,6 @@ cudaError_t launch_decode_combine(const DecodeArgs& a, cudaStream_t st);
 // fp16-cache decode on the tensor cores: K/V maps over the cache with 64-row boxes.
 struct DecodeMmaArgs {
   DecodeArgs base;
-  int32_t q8_row_bytes;  // Q8_0 only: bytes per tile row (the TMA box width), 16-byte multiple
   CUtensorMap k_map;  // dims {d, Hkv, capacity, batch}, box {64, 1, 64, 1}, 128-byte swizzle
   CUtensorMap v_map;
 };
@@ -112,8 +111,11 @@ struct PrefillArgs {
   void* out;                // [batch][S][Hq][d]
   int32_t out_dtype;
   int32_t* status;
+  int32_t split_kv;         // 1: the CTA's two softmax groups split one query tile's cache range
 };
 bool prefill_supported(int32_t head_dim);
+// Split mode pays off when pairing query tiles would leave SMs idle (about one wave or less).
+bool prefill_split_kv(int32_t batch, int32_t n_new, int32_t n_q_heads, int32_t num_sms);
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st);
 
 }  // namespace aihost

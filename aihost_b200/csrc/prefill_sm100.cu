@@ -100,26 +100,41 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   const int n_qt = (a.n_new + kBM - 1) / kBM;
   const int h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (a.n_q_heads / a.n_kv_heads);
-  // adjacent query tiles 2x and 2x+1 (B absent past the end); the longest pairs launch first
+  // Pair mode: adjacent query tiles 2x and 2x+1 (B absent past the end), both groups read the
+  // same K/V tile j. Split mode: both groups take query tile x, group A cache tiles [0, n/2),
+  // group B [n/2, n), merged at the end. The longest work launches first in both.
+  const bool split = a.split_kv != 0;
   const int x = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
-  const int qt[2] = {2 * x, 2 * x + 1};
-  const bool has_b = qt[1] < n_qt;
+  const int qt[2] = {split ? x : 2 * x, split ? x : 2 * x + 1};
+  const bool has_b = split || qt[1] < n_qt;
   const int32_t start = a.seq_len ? a.seq_len[b] : a.start_scalar;
   const int32_t Lk = start + a.len_offset;
   const bool bad = Lk < 1 || start < 0;
-  int n_kv[2];
+  int n_kv[2], kv_lo[2] = {0, 0};
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     const int32_t kv_end = min(Lk, start + qt[t] * kBM + kBM);  // rows j <= start + q0 + 127, j < Lk
     n_kv[t] = (t == 1 && !has_b) || kv_end <= 0 ? 0 : (kv_end + kBN - 1) / kBN;
   }
-  const int n_load = max(n_kv[0], n_kv[1]);
+  if (split) {
+    const int n = n_kv[0];
+    n_kv[0] = n / 2;
+    n_kv[1] = n - n / 2;
+    kv_lo[1] = n / 2;
+  }
+  // K/V tiles loaded, in load order: pair mode tile j at step j; split mode A0, B0, A1, B1, ...
+  // (B has at most one tile more than A, loaded last).
+  const int n_load = split ? n_kv[0] + n_kv[1] : max(n_kv[0], n_kv[1]);
+  auto load_index = [&](int t, int j) -> int {
+    if (!split) return j;
+    return j < n_kv[0] ? 2 * j + t : 2 * n_kv[0] + (j - n_kv[0]);
+  };
   int32_t* status = a.status;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar.q_full, 1);
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&bar.q_ready[t], 128);
+      mbar_init(&bar.q_ready[t], split && t == 0 ? 256 : 128);
       mbar_init(&bar.s_full[t], 1);
       mbar_init(&bar.p_full[t], 128);
       mbar_init(&bar.o_full[t], 1);
@@ -149,21 +164,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       tma_prefetch_desc(&a.q_map);
       tma_prefetch_desc(&a.k_map);
       tma_prefetch_desc(&a.v_map);
-      mbar_arrive_expect_tx(&bar.q_full, (has_b ? 2 : 1) * C::TILE_BYTES);
-      for (int t = 0; t < (has_b ? 2 : 1); ++t)
+      const int n_q_tiles = has_b && !split ? 2 : 1;
+      mbar_arrive_expect_tx(&bar.q_full, n_q_tiles * C::TILE_BYTES);
+      for (int t = 0; t < n_q_tiles; ++t)
         for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d(q_s[t] + kb * kBM * 128, &a.q_map, &bar.q_full, kb * 64, h, qt[t] * kBM, b);
-      for (int j = 0; j < n_load; ++j) {
-        const int s = j % C::NS;
-        const uint32_t par = ((j / C::NS) & 1) ^ 1;
+          tma_load_4d((t ? q_s[1] : q_s[0]) + kb * kBM * 128, &a.q_map, &bar.q_full, kb * 64, h,
+                      (t ? qt[1] : qt[0]) * kBM, b);
+      for (int g = 0; g < n_load; ++g) {
+        // cache tile of load g: pair mode g; split mode A's g/2, B's, then B's last
+        const int tile = !split ? g : g < 2 * n_kv[0] ? ((g & 1) ? kv_lo[1] : 0) + (g >> 1) : g;
+        const int s = g % C::NS;
+        const uint32_t par = ((g / C::NS) & 1) ^ 1;
         if (!mbar_wait(&bar.k_empty[s], par, status)) break;
         mbar_arrive_expect_tx(&bar.k_full[s], C::TILE_BYTES);
         for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d(k_s + s * C::TILE_BYTES + kb * kBN * 128, &a.k_map, &bar.k_full[s], kb * 64, kvh, j * kBN, b);
+          tma_load_4d(k_s + s * C::TILE_BYTES + kb * kBN * 128, &a.k_map, &bar.k_full[s], kb * 64, kvh, tile * kBN,
+                      b);
         if (!mbar_wait(&bar.v_empty[s], par, status)) break;
         mbar_arrive_expect_tx(&bar.v_full[s], C::TILE_BYTES);
         for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d(v_s + s * C::TILE_BYTES + kb * kBN * 128, &a.v_map, &bar.v_full[s], kb * 64, kvh, j * kBN, b);
+          tma_load_4d(v_s + s * C::TILE_BYTES + kb * kBN * 128, &a.v_map, &bar.v_full[s], kb * 64, kvh, tile * kBN,
+                      b);
       }
     }
     // Cache rows >= Lk in the last V tile may hold stale bits (NaN patterns included); P is 0
@@ -191,12 +212,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       constexpr uint32_t idesc_qk = make_idesc_f16(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_f16(kBM, D, 0, 1);
       const uint32_t k_addr = smem_u32(k_s), v_addr = smem_u32(v_s);
-      const uint32_t q_addr[2] = {smem_u32(q_s[0]), smem_u32(q_s[1])};
+      const uint32_t q_addr[2] = {smem_u32(q_s[0]), smem_u32(q_s[split ? 0 : 1])};
       bool ok = mbar_wait(&bar.q_ready[0], 0, status);
-      if (ok && has_b) ok = mbar_wait(&bar.q_ready[1], 0, status);
+      if (ok && has_b && !split) ok = mbar_wait(&bar.q_ready[1], 0, status);
       tc_fence_after();
-      auto issue_qk = [&](int t, int j) {
-        const int s = j % C::NS;
+      // S_t = Q_t K^T with the K tile in ring slot s
+      auto issue_qk = [&](int t, int s) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
@@ -206,8 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         umma_commit(&bar.s_full[t]);
       };
       const uint32_t p_addr[2] = {smem_u32(p_s[0]), smem_u32(p_s[1])};
-      auto issue_pv = [&](int t, int j) {
-        const int s = j % C::NS;
+      // O_t (+)= P_t V with the V tile in ring slot s; j = the group's tile count so far
+      auto issue_pv = [&](int t, int j, int s) {
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint64_t vd = make_sw128_desc(v_addr + s * C::TILE_BYTES + kk * 2048, kBN * 128, 1024);
@@ -220,14 +241,51 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             umma_f16_ts(tmem + C::o_col(t), tmem + C::s_col(t) + kk * 8, vd, idesc_pv, acc);
         }
       };
-      if (ok && n_load > 0) {
+      if (split) {
+        // each group walks its own cache tiles; slots follow the producer's load order
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (!ok || n_kv[t] == 0) continue;
+          const int g = load_index(t, 0);
+          ok = mbar_wait(&bar.k_full[g % C::NS], (g / C::NS) & 1, status);
+          tc_fence_after();
+          if (ok) {
+            issue_qk(t, g % C::NS);
+            umma_commit(&bar.k_empty[g % C::NS]);
+          }
+        }
+        const int steps = max(n_kv[0], n_kv[1]);
+        for (int j = 0; ok && j < steps; ++j) {
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (!ok || j >= n_kv[t]) continue;
+            const int gv = load_index(t, j), sv = gv % C::NS;
+            const bool next = j + 1 < n_kv[t];
+            const int gk = next ? load_index(t, j + 1) : 0, sk = gk % C::NS;
+            if (!mbar_wait(&bar.v_full[sv], (gv / C::NS) & 1, status)) { ok = false; break; }
+            if (gv == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
+            if (next && !mbar_wait(&bar.k_full[sk], (gk / C::NS) & 1, status)) { ok = false; break; }
+            if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, j, sv);
+            umma_commit(&bar.v_empty[sv]);
+            if (next) {
+              issue_qk(t, sk);
+              umma_commit(&bar.k_empty[sk]);
+            } else {
+              umma_commit(&bar.o_full[t]);
+            }
+          }
+        }
+      }
+      if (!split && ok && n_load > 0) {
         ok = mbar_wait(&bar.k_full[0], 0, status);
         tc_fence_after();
         if (ok && n_kv[0] > 0) issue_qk(0, 0);
         if (ok && n_kv[1] > 0) issue_qk(1, 0);
         if (ok) umma_commit(&bar.k_empty[0]);
       }
-      for (int j = 0; ok && j < n_load; ++j) {
+      for (int j = 0; !split && ok && j < n_load; ++j) {
         const int s = j % C::NS;
         const int s1 = (j + 1) % C::NS;
         // operands first (normally long resident), then the softmax hand-offs
@@ -240,8 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           if (j >= n_kv[t]) continue;
           if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(t, j);
-          if (j + 1 < n_kv[t]) issue_qk(t, j + 1);
+          issue_pv(t, j, s);
+          if (j + 1 < n_kv[t]) issue_qk(t, s1);
           else umma_commit(&bar.o_full[t]);
         }
         if (!ok) break;
@@ -257,31 +315,41 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const int nk = n_kv[t];
-    const int q0 = qt[t] * kBM;
+    const int nk = t ? n_kv[1] : n_kv[0];
+    const int kv_first = t ? kv_lo[1] : 0;
+    const int q0 = (t ? qt[1] : qt[0]) * kBM;
+    uint8_t* const q_tile = split || t == 0 ? q_s[0] : q_s[1];
+    uint8_t* const p_tile = t ? p_s[1] : p_s[0];
     const int32_t qpos = start + q0 + r;      // absolute position of this query row
     const int32_t limit = min(qpos, Lk - 1);  // last visible cache row
     const bool active = t == 0 || has_b;
     bool ok = true;
     if (active) {
+      // In split mode both groups share Q tile A and each rotates half of its pairs.
+      const int qb = split ? 0 : t;
       ok = mbar_wait(&bar.q_full, 0, status);
       if (ok && a.rope_mode != AIHOST_ROPE_NONE) {
         const float pos = static_cast<float>(qpos);
 #pragma unroll
-        for (int pair = 0; pair < D / 2; ++pair) {
-          const int c1 = a.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
-          const int c2 = a.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
-          __half* p1 = reinterpret_cast<__half*>(q_s[t] + sw128_off(r, c1, kBM));
-          __half* p2 = reinterpret_cast<__half*>(q_s[t] + sw128_off(r, c2, kBM));
-          const float x1 = __half2float(*p1), x2 = __half2float(*p2);
-          float sn, cs;
-          sincos_reduced(pos * a.freqs.f[pair], &sn, &cs);
-          *p1 = __float2half_rn(x1 * cs - x2 * sn);
-          *p2 = __float2half_rn(x1 * sn + x2 * cs);
+        for (int half = 0; half < 2; ++half) {
+          if (split && half != t) continue;
+#pragma unroll
+          for (int pp = 0; pp < D / 4; ++pp) {
+            const int pair = half * (D / 4) + pp;
+            const int c1 = a.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
+            const int c2 = a.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
+            __half* p1 = reinterpret_cast<__half*>(q_tile + sw128_off(r, c1, kBM));
+            __half* p2 = reinterpret_cast<__half*>(q_tile + sw128_off(r, c2, kBM));
+            const float x1 = __half2float(*p1), x2 = __half2float(*p2);
+            float sn, cs;
+            sincos_reduced(pos * a.freqs.f[pair], &sn, &cs);
+            *p1 = __float2half_rn(x1 * cs - x2 * sn);
+            *p2 = __float2half_rn(x1 * sn + x2 * cs);
+          }
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&bar.q_ready[t]);
+      mbar_arrive(&bar.q_ready[qb]);
     }
 
     const float sl2 = a.scale * kLog2e;
@@ -295,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, sr[c]);
       tmem_wait_ld();
-      const int kv0 = j * kBN;
+      const int kv0 = (kv_first + j) * kBN;
       const bool need_mask = __any_sync(0xffffffffu, kv0 + kBN - 1 > limit);
       if (need_mask) {
 #pragma unroll
@@ -353,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             const int ch = (c & 1) * 4 + q * 2;  // 16-byte chunk index within the 128-byte row
-            uint8_t* row = p_s[t] + (c >> 1) * (kBM * 128) + r * 128;
+            uint8_t* row = p_tile + (c >> 1) * (kBM * 128) + r * 128;
             *reinterpret_cast<uint4*>(row + (((ch) ^ (r & 7)) << 4)) =
                 make_uint4(pk[8 * q], pk[8 * q + 1], pk[8 * q + 2], pk[8 * q + 3]);
             *reinterpret_cast<uint4*>(row + (((ch + 1) ^ (r & 7)) << 4)) =
@@ -371,33 +439,70 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       mbar_arrive(&bar.p_full[t]);
     }
     // ---- epilogue: O / l -> out[b][q0 + r][h][:]
-    if (active && ok && nk > 0 && mbar_wait(&bar.o_full[t], 0, status)) {
+    const bool valid = q0 + r < a.n_new;
+    const int64_t orow = ((static_cast<int64_t>(b) * a.n_new + q0 + r) * a.n_q_heads + h) * D;
+    auto store32 = [&](int c, const float (&o)[32]) {
+      if (!valid) return;
+      if (a.out_dtype == AIHOST_F16) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + orow + c * 32);
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          dst[v] = make_uint4(pack_half2(o[8 * v], o[8 * v + 1]), pack_half2(o[8 * v + 2], o[8 * v + 3]),
+                              pack_half2(o[8 * v + 4], o[8 * v + 5]), pack_half2(o[8 * v + 6], o[8 * v + 7]));
+      } else {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow + c * 32);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) dst[v] = make_float4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+      }
+    };
+    if (split) {
+      // Merge the two groups' partial softmax states of the same rows: (m, l) through shared
+      // memory (Q tile B's space, unused in this mode), O from both TMEM blocks. Each group writes
+      // half of the output columns.
+      float* ml = reinterpret_cast<float*>(q_s[1]);
+      ml[(t * kBM + r) * 2] = m;
+      ml[(t * kBM + r) * 2 + 1] = l;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      bool ready = ok;
+      if (ready && n_kv[0] > 0) ready = mbar_wait(&bar.o_full[0], 0, status);
+      if (ready) ready = mbar_wait(&bar.o_full[1], 0, status);
+      if (__all_sync(0xffffffffu, ready)) {
+        tc_fence_after();
+        const float mA = ml[r * 2], lA = ml[r * 2 + 1];
+        const float mB = ml[(kBM + r) * 2], lB = ml[(kBM + r) * 2 + 1];
+        const float mm = fmaxf(mA, mB);
+        const float aA = n_kv[0] > 0 ? ex2_approx(mA - mm) : 0.0f;
+        const float aB = ex2_approx(mB - mm);
+        const float L = lA * aA + lB * aB;
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        const float fA = aA * inv, fB = aB * inv;
+        const uint32_t oa_tmem = tmem + lane_base + C::o_col(0), ob_tmem = tmem + lane_base + C::o_col(1);
+#pragma unroll
+        for (int cc = 0; cc < D / 64; ++cc) {
+          const int c = t * (D / 64) + cc;
+          uint32_t ob[32], oa[32];
+          tmem_ld32(ob_tmem + c * 32, ob);
+          if (n_kv[0] > 0) tmem_ld32(oa_tmem + c * 32, oa);
+          tmem_wait_ld();
+          float o[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[i] = __uint_as_float(ob[i]) * fB + (n_kv[0] > 0 ? __uint_as_float(oa[i]) * fA : 0.0f);
+          store32(c, o);
+        }
+      }
+    } else if (active && ok && nk > 0 && mbar_wait(&bar.o_full[t], 0, status)) {
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      const bool valid = q0 + r < a.n_new;
-      const int64_t orow = ((static_cast<int64_t>(b) * a.n_new + q0 + r) * a.n_q_heads + h) * D;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_tmem + c * 32, o);
+        uint32_t ou[32];
+        tmem_ld32(o_tmem + c * 32, ou);
         tmem_wait_ld();
-        if (valid) {
-          if (a.out_dtype == AIHOST_F16) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + orow + c * 32);
+        float o[32];
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_uint4(pack_half2(__uint_as_float(o[8 * v]) * inv, __uint_as_float(o[8 * v + 1]) * inv),
-                                  pack_half2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv),
-                                  pack_half2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv),
-                                  pack_half2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv));
-          } else {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + orow + c * 32);
-#pragma unroll
-            for (int v = 0; v < 8; ++v)
-              dst[v] = make_float4(__uint_as_float(o[4 * v]) * inv, __uint_as_float(o[4 * v + 1]) * inv,
-                                   __uint_as_float(o[4 * v + 2]) * inv, __uint_as_float(o[4 * v + 3]) * inv);
-          }
-        }
+        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(ou[i]) * inv;
+        store32(c, o);
       }
     }
   }
@@ -418,7 +523,7 @@ cudaError_t launch_d(const PrefillArgs& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int n_qt = (a.n_new + kBM - 1) / kBM;
-  dim3 grid((n_qt + 1) / 2, a.n_q_heads, a.batch);
+  dim3 grid(a.split_kv ? n_qt : (n_qt + 1) / 2, a.n_q_heads, a.batch);
   kern<<<grid, kThreads, C::SMEM, st>>>(a);
   return cudaGetLastError();
 }
@@ -426,6 +531,12 @@ cudaError_t launch_d(const PrefillArgs& a, cudaStream_t st) {
 }  // namespace
 
 bool prefill_supported(int32_t head_dim) { return head_dim == 64 || head_dim == 128; }
+
+bool prefill_split_kv(int32_t batch, int32_t n_new, int32_t n_q_heads, int32_t num_sms) {
+  const int64_t n_qt = (n_new + kBM - 1) / kBM;
+  const int64_t pair_ctas = (n_qt + 1) / 2 * n_q_heads * static_cast<int64_t>(batch);
+  return pair_ctas < 2LL * num_sms;
+}
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st) {
   return a.head_dim == 64 ? launch_d<64>(a, st) : launch_d<128>(a, st);

@@ -338,6 +338,13 @@ def max_over_ranks(x: float, dist_on: bool) -> float:
     return float(t.item())
 
 
+def decode_kernel_name(cfg) -> str:
+    """The decode kernel the library picks for this cache dtype (token-major default strides)."""
+    from aihost_b200 import F16, Q8_0
+
+    return {F16: "decode_mma_kernel", Q8_0: "decode_q8_kernel"}.get(cfg.kv_dtype, "decode_splitk_kernel")
+
+
 def summarize(cfg, r, n_gpus, dist_on, pk, pk_kind):
     w = r["work"]
     ms_step = max_over_ranks(statistics.mean(r["ms"]), dist_on)
@@ -362,7 +369,7 @@ def summarize(cfg, r, n_gpus, dist_on, pk, pk_kind):
     else:
         achieved = w["kernel_bytes"] / (k_ms * 1e-3) * 1e-9
         roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": "decode_splitk_kernel",
+                "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": decode_kernel_name(cfg),
                 "kernel_ms": k_ms, "algorithmic_per_launch": w["kernel_bytes"], "peak_source": f"{pk_kind} copy",
                 "frac_of_8tbs_spec": achieved / 8000.0}
     traffic = read_traffic(cfg.number)

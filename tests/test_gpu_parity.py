@@ -135,6 +135,16 @@ def test_prefill_ragged(ctx, s, d):
     check_call(ctx, cfg)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_prefill_pair_schedule(ctx, d):
+    """A grid of more than two waves of query-tile pairs: the kernel pairs adjacent query tiles
+    (shared K/V tiles) instead of splitting each tile's cache range over its two groups."""
+    cfg = CONFIGS[2].scaled(batch=2, n_new=1200, n_q_heads=32, n_kv_heads=8, head_dim=d, cached=None,
+                            cached_list=[0, 64])
+    # the partial oracle appends only the KV heads of its query heads: compare the output only
+    check_call(ctx, cfg, part=(0, 2, 0, 3), check_cache=False)
+
+
 @pytest.mark.parametrize("cached", [[100], [1, 257]])
 def test_prefill_chunked(ctx, cached):
     """Prefill after cached rows (chunked prefill): causal rule j <= P + i with P > 0."""

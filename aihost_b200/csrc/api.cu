@@ -32,6 +32,8 @@ struct aihost_attn_ctx {
   int32_t* d_status = nullptr;
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
+  unsigned long long* counters = nullptr;  // fused split merge: epoch-tagged arrival counts
+  uint32_t epoch = 0;
   bool profiling = false;
   std::mutex prof_mu;
   ProfSlot prof[AIHOST_KERNEL_COUNT];
@@ -132,12 +134,29 @@ RopeFreqs make_freqs(float theta, int32_t head_dim) {
 }
 
 // Decode split plan: rows per split chosen from the capacity (so the scratch size is a
-// function of the description alone), aiming at ~8 resident CTAs per SM.
+// function of the description alone).
+//  - fp16 / Q8_0 caches (tensor-core kernels, 2 CTAs per SM, one CTA per <= 16 query heads):
+//    splits of at most 4096 rows, evenly sized, and enough of them for two CTAs per SM. Long
+//    splits amortise each CTA's fixed work (Q rotation, pipeline fill, the four-warp merge).
+//  - fp32 caches (CUDA-core kernel): ~8 resident CTAs per SM, 64..512 rows per split.
 struct DecodePlan {
   int32_t chunk, max_splits;
 };
 DecodePlan plan_decode(const aihost_attn_desc* d, int32_t batch, int32_t num_sms) {
   const int32_t G = d->n_q_heads / d->n_kv_heads;
+  DecodePlan p;
+  if (d->kv_dtype == AIHOST_F16 || d->kv_dtype == AIHOST_Q8_0) {
+    const int64_t units = static_cast<int64_t>(batch) * d->n_kv_heads * ((G + 15) / 16);
+    const int64_t cap = d->kv_capacity;
+    int64_t splits = (cap + 4095) / 4096;
+    const int64_t fill = (2LL * num_sms + units - 1) / units;
+    if (splits < fill) splits = fill;
+    int64_t chunk = (cap + splits - 1) / splits;
+    chunk = (chunk + 63) / 64 * 64;
+    p.chunk = static_cast<int32_t>(chunk);
+    p.max_splits = static_cast<int32_t>((cap + chunk - 1) / chunk);
+    return p;
+  }
   const int32_t gt = G >= 8 ? 8 : G >= 4 ? 4 : G >= 2 ? 2 : 1;
   const int64_t units = static_cast<int64_t>(batch) * d->n_kv_heads * ((G + gt - 1) / gt);
   const int64_t target = static_cast<int64_t>(num_sms) * 8;
@@ -145,7 +164,6 @@ DecodePlan plan_decode(const aihost_attn_desc* d, int32_t batch, int32_t num_sms
   chunk = (chunk + 31) / 32 * 32;
   if (chunk < 64) chunk = 64;
   if (chunk > 512) chunk = 512;
-  DecodePlan p;
   p.chunk = static_cast<int32_t>(chunk);
   p.max_splits = static_cast<int32_t>((d->kv_capacity + chunk - 1) / chunk);
   return p;
@@ -243,9 +261,12 @@ cudaError_t timed_launch(aihost_attn_ctx* ctx, int kind, cudaStream_t st, F&& fn
   return cudaSuccess;
 }
 
+// One-token attention over rows [0, start + len_offset). With k_new / v_new (forward decode) the
+// new rows are appended at row seq_len[b] first (inside the decode kernel where it can).
 aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const KvLayout& kv, float scale,
                          int32_t batch, const void* q, const void* kc, const void* vc, const int32_t* seq_len,
-                         int32_t start_scalar, int32_t len_offset, int32_t rope_mode, void* out, cudaStream_t st) {
+                         int32_t start_scalar, int32_t len_offset, int32_t rope_mode, void* out, cudaStream_t st,
+                         const void* k_new = nullptr, const void* v_new = nullptr) {
   DecodePlan plan = plan_decode(d, batch, ctx->num_sms);
   const size_t need = decode_scratch_bytes(batch, d->n_q_heads, d->head_dim, plan.max_splits);
   if (need > ctx->scratch_bytes)
@@ -277,6 +298,9 @@ aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const 
   a.out = out;
   a.out_dtype = d->out_dtype;
   a.status = ctx->d_status;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.new_dtype = d->q_dtype;
   cudaError_t e = launch_decode_any(a, st, ctx);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return AIHOST_OK;
@@ -302,10 +326,11 @@ size_t prefill_stage_bytes(const aihost_attn_desc* d, int32_t batch, int32_t n_q
 aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const KvLayout& kv_in, float scale,
                           int32_t batch, int32_t n_q, const void* q, const void* kc, const void* vc,
                           const int32_t* seq_len, int32_t start_scalar, int32_t len_offset, int32_t kv_rows,
-                          int32_t rope_mode, void* out, cudaStream_t st) {
+                          int32_t rope_mode, void* out, cudaStream_t st, bool after_append) {
   if (!prefill_supported(d->head_dim)) return fail(AIHOST_EUNSUPPORTED, "prefill head_dim %d", d->head_dim);
   KvLayout kv = kv_in;
-  if (d->q_dtype != AIHOST_F16 || d->kv_dtype != AIHOST_F16) {
+  const bool q_staged = d->q_dtype != AIHOST_F16, kv_staged = d->kv_dtype != AIHOST_F16;
+  if (q_staged || kv_staged) {
     const size_t need = prefill_stage_bytes(d, batch, n_q, kv_rows);
     if (need > ctx->scratch_bytes)
       return fail(AIHOST_ENOMEM,
@@ -371,6 +396,10 @@ aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const
   a.out_dtype = d->out_dtype;
   a.status = ctx->d_status;
   a.split_kv = prefill_split_kv(batch, n_q, d->n_q_heads, ctx->num_sms) ? 1 : 0;
+  // The kernel launched just before the prefill: staging of the cache (q, if staged, was
+  // written one launch earlier), else staging of q, else (forward) the append, which leaves q
+  // alone, else (mha) the caller's own work, which may have produced q.
+  a.q_early = kv_staged || (!q_staged && after_append) ? 1 : 0;
   cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_PREFILL, st, [&] { return launch_prefill(a, st); });
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return AIHOST_OK;
@@ -379,43 +408,53 @@ aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const
 }  // namespace
 
 namespace aihost {
-cudaError_t launch_decode_any(const DecodeArgs& a, cudaStream_t st, aihost_attn_ctx* ctx) {
+cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ctx) {
   auto run = [&](int kind, auto&& fn) -> cudaError_t { return ctx ? timed_launch(ctx, kind, st, fn) : fn(); };
-  cudaError_t e = cudaSuccess;
-  bool done = false;
+  // Tensor-core path: TMA maps over the cache (fp16 tiles, or Q8_0 rows as 32-bit words).
+  DecodeMmaArgs m;
+  memset(&m, 0, sizeof(m));
+  bool mma = false;
+  char saved[sizeof(g_err)];
+  memcpy(saved, g_err, sizeof(g_err));
   if (a.kv.dtype == AIHOST_F16) {
-    DecodeMmaArgs m;
-    memset(&m, 0, sizeof(m));
-    m.base = a;
     const int64_t seq_stride = a.kv.seq_stride ? a.kv.seq_stride : a.kv.token_stride * a.kv.capacity;
-    char saved[sizeof(g_err)];
-    memcpy(saved, g_err, sizeof(g_err));
-    if (encode_f16_map(&m.k_map, a.k_cache, a.head_dim, a.n_kv_heads, a.kv.capacity, a.batch, a.kv.head_stride,
-                       a.kv.token_stride, seq_stride, "k_cache", 64) == AIHOST_OK &&
-        encode_f16_map(&m.v_map, a.v_cache, a.head_dim, a.n_kv_heads, a.kv.capacity, a.batch, a.kv.head_stride,
-                       a.kv.token_stride, seq_stride, "v_cache", 64) == AIHOST_OK) {
-      e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode_mma(m, st); });
-      done = true;
-    } else {
-      memcpy(g_err, saved, sizeof(g_err));  // strides TMA cannot describe: CUDA-core kernel instead
-    }
+    mma = encode_f16_map(&m.k_map, a.k_cache, a.head_dim, a.n_kv_heads, a.kv.capacity, a.batch, a.kv.head_stride,
+                         a.kv.token_stride, seq_stride, "k_cache", 64) == AIHOST_OK &&
+          encode_f16_map(&m.v_map, a.v_cache, a.head_dim, a.n_kv_heads, a.kv.capacity, a.batch, a.kv.head_stride,
+                         a.kv.token_stride, seq_stride, "v_cache", 64) == AIHOST_OK;
   } else if (a.kv.dtype == AIHOST_Q8_0) {
-    DecodeMmaArgs m;
-    memset(&m, 0, sizeof(m));
-    m.base = a;
-    char saved[sizeof(g_err)];
-    memcpy(saved, g_err, sizeof(g_err));
     const uint32_t bw = q8_box_words(a.head_dim, a.kv.head_stride);
-    if (bw && encode_q8_map(&m.k_map, a.k_cache, a.kv, a.batch, bw) == AIHOST_OK &&
-        encode_q8_map(&m.v_map, a.v_cache, a.kv, a.batch, bw) == AIHOST_OK) {
-      e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode_mma(m, st); });
-      done = true;
-    } else {
-      memcpy(g_err, saved, sizeof(g_err));
-    }
+    mma = bw && encode_q8_map(&m.k_map, a.k_cache, a.kv, a.batch, bw) == AIHOST_OK &&
+          encode_q8_map(&m.v_map, a.v_cache, a.kv, a.batch, bw) == AIHOST_OK;
   }
-  if (!done) e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode(a, st); });
-  if (e != cudaSuccess || a.max_splits <= 1) return e;
+  if (!mma) memcpy(g_err, saved, sizeof(g_err));  // strides TMA cannot describe: CUDA-core kernel instead
+  // One CTA per <= 16 query heads: with a single head group per KV head, the CTA of the last
+  // split appends the new rows itself and the last split to finish merges the partials.
+  const int32_t G = a.n_q_heads / a.n_kv_heads;
+  const bool one_group = G <= 16;
+  const int64_t n_counters = static_cast<int64_t>(a.batch) * a.n_kv_heads;
+  a.fuse_append = mma && one_group && a.k_new ? 1 : 0;
+  if (ctx) {
+    a.counters = ctx->counters;
+    a.epoch = ctx->epoch++;
+  }
+  if (!(mma && one_group && n_counters <= kMaxSplitCounters)) a.counters = nullptr;
+  cudaError_t e = cudaSuccess;
+  if (a.k_new && !a.fuse_append) {
+    e = run(AIHOST_KERNEL_APPEND, [&] {
+      return launch_kv_append(a.k_new, a.v_new, a.new_dtype, const_cast<void*>(a.k_cache), const_cast<void*>(a.v_cache),
+                              a.kv, a.seq_len, a.batch, 1, a.n_kv_heads, a.head_dim, a.rope_mode, a.freqs, a.status,
+                              st);
+    });
+    if (e != cudaSuccess) return e;
+  }
+  if (mma) {
+    m.base = a;
+    e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode_mma(m, st); });
+  } else {
+    e = run(AIHOST_KERNEL_DECODE, [&] { return launch_decode(a, st); });
+  }
+  if (e != cudaSuccess || a.max_splits <= 1 || a.counters) return e;
   return run(AIHOST_KERNEL_COMBINE, [&] { return launch_decode_combine(a, st); });
 }
 
@@ -462,10 +501,13 @@ aihost_status aihost_attn_create(int32_t device, aihost_attn_ctx** out_ctx) {
     return cuda_fail(e, "cudaMalloc(status)");
   }
   e = cudaMemset(ctx->d_status, 0, sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->counters, kMaxSplitCounters * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(ctx->counters, 0, kMaxSplitCounters * sizeof(unsigned long long));
   if (e != cudaSuccess) {
+    cudaFree(ctx->counters);
     cudaFree(ctx->d_status);
     delete ctx;
-    return cuda_fail(e, "cudaMemset(status)");
+    return cuda_fail(e, "context setup");
   }
   *out_ctx = ctx;
   return AIHOST_OK;
@@ -481,6 +523,7 @@ aihost_status aihost_attn_destroy(aihost_attn_ctx* ctx) {
     }
   for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
   cudaFree(ctx->scratch);
+  cudaFree(ctx->counters);
   cudaFree(ctx->d_status);
   delete ctx;
   return AIHOST_OK;
@@ -551,21 +594,22 @@ aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* 
   DeviceGuard g(ctx->device);
   if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_new == 1)  // append + attention (the append fused into the decode kernel where it can be)
+    return run_decode(ctx, desc, kv, scale, batch, q, k_cache, v_cache, seq_len, 0, 1, desc->rope_mode, out, st,
+                      k_new, v_new);
   const RopeFreqs freqs = make_freqs(desc->rope_mode != AIHOST_ROPE_NONE ? desc->rope_theta : 1.0f, desc->head_dim);
   cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_APPEND, st, [&] {
     return launch_kv_append(k_new, v_new, desc->q_dtype, k_cache, v_cache, kv, seq_len, batch, n_new,
                             desc->n_kv_heads, desc->head_dim, desc->rope_mode, freqs, ctx->d_status, st);
   });
   if (e != cudaSuccess) return cuda_fail(e, "kv append launch");
-  if (n_new == 1)
-    return run_decode(ctx, desc, kv, scale, batch, q, k_cache, v_cache, seq_len, 0, 1, desc->rope_mode, out, st);
   int32_t kv_rows = desc->kv_capacity;
   if (h_seq_len) {
     kv_rows = 0;
     for (int32_t b = 0; b < batch; ++b) kv_rows = h_seq_len[b] + n_new > kv_rows ? h_seq_len[b] + n_new : kv_rows;
   }
   return run_prefill(ctx, desc, kv, scale, batch, n_new, q, k_cache, v_cache, seq_len, 0, n_new, kv_rows,
-                     desc->rope_mode, out, st);
+                     desc->rope_mode, out, st, true);
 }
 
 aihost_status aihost_attn_mha(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t n_q, int32_t n_kv,
@@ -590,7 +634,7 @@ aihost_status aihost_attn_mha(aihost_attn_ctx* ctx, const aihost_attn_desc* desc
   if (n_q == 1)  // FusedMHAGenerate: every row visible, no mask
     return run_decode(ctx, desc, kv, scale, 1, q, k, v, nullptr, 0, n_kv, AIHOST_ROPE_NONE, out, st);
   return run_prefill(ctx, desc, kv, scale, 1, n_q, q, k, v, nullptr, start_pos, n_kv - start_pos, n_kv,
-                     AIHOST_ROPE_NONE, out, st);
+                     AIHOST_ROPE_NONE, out, st, false);
 }
 
 aihost_status aihost_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,

@@ -232,6 +232,16 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t m, uint32_t n, ui
          | (a_mn << 15) | (b_mn << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// ------------------------------------------------------------------------------- dependent launch
+// Programmatic dependent launch: a kernel that feeds the next one signals early that the next
+// may be scheduled; the next kernel waits for the full completion (and memory visibility) of
+// its predecessor before it reads what that predecessor wrote. Both are no-ops when the launch
+// was not programmatic.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------- numeric helpers
 __device__ __forceinline__ float ld_as_float(const float* p) { return *p; }
 __device__ __forceinline__ float ld_as_float(const __half* p) { return __half2float(*p); }

@@ -18,6 +18,7 @@
 // (ring depth x 2 x 64 x head_dim x 2 bytes) and few instructions per byte.
 #include "common.cuh"
 #include "kernels.h"
+#include "rows.cuh"
 
 namespace aihost {
 namespace {
@@ -39,6 +40,7 @@ struct DecodeCfg {
   static constexpr int Q_BYTES = 16 * QROW * 2;
   static constexpr int BAR_OFF = Q_OFF + Q_BYTES;
   static constexpr int SMEM = BAR_OFF + 128 + 1024;
+  static_assert(NS * TILE_BYTES >= kComputeWarps * 16 * (D + 8 + 2) * 4, "merge buffer reuses the K ring");
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -73,6 +75,40 @@ __device__ __forceinline__ uint32_t sw_addr(uint32_t tile, int row, int col) {
 struct DecBars {
   uint64_t full[6], empty[6];
 };
+
+// The new token's K (warp 0, rotated) or V (warp 1) row of KV head kvh, written into cache row
+// t the way the append kernel writes it, then made visible to this CTA's later TMA reads.
+template <int D>
+__device__ __forceinline__ void append_new_row(const DecodeArgs& p, int b, int kvh, int32_t t, int warp, int lane) {
+  constexpr int E = D / 32;
+  const bool is_k = warp == 0;
+  const int64_t row = static_cast<int64_t>(b) * p.n_kv_heads + kvh;
+  const int esz = p.new_dtype == AIHOST_F32 ? 4 : 2;
+  const uint8_t* src = static_cast<const uint8_t*>(is_k ? p.k_new : p.v_new) + row * D * esz;
+  float x[E];
+  load_row_warp<E>(src, p.new_dtype, lane, x);
+  if (is_k && p.rope_mode != AIHOST_ROPE_NONE) rope_row_warp<E>(x, lane, static_cast<float>(t), p.rope_mode, p.freqs);
+  uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(is_k ? p.k_cache : p.v_cache)) + b * p.kv.seq_stride +
+                 static_cast<int64_t>(t) * p.kv.token_stride + static_cast<int64_t>(kvh) * p.kv.head_stride;
+  store_row_warp<E>(x, lane, dst, p.kv.dtype);
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Counts this split's arrival on an epoch-tagged counter (high 32 bits: the call's epoch, low:
+// arrivals); true for the last of n_splits arrivals of this call. A counter still holding an
+// earlier epoch restarts at 1. Never waits on another CTA; the CAS retries only on contention.
+__device__ __forceinline__ bool split_arrive(unsigned long long* c, uint32_t epoch, int n_splits, int32_t* status) {
+  unsigned long long cur = atomicAdd(c, 0ull);
+  for (uint32_t it = 0; it < kMaxWaitIters; ++it) {
+    const bool same = static_cast<uint32_t>(cur >> 32) == epoch;
+    const unsigned long long want = same ? cur + 1 : ((static_cast<unsigned long long>(epoch) << 32) | 1ull);
+    const unsigned long long seen = atomicCAS(c, cur, want);
+    if (seen == cur) return static_cast<uint32_t>(want) == static_cast<uint32_t>(n_splits);
+    cur = seen;
+  }
+  atomicOr(status, kStatusWaitTimeout);
+  return false;
+}
 
 // Compute-warp half of both kernels (warps 0-3): streams the fp16 K/V tiles of ring `full` /
 // `empty` (NS stages of TILE_BYTES each at k_off / v_off), keeps (max, sum, O) per query row in
@@ -204,8 +240,10 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& p, uint8_t* sme
   }
   // all tiles consumed: `merge` reuses ring memory no producer can target any more
   asm volatile("bar.sync 1, 128;" ::: "memory");
+  // O rows padded to D + 8 floats: a quad's float2 stores then cover all 32 banks per half-warp
+  constexpr int OP = D + 8;
   float* ml_s = merge;                           // [4 warps][16 rows][2]
-  float* o_s = ml_s + kComputeWarps * 16 * 2;    // [4 warps][16 rows][D]
+  float* o_s = ml_s + kComputeWarps * 16 * 2;    // [4 warps][16 rows][OP]
   if (tig == 0) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -216,10 +254,9 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& p, uint8_t* sme
 #pragma unroll
   for (int nb = 0; nb < D / 8; ++nb)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int row = grp + 8 * (e >> 1), col = nb * 8 + 2 * tig + (e & 1);
-      o_s[(warp * 16 + row) * D + col] = o[nb][e];
-    }
+    for (int h = 0; h < 2; ++h)
+      *reinterpret_cast<float2*>(&o_s[(warp * 16 + grp + 8 * h) * OP + nb * 8 + 2 * tig]) =
+          make_float2(o[nb][2 * h], o[nb][2 * h + 1]);
   asm volatile("bar.sync 1, 128;" ::: "memory");
   for (int idx = threadIdx.x; idx < g_count * D; idx += kComputeWarps * 32) {
     const int g = idx / D, d = idx % D;
@@ -231,7 +268,7 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& p, uint8_t* sme
     for (int w = 0; w < kComputeWarps; ++w) {
       const float wt = ex2_approx(ml_s[(w * 16 + g) * 2] - m);
       l = fmaf(ml_s[(w * 16 + g) * 2 + 1], wt, l);
-      acc = fmaf(o_s[(w * 16 + g) * D + d], wt, acc);
+      acc = fmaf(o_s[(w * 16 + g) * OP + d], wt, acc);
     }
     const int h = h0 + g;
     if (n_splits == 1) {
@@ -246,6 +283,78 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& p, uint8_t* sme
         p.part_ml[pidx * 2] = m;
         p.part_ml[pidx * 2 + 1] = l;
       }
+    }
+  }
+  if (n_splits == 1 || !p.counters) return;
+  // ---- fused combine: the last split of this (sequence, head group) to finish merges them all
+  __shared__ int s_last;
+  __threadfence();
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (threadIdx.x == 0)
+    s_last = split_arrive(&p.counters[static_cast<int64_t>(b) * gridDim.y + blockIdx.y], p.epoch, n_splits, p.status);
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (!s_last) return;
+  __threadfence();
+  // per-(head, split) weights 2^(m_s - m) / l first (one thread per head), then every output
+  // element as a weighted sum of the splits' partial O, four columns per thread
+  float* wts = ml_s;  // [16 heads][max_splits <= kMergeSplits], reusing the merge buffer
+  constexpr int kMergeSplits = 64;
+  const bool fits = p.max_splits <= kMergeSplits;
+  if (fits && threadIdx.x < g_count) {
+    const int64_t base = (static_cast<int64_t>(b) * p.n_q_heads + h0 + threadIdx.x) * p.max_splits;
+    float m = -INFINITY;
+    for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, __ldcg(&p.part_ml[(base + sp) * 2]));
+    float l = 0.0f;
+    for (int sp = 0; sp < n_splits; ++sp) {
+      const float w = exp2f(__ldcg(&p.part_ml[(base + sp) * 2]) - m);
+      wts[threadIdx.x * kMergeSplits + sp] = w;
+      l = fmaf(__ldcg(&p.part_ml[(base + sp) * 2 + 1]), w, l);
+    }
+    const float inv = 1.0f / l;
+    for (int sp = 0; sp < n_splits; ++sp) wts[threadIdx.x * kMergeSplits + sp] *= inv;
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (int idx = threadIdx.x; idx < g_count * (D / 4); idx += kComputeWarps * 32) {
+    const int g = idx / (D / 4), d = (idx % (D / 4)) * 4;
+    const int64_t base = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * p.max_splits;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (fits) {
+      for (int sp = 0; sp < n_splits; ++sp) {
+        const float w = wts[g * kMergeSplits + sp];
+        const float4 o4 = __ldcg(reinterpret_cast<const float4*>(&p.part_o[(base + sp) * D + d]));
+        acc.x = fmaf(o4.x, w, acc.x);
+        acc.y = fmaf(o4.y, w, acc.y);
+        acc.z = fmaf(o4.z, w, acc.z);
+        acc.w = fmaf(o4.w, w, acc.w);
+      }
+    } else {  // more splits than the weight table holds: weights recomputed per element
+      float m = -INFINITY;
+      for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, __ldcg(&p.part_ml[(base + sp) * 2]));
+      float l = 0.0f;
+      for (int sp = 0; sp < n_splits; ++sp) {
+        const float w = exp2f(__ldcg(&p.part_ml[(base + sp) * 2]) - m);
+        l = fmaf(__ldcg(&p.part_ml[(base + sp) * 2 + 1]), w, l);
+        const float4 o4 = __ldcg(reinterpret_cast<const float4*>(&p.part_o[(base + sp) * D + d]));
+        acc.x = fmaf(o4.x, w, acc.x);
+        acc.y = fmaf(o4.y, w, acc.y);
+        acc.z = fmaf(o4.z, w, acc.z);
+        acc.w = fmaf(o4.w, w, acc.w);
+      }
+      const float inv = 1.0f / l;
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
+    }
+    const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D + d;
+    if (p.out_dtype == AIHOST_F32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oidx) = acc;
+    } else {
+      const __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t*>(&lo);
+      u.y = *reinterpret_cast<const uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + oidx) = u;
     }
   }
 }
@@ -321,6 +430,8 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
     }
     fence_mbar_init();
   }
+  // the last split's CTA writes the new token's rows before any TMA reads them
+  if (p.fuse_append && sub == 0 && t0 + p.chunk >= Lk && warp < 2) append_new_row<D>(p, b, kvh, Lk - 1, warp, lane);
   load_q_rows<D>(p, q_s, b, h0, g_count, start, kThreads);
   __syncthreads();
 
@@ -386,7 +497,7 @@ struct Q8Cfg {
   static constexpr int Q_BYTES = 16 * QROW * 2;
   static constexpr int BAR_OFF = Q_OFF + Q_BYTES;
   static constexpr int SMEM = BAR_OFF + 128 + 1024;
-  static constexpr int MERGE_BYTES = kComputeWarps * 16 * (D + 2) * 4;
+  static constexpr int MERGE_BYTES = kComputeWarps * 16 * (D + 8 + 2) * 4;
   static_assert(2 * NSF * F_TILE >= MERGE_BYTES, "merge buffer reuses the fp16 rings");
   static_assert(NSR <= 4 && NSF <= 4, "barrier arrays hold four stages");
 };
@@ -473,6 +584,9 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
     }
     fence_mbar_init();
   }
+  // the last split's CTA writes the new token's rows before any TMA reads them
+  if (p.fuse_append && sub == 0 && t0 + p.chunk >= Lk && warp < 2)
+    append_new_row<D>(p, b, kvh, Lk - 1, warp, threadIdx.x & 31);
   load_q_rows<D>(p, q_s, b, h0, g_count, start, kQ8Threads);
   __syncthreads();
 

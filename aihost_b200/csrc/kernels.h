@@ -68,7 +68,19 @@ struct DecodeArgs {
   void* out;                // [batch][Hq][d], out_dtype
   int32_t out_dtype;
   int32_t* status;
+  // The new token's rows (forward decode): k_new / v_new [batch][Hkv][d] of new_dtype, appended at
+  // row seq_len[b] (K rotated). NULL when the cache is already complete (mha).
+  const void* k_new;
+  const void* v_new;
+  int32_t new_dtype;
+  int32_t fuse_append;          // set by launch_decode_any: the kernel appends the rows itself
+  // Fused combine (tensor-core kernels): per (sequence, blockIdx.y) arrival counters tagged with
+  // the call's epoch; the last split to arrive merges the partials. NULL: combine kernel.
+  unsigned long long* counters;
+  uint32_t epoch;
 };
+// Arrival counters a fused combine may use (per (sequence, KV head, head group)).
+constexpr int64_t kMaxSplitCounters = 1 << 16;
 size_t decode_scratch_bytes(int32_t batch, int32_t n_q_heads, int32_t head_dim, int32_t max_splits);
 // Split kernel; writes the output directly for sequences that fit in one split.
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t st);
@@ -90,10 +102,13 @@ uint32_t q8_box_words(int32_t head_dim, int64_t head_stride);
 }  // namespace aihost
 struct aihost_attn_ctx;
 namespace aihost {
-// Decode kernel for the cache dtype (tensor-core path for fp16 caches with TMA-compatible
-// strides, CUDA-core path otherwise) followed by the split merge; launches are timed by the
-// context's profiler when ctx is non-NULL. Defined in api.cu.
-cudaError_t launch_decode_any(const DecodeArgs& a, cudaStream_t st, aihost_attn_ctx* ctx);
+// Decode with whichever kernel fits the cache: the tensor-core kernels for fp16 / Q8_0 caches
+// with TMA-compatible strides, the CUDA-core split kernel otherwise. Includes the new rows'
+// append (when a.k_new is set) and the split merge, both fused into the tensor-core kernels when
+// a group of query heads fits one CTA. Launches are timed by the context's profiler when ctx is
+// non-NULL; the context also supplies the merge counters and epoch (with ctx NULL the caller
+// sets a.counters / a.epoch, or leaves counters NULL for the combine kernel). Defined in api.cu.
+cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ctx);
 
 // ---------------------------------------------------------------- prefill_sm100.cu
 struct PrefillArgs {
@@ -112,6 +127,7 @@ struct PrefillArgs {
   int32_t out_dtype;
   int32_t* status;
   int32_t split_kv;         // 1: the CTA's two softmax groups split one query tile's cache range
+  int32_t q_early;          // 1: q is not written by the kernel launched just before this one
 };
 bool prefill_supported(int32_t head_dim);
 // Split mode pays off when pairing query tiles would leave SMs idle (about one wave or less).

@@ -6,7 +6,8 @@
 // running while another component holds the GPU's allocation budget. aihost_attn_forward needs
 // a context (one cudaMalloc for its status word) and split scratch sized by
 // aihost_attn_reserve (another cudaMalloc). aihost_attn_decode_noalloc does the same
-// decode step (RoPE, KV append, split-K attention, split merge) with the split scratch in
+// decode step (RoPE, KV append, split-K attention, split merge) with the split scratch and the
+// merge counters in
 // g_noalloc_scratch below: a fixed array that the CUDA runtime places in every device's
 // memory when the library's module is loaded, and that stays there until the process exits.
 //
@@ -19,8 +20,10 @@
 //     stream capture;
 //   - all calls share the one array: calls whose kernels overlap on the GPU (different streams,
 //     different host threads) race on it. Serialise them, e.g. one stream per device;
-//   - the array keeps the last call's contents; the only field that must start at zero, the
-//     device status word, is cleared (cudaMemsetAsync) at the start of every call.
+//   - the array keeps the last call's contents. Two fields must start at zero: the device
+//     status word, cleared (cudaMemsetAsync) at the start of every call, and the split-merge
+//     arrival counters, zero when the module loads and tagged with a per-device call epoch
+//     afterwards, so stale counts of earlier calls are never mistaken for this call's.
 #include <string.h>
 
 #include <mutex>
@@ -39,13 +42,15 @@ aihost_status noalloc_prepare(const aihost_attn_desc* desc, int32_t batch, KvLay
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
-constexpr size_t kStatusBytes = 256;  // status word, kept at the front (256-byte aligned partials after it)
+constexpr size_t kStatusBytes = 256;  // status word, kept at the front
+constexpr size_t kCounterBytes = kMaxSplitCounters * sizeof(unsigned long long);  // then the counters
 constexpr int kMaxDevices = 64;
 
-__device__ __align__(256) uint8_t g_noalloc_scratch[kStatusBytes + kNoAllocScratchBytes];
+__device__ __align__(256) uint8_t g_noalloc_scratch[kStatusBytes + kCounterBytes + kNoAllocScratchBytes];
 
 std::mutex g_mu;
 void* g_dev_addr[kMaxDevices] = {};
+uint32_t g_epoch[kMaxDevices] = {};
 
 // Device address of g_noalloc_scratch on the current device (looked up once per device).
 aihost_status scratch_address(int dev, uint8_t** out) {
@@ -60,6 +65,11 @@ aihost_status scratch_address(int dev, uint8_t** out) {
   }
   *out = static_cast<uint8_t*>(g_dev_addr[dev]);
   return AIHOST_OK;
+}
+
+uint32_t next_epoch(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return g_epoch[dev]++;
 }
 
 }  // namespace
@@ -84,6 +94,13 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   RopeFreqs freqs;
   aihost_status s = noalloc_prepare(desc, batch, &kv, &scale, &chunk, &max_splits, &freqs, sms);
   if (s != AIHOST_OK) return s;
+  // the size check depends on the description alone and comes before the pointer checks
+  const size_t need = decode_scratch_bytes(batch, desc->n_q_heads, desc->head_dim, max_splits);
+  if (need > kNoAllocScratchBytes)
+    return api_fail(AIHOST_ENOMEM,
+                 "aihost_attn_decode_noalloc: this call needs %zu bytes of split scratch; the static array holds "
+                 "%zu (8 MiB). Use aihost_attn_forward with a reserved context for larger batches or contexts",
+                 need, kNoAllocScratchBytes);
   if (!q || !k_new || !v_new || !k_cache || !v_cache || !seq_len || !out)
     return api_fail(AIHOST_EINVAL, "q, k_new, v_new, k_cache, v_cache, seq_len and out must be non-NULL");
   for (const void* p : {q, k_new, v_new, static_cast<const void*>(k_cache), static_cast<const void*>(v_cache),
@@ -95,12 +112,6 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
       if (h_seq_len[b] < 0 || static_cast<int64_t>(h_seq_len[b]) + 1 > desc->kv_capacity)
         return api_fail(AIHOST_EINVAL, "sequence %d: %d cached rows + 1 exceed kv_capacity %d", b, h_seq_len[b],
                      desc->kv_capacity);
-  const size_t need = decode_scratch_bytes(batch, desc->n_q_heads, desc->head_dim, max_splits);
-  if (need > kNoAllocScratchBytes)
-    return api_fail(AIHOST_ENOMEM,
-                 "aihost_attn_decode_noalloc: this call needs %zu bytes of split scratch; the static array holds "
-                 "%zu (8 MiB). Use aihost_attn_forward with a reserved context for larger batches or contexts",
-                 need, kNoAllocScratchBytes);
   uint8_t* base = nullptr;
   s = scratch_address(dev, &base);
   if (s != AIHOST_OK) return s;
@@ -109,9 +120,6 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "cudaMemsetAsync(status): %s", cudaGetErrorString(e));
 
-  e = launch_kv_append(k_new, v_new, desc->q_dtype, k_cache, v_cache, kv, seq_len, batch, 1, desc->n_kv_heads,
-                       desc->head_dim, desc->rope_mode, freqs, status, st);
-  if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "kv append launch: %s", cudaGetErrorString(e));
   DecodeArgs a;
   memset(&a, 0, sizeof(a));
   a.q = q;
@@ -130,12 +138,17 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   a.freqs = freqs;
   a.chunk = chunk;
   a.max_splits = max_splits;
-  float* part = reinterpret_cast<float*>(base + kStatusBytes);
+  float* part = reinterpret_cast<float*>(base + kStatusBytes + kCounterBytes);
   a.part_o = part;
   a.part_ml = part + static_cast<size_t>(batch) * desc->n_q_heads * max_splits * desc->head_dim;
   a.out = out;
   a.out_dtype = desc->out_dtype;
   a.status = status;
+  a.k_new = k_new;  // appended by the decode kernel itself, or by the append kernel first
+  a.v_new = v_new;
+  a.new_dtype = desc->q_dtype;
+  a.counters = reinterpret_cast<unsigned long long*>(base + kStatusBytes);
+  a.epoch = next_epoch(dev);
   e = launch_decode_any(a, st, nullptr);
   if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "decode launch: %s", cudaGetErrorString(e));
   return AIHOST_OK;

@@ -98,13 +98,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (a.n_new + kBM - 1) / kBM;
-  const int h = blockIdx.y, b = blockIdx.z;
+  // grid: (sequence x head, work rank) with the heads fastest, so CTAs dispatch in order of
+  // decreasing causal work across all heads and sequences
+  const int h = static_cast<int>(blockIdx.x) % a.n_q_heads, b = static_cast<int>(blockIdx.x) / a.n_q_heads;
   const int kvh = h / (a.n_q_heads / a.n_kv_heads);
   // Pair mode: adjacent query tiles 2x and 2x+1 (B absent past the end), both groups read the
   // same K/V tile j. Split mode: both groups take query tile x, group A cache tiles [0, n/2),
   // group B [n/2, n), merged at the end. The longest work launches first in both.
   const bool split = a.split_kv != 0;
-  const int x = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
+  const int x = static_cast<int>(gridDim.y) - 1 - static_cast<int>(blockIdx.y);
   const int qt[2] = {split ? x : 2 * x, split ? x : 2 * x + 1};
   const bool has_b = split || qt[1] < n_qt;
   const int32_t start = a.seq_len ? a.seq_len[b] : a.start_scalar;
@@ -164,12 +166,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       tma_prefetch_desc(&a.q_map);
       tma_prefetch_desc(&a.k_map);
       tma_prefetch_desc(&a.v_map);
+      // Q may be read before the preceding kernel finishes when that kernel does not write it;
+      // the cache rows (appended or staged by the preceding kernel) only after griddep_wait.
       const int n_q_tiles = has_b && !split ? 2 : 1;
-      mbar_arrive_expect_tx(&bar.q_full, n_q_tiles * C::TILE_BYTES);
-      for (int t = 0; t < n_q_tiles; ++t)
-        for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d((t ? q_s[1] : q_s[0]) + kb * kBM * 128, &a.q_map, &bar.q_full, kb * 64, h,
-                      (t ? qt[1] : qt[0]) * kBM, b);
+      auto load_q = [&] {
+        mbar_arrive_expect_tx(&bar.q_full, n_q_tiles * C::TILE_BYTES);
+        for (int t = 0; t < n_q_tiles; ++t)
+          for (int kb = 0; kb < C::KB; ++kb)
+            tma_load_4d((t ? q_s[1] : q_s[0]) + kb * kBM * 128, &a.q_map, &bar.q_full, kb * 64, h,
+                        (t ? qt[1] : qt[0]) * kBM, b);
+      };
+      if (a.q_early) load_q();
+      griddep_wait();
+      if (!a.q_early) load_q();
       for (int g = 0; g < n_load; ++g) {
         // cache tile of load g: pair mode g; split mode A's g/2, B's, then B's last
         const int tile = !split ? g : g < 2 * n_kv[0] ? ((g & 1) ? kv_lo[1] : 0) + (g >> 1) : g;
@@ -329,22 +338,51 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       const int qb = split ? 0 : t;
       ok = mbar_wait(&bar.q_full, 0, status);
       if (ok && a.rope_mode != AIHOST_ROPE_NONE) {
+        // whole 16-byte chunks of the swizzled row (8 consecutive elements): a quarter-warp's
+        // 8 rows hit 8 distinct bank groups. In split mode each group rotates half the chunks.
         const float pos = static_cast<float>(qpos);
+        auto rot = [&](uint32_t& w1, uint32_t& w2, int pair) {  // w1 / w2: the pair's two halves
+          float sn, cs;
+          sincos_reduced(pos * a.freqs.f[pair], &sn, &cs);
+          const float x1 = __half2float(*reinterpret_cast<const __half*>(&w1));
+          const float x2 = __half2float(*reinterpret_cast<const __half*>(&w2));
+          const __half y1 = __float2half_rn(x1 * cs - x2 * sn), y2 = __float2half_rn(x1 * sn + x2 * cs);
+          w1 = __half_as_ushort(y1);
+          w2 = __half_as_ushort(y2);
+        };
+        constexpr int NC = D / 8;  // 16-byte chunks per row
+        if (a.rope_mode == AIHOST_ROPE_NEOX) {  // chunk c pairs with chunk c + NC/2, element by element
+          const int c0 = split ? t * (NC / 4) : 0, c1 = split ? c0 + NC / 4 : NC / 2;
+          for (int c = c0; c < c1; ++c) {
+            uint4* pa = reinterpret_cast<uint4*>(q_tile + sw128_off(r, 8 * c, kBM));
+            uint4* pb = reinterpret_cast<uint4*>(q_tile + sw128_off(r, 8 * (c + NC / 2), kBM));
+            uint4 va = *pa, vb = *pb;
+            uint32_t* ua = reinterpret_cast<uint32_t*>(&va);
+            uint32_t* ub = reinterpret_cast<uint32_t*>(&vb);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          if (split && half != t) continue;
+            for (int k = 0; k < 4; ++k) {
+              uint32_t a0 = ua[k] & 0xffffu, a1 = ua[k] >> 16, b0 = ub[k] & 0xffffu, b1 = ub[k] >> 16;
+              rot(a0, b0, 8 * c + 2 * k);
+              rot(a1, b1, 8 * c + 2 * k + 1);
+              ua[k] = a0 | (a1 << 16);
+              ub[k] = b0 | (b1 << 16);
+            }
+            *pa = va;
+            *pb = vb;
+          }
+        } else {  // interleaved: the 4 pairs (2i, 2i + 1) of a chunk sit in its four 32-bit words
+          const int c0 = split ? t * (NC / 2) : 0, c1 = split ? c0 + NC / 2 : NC;
+          for (int c = c0; c < c1; ++c) {
+            uint4* pc = reinterpret_cast<uint4*>(q_tile + sw128_off(r, 8 * c, kBM));
+            uint4 v = *pc;
+            uint32_t* u = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
-          for (int pp = 0; pp < D / 4; ++pp) {
-            const int pair = half * (D / 4) + pp;
-            const int c1 = a.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
-            const int c2 = a.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
-            __half* p1 = reinterpret_cast<__half*>(q_tile + sw128_off(r, c1, kBM));
-            __half* p2 = reinterpret_cast<__half*>(q_tile + sw128_off(r, c2, kBM));
-            const float x1 = __half2float(*p1), x2 = __half2float(*p2);
-            float sn, cs;
-            sincos_reduced(pos * a.freqs.f[pair], &sn, &cs);
-            *p1 = __float2half_rn(x1 * cs - x2 * sn);
-            *p2 = __float2half_rn(x1 * sn + x2 * cs);
+            for (int k = 0; k < 4; ++k) {
+              uint32_t lo = u[k] & 0xffffu, hi = u[k] >> 16;
+              rot(lo, hi, 4 * c + k);
+              u[k] = lo | (hi << 16);
+            }
+            *pc = v;
           }
         }
       }
@@ -523,9 +561,20 @@ cudaError_t launch_d(const PrefillArgs& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int n_qt = (a.n_new + kBM - 1) / kBM;
-  dim3 grid(a.split_kv ? n_qt : (n_qt + 1) / 2, a.n_q_heads, a.batch);
-  kern<<<grid, kThreads, C::SMEM, st>>>(a);
-  return cudaGetLastError();
+  // programmatic launch: the CTAs' set-up overlaps the tail of the kernel before (append or
+  // staging), which signals griddepcontrol.launch_dependents; the producer waits for it in full
+  // before reading the cache
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_q_heads * a.batch, a.split_kv ? n_qt : (n_qt + 1) / 2, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace

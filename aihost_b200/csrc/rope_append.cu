@@ -10,20 +10,13 @@
 //                      q = roundf(x * (1/d)), d stored as fp16).
 // stage_q_kernel / stage_kv_kernel: fp32 Q and fp32 / Q8_0 cache rows converted to fp16 for
 //                      the tensor-core prefill (the reference computes those in fp32 shaders).
-// Rotation arithmetic uses explicitly rounded multiplies/adds (no FMA contraction), so a
-// kernel and a CPU restatement that see the same cos/sin produce the same bits.
+// Row RoPE and storage conversion live in rows.cuh (shared with the decode kernels).
 #include "common.cuh"
 #include "kernels.h"
+#include "rows.cuh"
 
 namespace aihost {
 namespace {
-
-__device__ __forceinline__ void rotate_pair(float& x1, float& x2, float c, float s) {
-  const float a = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-  const float b = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
-  x1 = a;
-  x2 = b;
-}
 
 template <typename T>
 __global__ void rope_full_kernel(T* __restrict__ x, int32_t seq, int32_t n_heads, int32_t head_dim,
@@ -48,35 +41,6 @@ __global__ void rope_full_kernel(T* __restrict__ x, int32_t seq, int32_t n_heads
   }
 }
 
-// RoPE of one head row held by a warp (lane l holds elements [l*E, l*E+E), E = D/32) at
-// position `pos`. Interleaved pairs (2i, 2i+1) sit in one lane; NEOX pairs (i, i + D/2) sit in
-// lanes l and l ^ 16.
-template <int E>
-__device__ __forceinline__ void rope_row_warp(float (&x)[E], int32_t lane, float pos, int32_t rope_mode,
-                                              const RopeFreqs& freqs) {
-  if (rope_mode == AIHOST_ROPE_INTERLEAVED) {
-#pragma unroll
-    for (int e = 0; e < E; e += 2) {
-      const int pair = (lane * E + e) >> 1;
-      float sn, cs;
-      sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
-      rotate_pair(x[e], x[e + 1], cs, sn);
-    }
-  } else if (rope_mode == AIHOST_ROPE_NEOX) {
-    const bool lo = lane < 16;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
-      const int pair = (lane & 15) * E + e;
-      float sn, cs;
-      sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
-      float x1 = lo ? x[e] : other, x2 = lo ? other : x[e];
-      rotate_pair(x1, x2, cs, sn);
-      x[e] = lo ? x1 : x2;
-    }
-  }
-}
-
 __device__ __forceinline__ float load_in(const float* p) { return *p; }
 __device__ __forceinline__ float load_in(const __half* p) { return __half2float(*p); }
 
@@ -88,6 +52,7 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
                                  const int32_t* __restrict__ seq_len, int32_t batch, int32_t n_new,
                                  int32_t n_kv_heads, int32_t rope_mode, RopeFreqs freqs, int32_t* status) {
   constexpr int E = D / 32;
+  griddep_launch_dependents();  // the prefill that follows may start its own set-up now
   const int32_t lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t rows = static_cast<int64_t>(batch) * n_new * n_kv_heads;
@@ -111,37 +76,8 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
 
   uint8_t* dst = (is_k ? k_cache : v_cache) + b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride +
                  static_cast<int64_t>(h) * kv.head_stride;
-  if (kv.dtype == AIHOST_F32) {
-    float* d = reinterpret_cast<float*>(dst) + lane * E;
-#pragma unroll
-    for (int e = 0; e < E; ++e) d[e] = x[e];
-  } else if (kv.dtype == AIHOST_F16) {
-    __half* d = reinterpret_cast<__half*>(dst) + lane * E;
-#pragma unroll
-    for (int e = 0; e < E; ++e) d[e] = __float2half_rn(x[e]);
-  } else {  // Q8_0: 32 values per block = 32/E lanes
-    constexpr int LPB = 32 / E;
-    float amax = 0.0f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) amax = fmaxf(amax, fabsf(x[e]));
-#pragma unroll
-    for (int off = 1; off < LPB; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    const float dsc = __fdiv_rn(amax, 127.0f);
-    const float id = dsc != 0.0f ? __frcp_rn(dsc) : 0.0f;
-    const int blk = lane / LPB, sub = lane % LPB;
-    // Every field is stored with 16-bit stores: the row base, the 34-byte block stride and the
-    // 2-byte scale are all even, so each pair of bytes is 2-byte aligned.
-    uint16_t* bp = reinterpret_cast<uint16_t*>(dst + blk * 34);
-    if (sub == 0) bp[0] = __half_as_ushort(__float2half_rn(dsc));
-#pragma unroll
-    for (int e = 0; e < E; e += 2) {
-      const uint32_t q0 = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[e], id))));
-      const uint32_t q1 = static_cast<uint8_t>(static_cast<int8_t>(roundf(__fmul_rn(x[e + 1], id))));
-      bp[1 + (sub * E + e) / 2] = static_cast<uint16_t>(q0 | (q1 << 8));
-    }
-  }
+  store_row_warp<E>(x, lane, dst, kv.dtype);
 }
-
 
 // fp16 staging for the tensor-core prefill, whose operands are fp16 (fp32 accumulation).
 // stage_q_kernel: q [B][S][Hq][D] fp32 -> fp16, rotated at position start_b + s on the way (one
@@ -151,6 +87,7 @@ __global__ void stage_q_kernel(const float* __restrict__ q, __half* __restrict__
                                int32_t start_scalar, int32_t batch, int32_t n_q, int32_t n_heads, int32_t rope_mode,
                                RopeFreqs freqs) {
   constexpr int E = D / 32;
+  griddep_launch_dependents();  // the prefill that follows may start its own set-up now
   const int32_t lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= static_cast<int64_t>(batch) * n_q * n_heads) return;
@@ -178,6 +115,7 @@ __global__ void stage_kv_kernel(const uint8_t* __restrict__ k_cache, const uint8
                                 const int32_t* __restrict__ seq_len, int32_t start_scalar, int32_t len_offset,
                                 int32_t batch, int32_t n_kv_heads) {
   constexpr int E = D / 32;
+  griddep_launch_dependents();  // the prefill that follows may start its own set-up now
   const int32_t lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= static_cast<int64_t>(batch) * rows * n_kv_heads) return;

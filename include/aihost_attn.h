@@ -159,7 +159,8 @@ aihost_status aihost_attn_profiler_reset(aihost_attn_ctx* ctx);
  * (n_new == 1: RoPE, KV append, split-K attention, split merge) for hosts that cannot allocate
  * device memory when they decode (their allocator is taken by a pool, or may not be entered on
  * the token path). It needs no context and allocates nothing: the split scratch is a static
- * 8 MiB array that every GPU loading this library holds until the process exits. Calls whose
+ * 8 MiB array (plus 512 KiB of split-merge counters) that every GPU loading this library holds
+ * until the process exits. Calls whose
  * split scratch, batch * n_q_heads * splits * (head_dim + 2) * 4 bytes, exceeds 8 MiB return
  * AIHOST_ENOMEM. Runs on the current CUDA device. The first call on each device looks up the
  * array's device address: make it before any stream capture. All calls share the array, so

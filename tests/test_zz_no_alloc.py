@@ -76,10 +76,12 @@ def test_noalloc_matches_forward_on_two_calls_in_a_row(ctx):
 
 def test_noalloc_refuses_requests_past_its_static_scratch():
     torch.cuda.set_device(0)
-    cfg = CONFIGS[3]  # 64 sequences of up to 8193 rows: ~18 MB of split scratch > 8 MiB
-    spec = cfg.spec(8193)
-    d = spec.desc()
-    st = lib().aihost_attn_decode_noalloc(ctypes.byref(d), cfg.batch, 16, 16, 16, 16, 16, 16, None, 16, None)
+    # 1024 sequences x 32 query heads need 1024 * 32 * (128 + 2) * 4 bytes = 17 MB of partials even
+    # with a single split: more than the 8 MiB array under any split plan. The size is checked
+    # before the pointers, and the pointers are NULL, so no kernel can be launched either way.
+    d = CONFIGS[3].scaled(batch=1024).spec(8193).desc()
+    st = lib().aihost_attn_decode_noalloc(ctypes.byref(d), 1024, None, None, None, None, None, None, None, None,
+                                          None)
     assert st == ENOMEM
     assert b"8 MiB" in lib().aihost_attn_last_error()
     assert st != OK

@@ -65,6 +65,13 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
+// Transpose of an 8x8 matrix of 16-bit elements held one 32-bit pair per lane in the mma
+// fragment layout (lane 4r + c holds row r, columns 2c and 2c + 1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
 
 // Shared-memory byte address of fp16 element (row, col) of a 64-row tile written by TMA with
 // 128-byte swizzle (16-byte chunk index XOR row % 8; 64-column blocks of 64 * 128 bytes).
@@ -109,6 +116,119 @@ __device__ __forceinline__ bool split_arrive(unsigned long long* c, uint32_t epo
   atomicOr(status, kStatusWaitTimeout);
   return false;
 }
+
+// Output of one split (compute warps, after each warp has put its per-head (max, sum) at
+// merge[(warp * 16 + head) * 2] and its unnormalised O row at o_s[(warp * 16 + head) * (D + 8)]):
+// the four warps merged per head, then either the output (one split), or the split's partial
+// and, when this split is the last of its (sequence, head group) to finish, the merged output.
+template <int D>
+__device__ __forceinline__ void decode_emit(const DecodeArgs& p, float* merge, int h0, int g_count, int b, int split,
+                                            int n_splits) {
+  constexpr int OP = D + 8;
+  float* ml_s = merge;
+  float* o_s = ml_s + kComputeWarps * 16 * 2;
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (int idx = threadIdx.x; idx < g_count * D; idx += kComputeWarps * 32) {
+    const int g = idx / D, d = idx % D;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kComputeWarps; ++w) m = fmaxf(m, ml_s[(w * 16 + g) * 2]);
+    float l = 0.0f, acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kComputeWarps; ++w) {
+      const float wt = ex2_approx(ml_s[(w * 16 + g) * 2] - m);
+      l = fmaf(ml_s[(w * 16 + g) * 2 + 1], wt, l);
+      acc = fmaf(o_s[(w * 16 + g) * OP + d], wt, acc);
+    }
+    const int h = h0 + g;
+    if (n_splits == 1) {
+      const float v = acc / l;
+      const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * D + d;
+      if (p.out_dtype == AIHOST_F32) static_cast<float*>(p.out)[oidx] = v;
+      else static_cast<__half*>(p.out)[oidx] = __float2half_rn(v);
+    } else {
+      const int64_t pidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * p.max_splits + split;
+      p.part_o[pidx * D + d] = acc;
+      if (d == 0) {
+        p.part_ml[pidx * 2] = m;
+        p.part_ml[pidx * 2 + 1] = l;
+      }
+    }
+  }
+  if (n_splits == 1 || !p.counters) return;
+  // ---- fused combine: the last split of this (sequence, head group) to finish merges them all
+  __shared__ int s_last;
+  __threadfence();
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (threadIdx.x == 0)
+    s_last = split_arrive(&p.counters[static_cast<int64_t>(b) * gridDim.y + blockIdx.y], p.epoch, n_splits, p.status);
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (!s_last) return;
+  __threadfence();
+  // per-(head, split) weights 2^(m_s - m) / l first (one thread per head), then every output
+  // element as a weighted sum of the splits' partial O, four columns per thread
+  float* wts = ml_s;  // [16 heads][max_splits <= kMergeSplits], reusing the merge buffer
+  constexpr int kMergeSplits = 64;
+  const bool fits = p.max_splits <= kMergeSplits;
+  if (fits && threadIdx.x < g_count) {
+    const int64_t base = (static_cast<int64_t>(b) * p.n_q_heads + h0 + threadIdx.x) * p.max_splits;
+    float m = -INFINITY;
+    for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, __ldcg(&p.part_ml[(base + sp) * 2]));
+    float l = 0.0f;
+    for (int sp = 0; sp < n_splits; ++sp) {
+      const float w = exp2f(__ldcg(&p.part_ml[(base + sp) * 2]) - m);
+      wts[threadIdx.x * kMergeSplits + sp] = w;
+      l = fmaf(__ldcg(&p.part_ml[(base + sp) * 2 + 1]), w, l);
+    }
+    const float inv = 1.0f / l;
+    for (int sp = 0; sp < n_splits; ++sp) wts[threadIdx.x * kMergeSplits + sp] *= inv;
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (int idx = threadIdx.x; idx < g_count * (D / 4); idx += kComputeWarps * 32) {
+    const int g = idx / (D / 4), d = (idx % (D / 4)) * 4;
+    const int64_t base = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * p.max_splits;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (fits) {
+      for (int sp = 0; sp < n_splits; ++sp) {
+        const float w = wts[g * kMergeSplits + sp];
+        const float4 o4 = __ldcg(reinterpret_cast<const float4*>(&p.part_o[(base + sp) * D + d]));
+        acc.x = fmaf(o4.x, w, acc.x);
+        acc.y = fmaf(o4.y, w, acc.y);
+        acc.z = fmaf(o4.z, w, acc.z);
+        acc.w = fmaf(o4.w, w, acc.w);
+      }
+    } else {  // more splits than the weight table holds: weights recomputed per element
+      float m = -INFINITY;
+      for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, __ldcg(&p.part_ml[(base + sp) * 2]));
+      float l = 0.0f;
+      for (int sp = 0; sp < n_splits; ++sp) {
+        const float w = exp2f(__ldcg(&p.part_ml[(base + sp) * 2]) - m);
+        l = fmaf(__ldcg(&p.part_ml[(base + sp) * 2 + 1]), w, l);
+        const float4 o4 = __ldcg(reinterpret_cast<const float4*>(&p.part_o[(base + sp) * D + d]));
+        acc.x = fmaf(o4.x, w, acc.x);
+        acc.y = fmaf(o4.y, w, acc.y);
+        acc.z = fmaf(o4.z, w, acc.z);
+        acc.w = fmaf(o4.w, w, acc.w);
+      }
+      const float inv = 1.0f / l;
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
+    }
+    const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D + d;
+    if (p.out_dtype == AIHOST_F32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oidx) = acc;
+    } else {
+      const __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t*>(&lo);
+      u.y = *reinterpret_cast<const uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + oidx) = u;
+    }
+  }
+}
+
 
 // Compute-warp half of both kernels (warps 0-3): streams the fp16 K/V tiles of ring `full` /
 // `empty` (NS stages of TILE_BYTES each at k_off / v_off), keeps (max, sum, O) per query row in
@@ -257,106 +377,137 @@ __device__ __forceinline__ void decode_compute(const DecodeArgs& p, uint8_t* sme
     for (int h = 0; h < 2; ++h)
       *reinterpret_cast<float2*>(&o_s[(warp * 16 + grp + 8 * h) * OP + nb * 8 + 2 * tig]) =
           make_float2(o[nb][2 * h], o[nb][2 * h + 1]);
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  for (int idx = threadIdx.x; idx < g_count * D; idx += kComputeWarps * 32) {
-    const int g = idx / D, d = idx % D;
-    float m = -INFINITY;
+  decode_emit<D>(p, merge, h0, g_count, b, split, n_splits);
+}
+
+// Transposed compute for a head group of at most 8 query heads (warps 0-3). The heads are the
+// N = 8 columns of every m16n8k16 MMA instead of padded M = 16 rows: S^T = K Q^T (M = the warp's
+// 16 cache rows) and O^T = V^T P^T (M = 16 head dimensions), which halves the MMAs and the O
+// registers. P^T reaches the B-fragment layout of the P.V product through two movmatrix
+// transposes of the S^T accumulators.
+template <int D, int NS, bool ZERO_V>
+__device__ __forceinline__ void decode_compute_t(const DecodeArgs& p, uint8_t* smem, int k_off, int v_off,
+                                                 uint64_t* full, uint64_t* empty, const __half* q_s, float* merge,
+                                                 int n, int n_tiles, int h0, int g_count, int b, int split,
+                                                 int n_splits) {
+  constexpr int KB = D / 64;
+  constexpr int TILE_BYTES = KB * kTileRows * 128;
+  constexpr int QROW = D + 8;
+  constexpr int OP = D + 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t k_base = smem_u32(smem + k_off), v_base = smem_u32(smem + v_off);
+  const int grp = lane >> 2, tig = lane & 3;
+  const int mi = lane >> 3, r8 = lane & 7;
+  // Q^T as B fragments (k = head dims, n = heads 0-7): qb[kk] covers dims [16kk, 16kk + 16)
+  uint32_t qb[D / 16][2];
+  {
+    const uint32_t qbase = smem_u32(q_s);
 #pragma unroll
-    for (int w = 0; w < kComputeWarps; ++w) m = fmaxf(m, ml_s[(w * 16 + g) * 2]);
-    float l = 0.0f, acc = 0.0f;
+    for (int kk = 0; kk < D / 16; kk += 2)
+      ldsm_x4(qbase + (r8 * QROW + kk * 16 + 8 * mi) * 2, qb[kk][0], qb[kk][1], qb[kk + 1][0], qb[kk + 1][1]);
+  }
+  const float sl2 = p.scale * kLog2e;
+  // per thread: heads 2tig and 2tig + 1
+  float m_run[2] = {-1e30f, -1e30f}, l_run[2] = {0.0f, 0.0f};
+  float o[D / 16][4];  // O^T: dims 16mt + grp (+8), heads 2tig (+1)
 #pragma unroll
-    for (int w = 0; w < kComputeWarps; ++w) {
-      const float wt = ex2_approx(ml_s[(w * 16 + g) * 2] - m);
-      l = fmaf(ml_s[(w * 16 + g) * 2 + 1], wt, l);
-      acc = fmaf(o_s[(w * 16 + g) * OP + d], wt, acc);
+  for (int mt = 0; mt < D / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
+
+  bool ok = true;
+  for (int i = 0; i < n_tiles && ok; ++i) {
+    const int s = i % NS;
+    if (!mbar_wait(&full[s], (i / NS) & 1, p.status)) { ok = false; break; }
+    const uint32_t kt = k_base + s * TILE_BYTES, vt = v_base + s * TILE_BYTES;
+    const int r0 = warp * 16;  // this warp's 16 rows of the tile
+    // ---- S^T = K Q^T: rows r0..r0+15 of the tile (keys) x 8 heads
+    float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(sw_addr(kt, r0 + r8 + 8 * (mi & 1), kk * 16 + 8 * (mi >> 1)), a0, a1, a2, a3);
+      mma16816(sacc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
     }
-    const int h = h0 + g;
-    if (n_splits == 1) {
-      const float v = acc / l;
-      const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * D + d;
-      if (p.out_dtype == AIHOST_F32) static_cast<float*>(p.out)[oidx] = v;
-      else static_cast<__half*>(p.out)[oidx] = __float2half_rn(v);
-    } else {
-      const int64_t pidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * p.max_splits + split;
-      p.part_o[pidx * D + d] = acc;
-      if (d == 0) {
-        p.part_ml[pidx * 2] = m;
-        p.part_ml[pidx * 2 + 1] = l;
+    // ---- mask rows past the split's end; online softmax per head (column) over the warp's rows
+    const int base_row = i * kTileRows + r0;
+    const bool lo_ok = base_row + grp < n, hi_ok = base_row + grp + 8 < n;
+    const float s0 = lo_ok ? sacc[0] * sl2 : -INFINITY, s1 = lo_ok ? sacc[1] * sl2 : -INFINITY;
+    const float s2 = hi_ok ? sacc[2] * sl2 : -INFINITY, s3 = hi_ok ? sacc[3] * sl2 : -INFINITY;
+    float mt[2] = {fmaxf(s0, s2), fmaxf(s1, s3)};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 4));
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 8));
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 16));
+    }
+    float f[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float m_new = fmaxf(m_run[h], mt[h]);
+      f[h] = ex2_approx(m_run[h] - m_new);
+      m_run[h] = m_new;
+      l_run[h] *= f[h];
+    }
+#pragma unroll
+    for (int m2 = 0; m2 < D / 16; ++m2) {
+      o[m2][0] *= f[0];
+      o[m2][1] *= f[1];
+      o[m2][2] *= f[0];
+      o[m2][3] *= f[1];
+    }
+    const float p0 = ex2_approx(s0 - m_run[0]), p1 = ex2_approx(s1 - m_run[1]);
+    const float p2 = ex2_approx(s2 - m_run[0]), p3 = ex2_approx(s3 - m_run[1]);
+    l_run[0] += p0 + p2;
+    l_run[1] += p1 + p3;
+    // P^T as B fragments: transpose the (rows x heads) 8x8 blocks into (heads x rows) order
+    const uint32_t pb0 = movmatrix_trans(pack_h2(p0, p1)), pb1 = movmatrix_trans(pack_h2(p2, p3));
+    // ---- rows past the split's end may hold stale bits (NaN patterns included); P is 0 there,
+    // but 0 * NaN is NaN, so the warp zeroes its own V rows beyond n before reading them
+    if (ZERO_V && base_row + 16 > n) {
+      uint8_t* vrow0 = smem + v_off + s * TILE_BYTES;
+      for (int c = lane; c < 16 * KB * 8; c += 32) {
+        const int rr = c / (KB * 8), ch = c % (KB * 8);
+        if (base_row + rr >= n)
+          *reinterpret_cast<uint4*>(vrow0 + (ch >> 3) * (kTileRows * 128) + (r0 + rr) * 128 + (ch & 7) * 16) =
+              make_uint4(0, 0, 0, 0);
       }
+      __syncwarp();
+    }
+    // ---- O^T += V^T P^T: dims in 16-row blocks (ldmatrix.trans of V gives the A fragments)
+#pragma unroll
+    for (int m2 = 0; m2 < D / 16; ++m2) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(sw_addr(vt, r0 + r8 + 8 * (mi >> 1), m2 * 16 + 8 * (mi & 1)), a0, a1, a2, a3);
+      mma16816(o[m2], a0, a1, a2, a3, pb0, pb1);
+    }
+    __syncwarp();
+    if (ZERO_V && base_row + 16 > n) fence_proxy_async_smem();  // zeroed rows are rewritten by TMA later
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ---- per-head sums over the warp's rows (lanes sharing tig), then through shared memory
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 4);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 8);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 16);
+  }
+  // all tiles consumed: `merge` reuses ring memory no producer can target any more
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  float* ml_s = merge;
+  float* o_s = ml_s + kComputeWarps * 16 * 2;
+  if (grp == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ml_s[(warp * 16 + 2 * tig + h) * 2] = m_run[h];
+      ml_s[(warp * 16 + 2 * tig + h) * 2 + 1] = l_run[h];
     }
   }
-  if (n_splits == 1 || !p.counters) return;
-  // ---- fused combine: the last split of this (sequence, head group) to finish merges them all
-  __shared__ int s_last;
-  __threadfence();
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (threadIdx.x == 0)
-    s_last = split_arrive(&p.counters[static_cast<int64_t>(b) * gridDim.y + blockIdx.y], p.epoch, n_splits, p.status);
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (!s_last) return;
-  __threadfence();
-  // per-(head, split) weights 2^(m_s - m) / l first (one thread per head), then every output
-  // element as a weighted sum of the splits' partial O, four columns per thread
-  float* wts = ml_s;  // [16 heads][max_splits <= kMergeSplits], reusing the merge buffer
-  constexpr int kMergeSplits = 64;
-  const bool fits = p.max_splits <= kMergeSplits;
-  if (fits && threadIdx.x < g_count) {
-    const int64_t base = (static_cast<int64_t>(b) * p.n_q_heads + h0 + threadIdx.x) * p.max_splits;
-    float m = -INFINITY;
-    for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, __ldcg(&p.part_ml[(base + sp) * 2]));
-    float l = 0.0f;
-    for (int sp = 0; sp < n_splits; ++sp) {
-      const float w = exp2f(__ldcg(&p.part_ml[(base + sp) * 2]) - m);
-      wts[threadIdx.x * kMergeSplits + sp] = w;
-      l = fmaf(__ldcg(&p.part_ml[(base + sp) * 2 + 1]), w, l);
-    }
-    const float inv = 1.0f / l;
-    for (int sp = 0; sp < n_splits; ++sp) wts[threadIdx.x * kMergeSplits + sp] *= inv;
-  }
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  for (int idx = threadIdx.x; idx < g_count * (D / 4); idx += kComputeWarps * 32) {
-    const int g = idx / (D / 4), d = (idx % (D / 4)) * 4;
-    const int64_t base = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * p.max_splits;
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (fits) {
-      for (int sp = 0; sp < n_splits; ++sp) {
-        const float w = wts[g * kMergeSplits + sp];
-        const float4 o4 = __ldcg(reinterpret_cast<const float4*>(&p.part_o[(base + sp) * D + d]));
-        acc.x = fmaf(o4.x, w, acc.x);
-        acc.y = fmaf(o4.y, w, acc.y);
-        acc.z = fmaf(o4.z, w, acc.z);
-        acc.w = fmaf(o4.w, w, acc.w);
-      }
-    } else {  // more splits than the weight table holds: weights recomputed per element
-      float m = -INFINITY;
-      for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, __ldcg(&p.part_ml[(base + sp) * 2]));
-      float l = 0.0f;
-      for (int sp = 0; sp < n_splits; ++sp) {
-        const float w = exp2f(__ldcg(&p.part_ml[(base + sp) * 2]) - m);
-        l = fmaf(__ldcg(&p.part_ml[(base + sp) * 2 + 1]), w, l);
-        const float4 o4 = __ldcg(reinterpret_cast<const float4*>(&p.part_o[(base + sp) * D + d]));
-        acc.x = fmaf(o4.x, w, acc.x);
-        acc.y = fmaf(o4.y, w, acc.y);
-        acc.z = fmaf(o4.z, w, acc.z);
-        acc.w = fmaf(o4.w, w, acc.w);
-      }
-      const float inv = 1.0f / l;
-      acc.x *= inv;
-      acc.y *= inv;
-      acc.z *= inv;
-      acc.w *= inv;
-    }
-    const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D + d;
-    if (p.out_dtype == AIHOST_F32) {
-      *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oidx) = acc;
-    } else {
-      const __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
-      uint2 u;
-      u.x = *reinterpret_cast<const uint32_t*>(&lo);
-      u.y = *reinterpret_cast<const uint32_t*>(&hi);
-      *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + oidx) = u;
-    }
-  }
+#pragma unroll
+  for (int m2 = 0; m2 < D / 16; ++m2)
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      o_s[(warp * 16 + 2 * tig + (e & 1)) * OP + m2 * 16 + grp + 8 * (e >> 1)] = o[m2][e];
+  decode_emit<D>(p, merge, h0, g_count, b, split, n_splits);
 }
 
 // Q rows of the group, rotated at the new token's position, as fp16 rows of QROW elements
@@ -394,7 +545,8 @@ __device__ __forceinline__ void load_q_rows(const DecodeArgs& p, __half* q_s, in
   }
 }
 
-template <int D>
+// TR: the transposed compute for head groups of at most 8 query heads.
+template <int D, bool TR>
 __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_constant__ DecodeMmaArgs a) {
   using C = DecodeCfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -455,9 +607,14 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
     }
     return;
   }
-  decode_compute<D, C::NS, true>(p, smem, C::K_OFF, C::V_OFF, bar.full, bar.empty, q_s,
-                                 reinterpret_cast<float*>(smem + C::K_OFF), n, n_tiles, h0, g_count, b, split,
-                                 n_splits);
+  if constexpr (TR)
+    decode_compute_t<D, C::NS, true>(p, smem, C::K_OFF, C::V_OFF, bar.full, bar.empty, q_s,
+                                     reinterpret_cast<float*>(smem + C::K_OFF), n, n_tiles, h0, g_count, b, split,
+                                     n_splits);
+  else
+    decode_compute<D, C::NS, true>(p, smem, C::K_OFF, C::V_OFF, bar.full, bar.empty, q_s,
+                                   reinterpret_cast<float*>(smem + C::K_OFF), n, n_tiles, h0, g_count, b, split,
+                                   n_splits);
 }
 
 // ------------------------------------------------------------------ GGUF Q8_0 caches
@@ -541,7 +698,7 @@ __device__ __forceinline__ void q8_row_to_f16(const uint32_t (&w)[Q8Cfg<D>::BOX_
   }
 }
 
-template <int D>
+template <int D, bool TR>
 __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_constant__ DecodeMmaArgs a) {
   using C = Q8Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -651,15 +808,21 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
     }
     return;
   }
-  decode_compute<D, C::NSF, false>(p, smem, C::F_OFF, C::F_OFF + C::NSF * C::F_TILE, bar.f_full, bar.f_empty, q_s,
-                                   reinterpret_cast<float*>(smem + C::F_OFF), n, n_tiles, h0, g_count, b, split,
-                                   n_splits);
+  if constexpr (TR)
+    decode_compute_t<D, C::NSF, false>(p, smem, C::F_OFF, C::F_OFF + C::NSF * C::F_TILE, bar.f_full, bar.f_empty,
+                                       q_s, reinterpret_cast<float*>(smem + C::F_OFF), n, n_tiles, h0, g_count, b,
+                                       split, n_splits);
+  else
+    decode_compute<D, C::NSF, false>(p, smem, C::F_OFF, C::F_OFF + C::NSF * C::F_TILE, bar.f_full, bar.f_empty,
+                                     q_s, reinterpret_cast<float*>(smem + C::F_OFF), n, n_tiles, h0, g_count, b,
+                                     split, n_splits);
 }
 
 template <int D>
 cudaError_t launch_q8(const DecodeMmaArgs& a, cudaStream_t st) {
   using C = Q8Cfg<D>;
-  auto kern = decode_q8_kernel<D>;
+  const bool tr = a.base.n_q_heads / a.base.n_kv_heads <= 8;
+  auto kern = tr ? decode_q8_kernel<D, true> : decode_q8_kernel<D, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int G = a.base.n_q_heads / a.base.n_kv_heads;
@@ -671,7 +834,8 @@ cudaError_t launch_q8(const DecodeMmaArgs& a, cudaStream_t st) {
 template <int D>
 cudaError_t launch_d(const DecodeMmaArgs& a, cudaStream_t st) {
   using C = DecodeCfg<D>;
-  auto kern = decode_mma_kernel<D>;
+  const bool tr = a.base.n_q_heads / a.base.n_kv_heads <= 8;
+  auto kern = tr ? decode_mma_kernel<D, true> : decode_mma_kernel<D, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int G = a.base.n_q_heads / a.base.n_kv_heads;

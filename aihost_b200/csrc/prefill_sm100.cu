@@ -36,8 +36,11 @@ constexpr int kBN = 128;  // cache rows per tile
 // setmaxnreg); WG1 / WG2 = softmax groups A / B (224 registers: a full 128-column score row
 // stays in registers). 128*56 + 256*224 = 384*168 = the launch's register file.
 constexpr int kThreads = 384;
-constexpr uint32_t kRegsWG0 = 56;
-constexpr uint32_t kRegsSoftmax = 224;
+// setmaxnreg split of the 168 x 384 registers the CTA launches with: producer / MMA warpgroup
+// 72, each softmax warpgroup 216 (128 * 72 + 2 * 128 * 216 = 168 * 384).
+constexpr uint32_t kRegsWG0 = 72;
+constexpr uint32_t kRegsSoftmax = 216;
+static_assert(128 * kRegsWG0 + 2 * 128 * kRegsSoftmax <= 168 * kThreads, "setmaxnreg split exceeds the launch");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -76,6 +79,7 @@ struct Barriers {
   uint64_t q_full;
   uint64_t q_ready[2], s_full[2], p_full[2], o_full[2];
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
+  uint64_t s_free[2], pv_done[2];  // P in shared memory: S read into registers / P.V complete
   uint64_t v_fix;  // last V tile's rows past the sequence end have been zeroed
   uint32_t tmem_base;
 };
@@ -140,6 +144,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       mbar_init(&bar.s_full[t], 1);
       mbar_init(&bar.p_full[t], 128);
       mbar_init(&bar.o_full[t], 1);
+      mbar_init(&bar.s_free[t], 128);
+      mbar_init(&bar.pv_done[t], 1);
     }
     mbar_init(&bar.v_fix, 1);
     for (int i = 0; i < C::NS; ++i) {
@@ -264,7 +270,33 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           }
         }
         const int steps = max(n_kv[0], n_kv[1]);
-        for (int j = 0; ok && j < steps; ++j) {
+        for (int j = 0; ok && C::P_SMEM && j < steps; ++j) {
+          // P in shared memory: each group's next QK^T as soon as it has read S(j), ahead of P.V(j)
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (!ok || j + 1 >= n_kv[t]) continue;
+            const int gk = load_index(t, j + 1), sk = gk % C::NS;
+            if (!mbar_wait(&bar.s_free[t], j & 1, status)) { ok = false; break; }
+            if (!mbar_wait(&bar.k_full[sk], (gk / C::NS) & 1, status)) { ok = false; break; }
+            tc_fence_after();
+            issue_qk(t, sk);
+            umma_commit(&bar.k_empty[sk]);
+          }
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (!ok || j >= n_kv[t]) continue;
+            const int gv = load_index(t, j), sv = gv % C::NS;
+            if (!mbar_wait(&bar.v_full[sv], (gv / C::NS) & 1, status)) { ok = false; break; }
+            if (gv == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
+            if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, j, sv);
+            umma_commit(&bar.pv_done[t]);
+            umma_commit(&bar.v_empty[sv]);
+            if (j + 1 == n_kv[t]) umma_commit(&bar.o_full[t]);
+          }
+        }
+        for (int j = 0; ok && !C::P_SMEM && j < steps; ++j) {
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (!ok || j >= n_kv[t]) continue;
@@ -294,7 +326,38 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         if (ok && n_kv[1] > 0) issue_qk(1, 0);
         if (ok) umma_commit(&bar.k_empty[0]);
       }
-      for (int j = 0; !split && ok && j < n_load; ++j) {
+      for (int j = 0; !split && ok && C::P_SMEM && j < n_load; ++j) {
+        const int s = j % C::NS;
+        const int s1 = (j + 1) % C::NS;
+        // P in shared memory: the next QK^T (K tile j + 1, shared by both groups) as soon as each
+        // group has read S(j), ahead of P.V(j)
+        if (j + 1 < n_load) {
+          if (!mbar_wait(&bar.k_full[s1], ((j + 1) / C::NS) & 1, status)) { ok = false; break; }
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (!ok || j + 1 >= n_kv[t]) continue;
+            if (!mbar_wait(&bar.s_free[t], j & 1, status)) { ok = false; break; }
+            tc_fence_after();
+            issue_qk(t, s1);
+          }
+          if (!ok) break;
+          umma_commit(&bar.k_empty[s1]);
+        }
+        if (!mbar_wait(&bar.v_full[s], (j / C::NS) & 1, status)) { ok = false; break; }
+        if (j == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (!ok || j >= n_kv[t]) continue;
+          if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j, s);
+          umma_commit(&bar.pv_done[t]);
+          if (j + 1 == n_kv[t]) umma_commit(&bar.o_full[t]);
+        }
+        if (!ok) break;
+        umma_commit(&bar.v_empty[s]);
+      }
+      for (int j = 0; !split && ok && !C::P_SMEM && j < n_load; ++j) {
         const int s = j % C::NS;
         const int s1 = (j + 1) % C::NS;
         // operands first (normally long resident), then the softmax hand-offs
@@ -401,6 +464,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, sr[c]);
       tmem_wait_ld();
+      if constexpr (C::P_SMEM) {  // S is in registers: the next QK^T may overwrite it
+        tc_fence_before();
+        mbar_arrive(&bar.s_free[t]);
+      }
       const int kv0 = (kv_first + j) * kBN;
       const bool need_mask = __any_sync(0xffffffffu, kv0 + kBN - 1 > limit);
       if (need_mask) {
@@ -423,8 +490,32 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       const float m_new = fmaxf(m, mx * sl2);
       const bool resc = m_new > m + kRescaleThreshold;
       const float f = resc ? ex2_approx(m - m_new) : 1.0f;
-      // O holds the P.V sums of tiles < j, complete because this tile's S was committed after
-      // them. The vote keeps the tcgen05.ld/st warp-collective; rows that keep their max use f = 1.
+      if (resc) {
+        l *= f;
+        m = m_new;
+      }
+      // P = 2^(s*scale*log2e - m) in fp16 (masked entries: 2^-inf = 0), from S in registers
+      const float neg_m = -m;
+      float rsp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      uint32_t pk[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), sl2, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), sl2, neg_m));
+          rsp[i & 3] += p0 + p1;
+          pk[c][i] = pack_half2(p0, p1);
+        }
+      l += (rsp[0] + rsp[1]) + (rsp[2] + rsp[3]);
+      // O and (shared-memory) P of the previous tile: with P in shared memory the previous P.V may
+      // still be running (the next QK^T was issued ahead of it), so wait for it; otherwise this
+      // tile's S was committed after it, which already orders it.
+      if constexpr (C::P_SMEM) {
+        if (j > 0 && !mbar_wait(&bar.pv_done[t], (j - 1) & 1, status)) { ok = false; break; }
+        tc_fence_after();
+      }
+      // The vote keeps the tcgen05.ld/st warp-collective; rows that keep their max use f = 1.
       if (j > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -436,24 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           tmem_st32(o_tmem + c * 32, o);
         }
       }
-      if (resc) {
-        l *= f;
-        m = m_new;
-      }
-      // P = 2^(s*scale*log2e - m) in fp16 (masked entries: 2^-inf = 0), written over the first
-      // 64 columns of this tile's S, which are already in registers.
-      const float neg_m = -m;
-      float rsp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), sl2, neg_m));
-          rsp[i & 3] += p0 + p1;
-          pk[i] = pack_half2(p0, p1);
-        }
         if constexpr (C::P_SMEM) {
           // row r of the K-major SW128 P tile: 16-byte chunk (c*2 + q) of key block c/2
 #pragma unroll
@@ -461,18 +536,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             const int ch = (c & 1) * 4 + q * 2;  // 16-byte chunk index within the 128-byte row
             uint8_t* row = p_tile + (c >> 1) * (kBM * 128) + r * 128;
             *reinterpret_cast<uint4*>(row + (((ch) ^ (r & 7)) << 4)) =
-                make_uint4(pk[8 * q], pk[8 * q + 1], pk[8 * q + 2], pk[8 * q + 3]);
+                make_uint4(pk[c][8 * q], pk[c][8 * q + 1], pk[c][8 * q + 2], pk[c][8 * q + 3]);
             *reinterpret_cast<uint4*>(row + (((ch + 1) ^ (r & 7)) << 4)) =
-                make_uint4(pk[8 * q + 4], pk[8 * q + 5], pk[8 * q + 6], pk[8 * q + 7]);
+                make_uint4(pk[c][8 * q + 4], pk[c][8 * q + 5], pk[c][8 * q + 6], pk[c][8 * q + 7]);
           }
         } else {
-          tmem_st16(s_tmem + c * 16, pk);
+          tmem_st16(s_tmem + c * 16, pk[c]);  // over the first 64 columns of this tile's S
         }
       }
-      const float rs = (rsp[0] + rsp[1]) + (rsp[2] + rsp[3]);
-      l += rs;
       if constexpr (C::P_SMEM) fence_proxy_async_smem();
-      else tmem_wait_st();
+      tmem_wait_st();  // the O rescale (and TMEM P) complete before the next P.V reads them
       tc_fence_before();
       mbar_arrive(&bar.p_full[t]);
     }

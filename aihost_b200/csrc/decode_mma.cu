@@ -818,10 +818,278 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
                                      split, n_splits);
 }
 
+// ------------------------------------------------------------------ Q8_0, head groups of <= 8
+// K straight from the raw tiles: the compute warps turn each 2-byte pair of int8 into an exact
+// fp16 pair in registers (the A fragments of S^T = K Q^T), keep one fp32 accumulator per
+// 32-element block and apply each row's fp16 block scale in fp32 (exactly the dequantise-then-
+// dot sum, up to fp32 rounding). Only V, whose A fragments need a transpose, goes through the
+// fp16 tiles, written by two converter warps (one V row per thread). A producer warp issues
+// the TMA loads (a raw slot is free once the compute warps have read its K and the converters
+// its V). The freed shared memory holds a 4-deep raw ring.
+constexpr int kQ8kConvWarps = 2;
+constexpr int kQ8kThreads = (kComputeWarps + kQ8kConvWarps + 1) * 32;
+
+template <int D>
+struct Q8kCfg {
+  using B = Q8Cfg<D>;
+  static constexpr int NSR = 4;                               // raw K+V ring depth
+  static constexpr int NSF = 2;                               // fp16 V ring depth
+  static constexpr int RAW_OFF = 0;                           // K raw [NSR], then V raw [NSR]
+  static constexpr int F_OFF = (2 * NSR * B::RAW_TILE + 1023) / 1024 * 1024;  // V fp16 [NSF]
+  static constexpr int Q_OFF = F_OFF + NSF * B::F_TILE;
+  static constexpr int BAR_OFF = Q_OFF + B::Q_BYTES;
+  static constexpr int SMEM = BAR_OFF + 128 + 1024;
+  static_assert(2 * NSR * B::RAW_TILE >= B::MERGE_BYTES, "merge buffer reuses the raw ring");
+};
+
+template <int D>
+__global__ void __launch_bounds__(kQ8kThreads, 2) decode_q8k_kernel(const __grid_constant__ DecodeMmaArgs a) {
+  using C = Q8kCfg<D>;
+  using B = Q8Cfg<D>;
+  constexpr int ROW = B::ROW_BYTES;
+  constexpr int OP = D + 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Q8Bars& bar = *reinterpret_cast<Q8Bars*>(smem + C::BAR_OFF);
+  __half* q_s = reinterpret_cast<__half*>(smem + C::Q_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const DecodeArgs& p = a.base;
+  const int split = blockIdx.x;
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int kvh = blockIdx.y;  // one head group per KV head (G <= 8)
+  const int b = blockIdx.z;
+  const int g_count = G;
+  const int h0 = kvh * G;
+  const int32_t start = p.seq_len ? p.seq_len[b] : p.start_scalar;
+  const int32_t Lk = start + p.len_offset;
+  if (Lk > p.kv.capacity || Lk < 1) {
+    if (threadIdx.x == 0 && split == 0 && blockIdx.y == 0) atomicOr(p.status, kStatusBadLength);
+    return;
+  }
+  const int32_t t0 = split * p.chunk;
+  if (t0 >= Lk) return;
+  const int32_t n = min(p.chunk, Lk - t0);
+  const int n_tiles = (n + kTileRows - 1) / kTileRows;
+  const int n_splits = (Lk + p.chunk - 1) / p.chunk;
+  const int head_word = static_cast<int>(kvh * (p.kv.head_stride / 4));
+  const int box_x = head_word & ~3;
+  const int off = (head_word - box_x) * 4;  // byte offset of the head slice in a raw row
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NSR; ++i) {
+      mbar_init(&bar.raw_full[i], 1);
+      mbar_init(&bar.raw_empty[i], kQ8kConvWarps * 32 + kComputeWarps);  // V rows read + K reads done
+    }
+    for (int i = 0; i < C::NSF; ++i) {
+      mbar_init(&bar.f_full[i], kQ8kConvWarps * 32);
+      mbar_init(&bar.f_empty[i], kComputeWarps);
+    }
+    fence_mbar_init();
+  }
+  // the last split's CTA writes the new token's rows before any TMA reads them
+  if (p.fuse_append && t0 + p.chunk >= Lk && warp < 2) append_new_row<D>(p, b, kvh, Lk - 1, warp, lane);
+  load_q_rows<D>(p, q_s, b, h0, g_count, start, kQ8kThreads);
+  __syncthreads();
+
+  if (warp == kComputeWarps + kQ8kConvWarps) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&a.k_map);
+      tma_prefetch_desc(&a.v_map);
+      for (int i = 0; i < n_tiles; ++i) {
+        const int s = i % C::NSR;
+        if (!mbar_wait(&bar.raw_empty[s], ((i / C::NSR) & 1) ^ 1, p.status)) break;
+        mbar_arrive_expect_tx(&bar.raw_full[s], 2 * B::RAW_TILE);  // bytes the two boxes deliver
+        const int r = t0 + i * kTileRows;
+        tma_load_4d(smem + C::RAW_OFF + s * B::RAW_TILE, &a.k_map, &bar.raw_full[s], box_x, r, b, 0);
+        tma_load_4d(smem + C::RAW_OFF + (C::NSR + s) * B::RAW_TILE, &a.v_map, &bar.raw_full[s], box_x, r, b, 0);
+      }
+    }
+    return;
+  }
+  if (warp >= kComputeWarps) {
+    // ------------------------------------------------------------------ V converters
+    const int row = threadIdx.x - kComputeWarps * 32;  // 0..63
+    const int off_words = off / 4;
+    for (int i = 0; i < n_tiles; ++i) {
+      const int sr = i % C::NSR, sf = i % C::NSF;
+      if (!mbar_wait(&bar.raw_full[sr], (i / C::NSR) & 1, p.status)) break;
+      uint32_t w[B::BOX_WORDS];
+      const uint4* src = reinterpret_cast<const uint4*>(smem + C::RAW_OFF + (C::NSR + sr) * B::RAW_TILE + row * ROW);
+#pragma unroll
+      for (int c = 0; c < B::BOX_WORDS / 4; ++c) {
+        const uint4 v = src[c];
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+      mbar_arrive(&bar.raw_empty[sr]);
+      if (!mbar_wait(&bar.f_empty[sf], ((i / C::NSF) & 1) ^ 1, p.status)) break;
+      uint8_t* tile = smem + C::F_OFF + sf * B::F_TILE;
+      if (i * kTileRows + row < n) {
+        if constexpr (D == 128) {
+          if (off_words == 0) q8_row_to_f16<D, 0>(w, tile, row);
+          else q8_row_to_f16<D, 2>(w, tile, row);
+        } else {
+          switch (off_words) {
+            case 0: q8_row_to_f16<D, 0>(w, tile, row); break;
+            case 1: q8_row_to_f16<D, 1>(w, tile, row); break;
+            case 2: q8_row_to_f16<D, 2>(w, tile, row); break;
+            default: q8_row_to_f16<D, 3>(w, tile, row); break;
+          }
+        }
+      } else {  // rows past the split's end: zeros (their stale bytes could decode to NaN)
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c)
+          *reinterpret_cast<uint4*>(tile + (c >> 3) * (kTileRows * 128) + row * 128 + (((c & 7) ^ (row & 7)) << 4)) =
+              make_uint4(0, 0, 0, 0);
+      }
+      mbar_arrive(&bar.f_full[sf]);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ compute warps
+  constexpr int QROW = D + 8;
+  const int grp = lane >> 2, tig = lane & 3;
+  const int mi = lane >> 3, r8 = lane & 7;
+  uint32_t qb[D / 16][2];  // Q^T as B fragments, as in decode_compute_t
+  {
+    const uint32_t qbase = smem_u32(q_s);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; kk += 2)
+      ldsm_x4(qbase + (r8 * QROW + kk * 16 + 8 * mi) * 2, qb[kk][0], qb[kk][1], qb[kk + 1][0], qb[kk + 1][1]);
+  }
+  const __half2 k1152 = __floats2half2_rn(1152.0f, 1152.0f);
+  auto i8pair = [&](const uint8_t* p2) -> uint32_t {  // two int8 (2-byte aligned) -> exact fp16 pair
+    const uint32_t x = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(p2)) ^ 0x8080u;
+    const uint32_t e = __byte_perm(x, 0x64646464u, 0x4140);
+    const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&e), k1152);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  };
+  const float sl2 = p.scale * kLog2e;
+  float m_run[2] = {-1e30f, -1e30f}, l_run[2] = {0.0f, 0.0f};
+  float o[D / 16][4];
+#pragma unroll
+  for (int m2 = 0; m2 < D / 16; ++m2) o[m2][0] = o[m2][1] = o[m2][2] = o[m2][3] = 0.0f;
+  const uint32_t v_base = smem_u32(smem + C::F_OFF);
+
+  bool ok = true;
+  for (int i = 0; i < n_tiles && ok; ++i) {
+    const int sr = i % C::NSR, sf = i % C::NSF;
+    if (!mbar_wait(&bar.raw_full[sr], (i / C::NSR) & 1, p.status)) { ok = false; break; }
+    const int r0 = warp * 16;  // this warp's 16 rows of the tile
+    const uint8_t* k_lo = smem + C::RAW_OFF + sr * B::RAW_TILE + (r0 + grp) * ROW + off;  // row r0 + grp
+    const uint8_t* k_hi = k_lo + 8 * ROW;                                                   // row r0 + grp + 8
+    // ---- S^T = K Q^T, one accumulator per 32-element block, then the rows' block scales
+    float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int blk = 0; blk < D / 32; ++blk) {
+      float sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int cb = blk * 34 + 2 + h * 16 + 2 * tig;  // byte of dims (16h + 2tig, +1) of the block
+        mma16816(sb, i8pair(k_lo + cb), i8pair(k_hi + cb), i8pair(k_lo + cb + 8), i8pair(k_hi + cb + 8),
+                 qb[2 * blk + h][0], qb[2 * blk + h][1]);
+      }
+      const float d_lo = __half2float(*reinterpret_cast<const __half*>(k_lo + blk * 34));
+      const float d_hi = __half2float(*reinterpret_cast<const __half*>(k_hi + blk * 34));
+      sacc[0] = fmaf(d_lo, sb[0], sacc[0]);
+      sacc[1] = fmaf(d_lo, sb[1], sacc[1]);
+      sacc[2] = fmaf(d_hi, sb[2], sacc[2]);
+      sacc[3] = fmaf(d_hi, sb[3], sacc[3]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar.raw_empty[sr]);  // this warp's K reads are done
+    // ---- mask rows past the split's end (their raw bytes may be anything); online softmax
+    const int base_row = i * kTileRows + r0;
+    const bool lo_ok = base_row + grp < n, hi_ok = base_row + grp + 8 < n;
+    const float s0 = lo_ok ? sacc[0] * sl2 : -INFINITY, s1 = lo_ok ? sacc[1] * sl2 : -INFINITY;
+    const float s2 = hi_ok ? sacc[2] * sl2 : -INFINITY, s3 = hi_ok ? sacc[3] * sl2 : -INFINITY;
+    float mt[2] = {fmaxf(s0, s2), fmaxf(s1, s3)};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 4));
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 8));
+      mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 16));
+    }
+    float f[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float m_new = fmaxf(m_run[h], mt[h]);
+      f[h] = ex2_approx(m_run[h] - m_new);
+      m_run[h] = m_new;
+      l_run[h] *= f[h];
+    }
+#pragma unroll
+    for (int m2 = 0; m2 < D / 16; ++m2) {
+      o[m2][0] *= f[0];
+      o[m2][1] *= f[1];
+      o[m2][2] *= f[0];
+      o[m2][3] *= f[1];
+    }
+    const float p0 = ex2_approx(s0 - m_run[0]), p1 = ex2_approx(s1 - m_run[1]);
+    const float p2 = ex2_approx(s2 - m_run[0]), p3 = ex2_approx(s3 - m_run[1]);
+    l_run[0] += p0 + p2;
+    l_run[1] += p1 + p3;
+    const uint32_t pb0 = movmatrix_trans(pack_h2(p0, p1)), pb1 = movmatrix_trans(pack_h2(p2, p3));
+    // ---- O^T += V^T P^T from the converted fp16 V tile
+    if (!mbar_wait(&bar.f_full[sf], (i / C::NSF) & 1, p.status)) { ok = false; break; }
+    const uint32_t vt = v_base + sf * B::F_TILE;
+#pragma unroll
+    for (int m2 = 0; m2 < D / 16; ++m2) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(sw_addr(vt, r0 + r8 + 8 * (mi >> 1), m2 * 16 + 8 * (mi & 1)), a0, a1, a2, a3);
+      mma16816(o[m2], a0, a1, a2, a3, pb0, pb1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar.f_empty[sf]);
+  }
+
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 4);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 8);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 16);
+  }
+  // all tiles consumed (every raw slot's K and V were read): the raw ring holds the merge
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  float* merge = reinterpret_cast<float*>(smem + C::RAW_OFF);
+  float* ml_s = merge;
+  float* o_s = ml_s + kComputeWarps * 16 * 2;
+  if (grp == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ml_s[(warp * 16 + 2 * tig + h) * 2] = m_run[h];
+      ml_s[(warp * 16 + 2 * tig + h) * 2 + 1] = l_run[h];
+    }
+  }
+#pragma unroll
+  for (int m2 = 0; m2 < D / 16; ++m2)
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      o_s[(warp * 16 + 2 * tig + (e & 1)) * OP + m2 * 16 + grp + 8 * (e >> 1)] = o[m2][e];
+  decode_emit<D>(p, merge, h0, g_count, b, split, n_splits);
+}
+
+template <int D>
+cudaError_t launch_q8k(const DecodeMmaArgs& a, cudaStream_t st) {
+  using C = Q8kCfg<D>;
+  auto kern = decode_q8k_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.base.max_splits, a.base.n_kv_heads, a.base.batch);
+  kern<<<grid, kQ8kThreads, C::SMEM, st>>>(a);
+  return cudaGetLastError();
+}
+
 template <int D>
 cudaError_t launch_q8(const DecodeMmaArgs& a, cudaStream_t st) {
   using C = Q8Cfg<D>;
   const bool tr = a.base.n_q_heads / a.base.n_kv_heads <= 8;
+  if (tr) return launch_q8k<D>(a, st);
   auto kern = tr ? decode_q8_kernel<D, true> : decode_q8_kernel<D, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;

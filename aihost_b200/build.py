@@ -15,8 +15,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libaihost_attn.so"
-SOURCES = ["api.cu", "rope_append.cu", "decode.cu", "prefill_sm100.cu", "noalloc.cu", "decode_mma.cu"]
-HEADERS = ["common.cuh", "kernels.h"]
+SOURCES = ["api.cu", "rope_append.cu", "decode.cu", "prefill_sm100.cu", "noalloc.cu", "decode_mma.cu", "dist.cu"]
+HEADERS = ["common.cuh", "kernels.h", "rows.cuh"]
 
 
 def nvcc_path() -> str:
@@ -43,7 +43,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         "-Xcompiler", "-fPIC", "-shared",
         "-Xptxas", "-v" if verbose else "-O3",
         "-o", str(LIB) + ".tmp",
-    ] + [str(CSRC / s) for s in SOURCES]
+    ] + [str(CSRC / s) for s in SOURCES] + ["-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if verbose or res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)

@@ -66,6 +66,32 @@ class HeadShard:
         dist.all_gather_into_tensor(buf.view(-1), out_local.contiguous().view(-1), group=group)
         return buf
 
+    def forward(self, dist: "NcclDist", ops, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, cache,
+                out: torch.Tensor | None = None, layer: int = 0) -> torch.Tensor:
+        """This rank's heads of the fused layer step through aihost_attn_forward_sharded: RoPE,
+        append into the local cache, attention, then one NCCL all-gather of the head outputs.
+        q [B, S, Hq/N, d], k_new / v_new [B, S, Hkv/N, d] (this rank's slices), `cache` a
+        KVCache built with local_spec(). Returns the rank-major [N, B, S, Hq/N, d] buffer."""
+        import ctypes
+
+        from . import check, lib
+        from .ops import _ptr, _stream
+
+        ls = cache.spec
+        B, S = q.shape[0], q.shape[1]
+        if out is None:
+            odt = torch.float32 if ls.out_dtype == 0 else torch.float16
+            out = torch.empty((self.world, B, S, ls.n_q_heads, ls.head_dim), dtype=odt, device=q.device)
+        ops.ctx.reserve_for(ls, B, S)
+        d = ls.desc()
+        hl = (ctypes.c_int32 * B)(*cache.host_len) if cache.host_len is not None else None
+        check(lib().aihost_attn_forward_sharded(dist.handle, ops.ctx.handle, ctypes.byref(d), B, S, _ptr(q),
+                                                _ptr(k_new), _ptr(v_new), _ptr(cache.k[layer]), _ptr(cache.v[layer]),
+                                                _ptr(cache.seq_len),
+                                                ctypes.cast(hl, ctypes.c_void_p) if hl is not None else None,
+                                                _ptr(out), _stream(ops.stream)))
+        return out
+
     @staticmethod
     def to_reference_layout(gathered: torch.Tensor) -> torch.Tensor:
         """[N, B, S, Hq/N, d] -> [B, S, Hq, d]."""
@@ -73,4 +99,42 @@ class HeadShard:
         return gathered.permute(1, 2, 0, 3, 4).reshape(b, s, n * hq_l, d)
 
 
-__all__ = ["HeadShard"]
+class NcclDist:
+    """aihost_attn_dist: the library's NCCL communicator for one rank (one process per GPU)."""
+
+    def __init__(self, world: int, rank: int, nccl_id: bytes, device: int):
+        import ctypes
+
+        from . import check, lib
+
+        if len(nccl_id) != 128:
+            raise ValueError("an NCCL unique id is 128 bytes")
+        self._id = ctypes.create_string_buffer(nccl_id, 128)
+        self._h = ctypes.c_void_p()
+        check(lib().aihost_attn_dist_init(world, rank, self._id, device, ctypes.byref(self._h)))
+        self.world, self.rank = world, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        """A fresh NCCL id (made by one rank and handed to the others by the host)."""
+        import ctypes
+
+        from . import check, lib
+
+        buf = ctypes.create_string_buffer(128)
+        check(lib().aihost_attn_dist_unique_id(buf))
+        return buf.raw
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self) -> None:
+        from . import lib
+
+        if self._h:
+            lib().aihost_attn_dist_destroy(self._h)
+            self._h = None
+
+
+__all__ = ["HeadShard", "NcclDist"]

@@ -260,10 +260,26 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_head
     need_flush = w["bytes"] < 2 * 126e6  # L2 is 126 MB: flush unless the step streams more than 2x that
     flush = torch.empty(flush_bytes, dtype=torch.uint8, device=device) if need_flush else None
 
+    nccl = None
+    result = out
+    if shard is not None:
+        # the library's own NCCL communicator: aihost_attn_forward_sharded runs this rank's heads
+        # and all-gathers every rank's head outputs (rank-major) in one call
+        import torch.distributed as tdist
+
+        from aihost_b200.shard import NcclDist
+
+        idb = [NcclDist.unique_id() if rank == 0 else None]
+        if world > 1:
+            tdist.broadcast_object_list(idb, src=0)
+        nccl = NcclDist(world, rank, idb[0], device.index)
+        result = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=device)
+
     def step():
-        ops.attention_layer(q, kn, vn, cache, out=out)
-        if shard is not None and world > 1:
-            shard.gather(out)  # NCCL all-gather of every rank's head outputs (rank-major)
+        if nccl is not None:
+            shard.forward(nccl, ops, q, kn, vn, cache, out=result)
+        else:
+            ops.attention_layer(q, kn, vn, cache, out=out)
 
     for _ in range(warmup):
         if flush is not None:
@@ -301,7 +317,7 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_head
 
     # end to end: pinned host inputs -> device, fused call, result -> host, per step
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, kn, vn))
-    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    hout = torch.empty(result.shape, dtype=result.dtype, pin_memory=True)
     e_ms = []
     for i in range(steps + warmup):
         if flush is not None:
@@ -312,13 +328,16 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_head
         kn.copy_(hk, non_blocking=True)
         vn.copy_(hv, non_blocking=True)
         step()
-        hout.copy_(out, non_blocking=True)
+        hout.copy_(result, non_blocking=True)
         s1.record()
         s1.synchronize()
         if i >= warmup:
             e_ms.append(s0.elapsed_time(s1))
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
+    if nccl is not None:
+        torch.cuda.synchronize()
+        nccl.close()
     return dict(ms=ms, wall=wall, kern=kern, launches=launches, e2e_ms=e_ms, h2d=h2d, d2h=d2h, work=w,
                 lengths=lengths, flushed=need_flush, sharded=shard is not None)
 
@@ -356,7 +375,9 @@ def decode_kernel_name(cfg) -> str:
     """The decode kernel the library picks for this cache dtype (token-major default strides)."""
     from aihost_b200 import F16, Q8_0
 
-    return {F16: "decode_mma_kernel", Q8_0: "decode_q8_kernel"}.get(cfg.kv_dtype, "decode_splitk_kernel")
+    if cfg.kv_dtype == Q8_0:  # head groups of up to 8 read K straight from the raw tiles
+        return "decode_q8k_kernel" if cfg.n_q_heads // cfg.n_kv_heads <= 8 else "decode_q8_kernel"
+    return {F16: "decode_mma_kernel"}.get(cfg.kv_dtype, "decode_splitk_kernel")
 
 
 def summarize(cfg, r, n_gpus, dist_on, pk, pk_kind):
@@ -447,6 +468,12 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    # torchrun sets OMP_NUM_THREADS=1 per process; the CPU reference uses every host thread
+    # (read by the OpenMP runtime when the oracle library loads, which happens below)
+    os.environ["OMP_NUM_THREADS"] = str(len(os.sched_getaffinity(0)))
+    from oracle import oracle as orc
+
+    orc.set_num_threads(len(os.sched_getaffinity(0)))
     cfg = CONFIGS[args.config]
     per_step = max(1.0, min(6.0, 150.0 / max(1, args.steps + args.warmup)))
     times, units, meta = [], None, None

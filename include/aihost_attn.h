@@ -170,6 +170,27 @@ aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc, int32_t b
                                          const int32_t* seq_len, const int32_t* h_seq_len, void* out,
                                          void* stream);
 
+/* ---- KV-head sharding across GPUs (one process per GPU, NCCL over NVLink). Replaces the
+ * reference's layer split with host staging (Inference/MultiGPUTransformer.cs:48-183).
+ * Rank r of N owns KV heads [r*Hkv/N, (r+1)*Hkv/N) and their query heads, and a cache holding only
+ * those heads. NCCL is loaded at run time (libnccl.so.2); AIHOST_EUNSUPPORTED when absent. */
+typedef struct aihost_attn_dist aihost_attn_dist;
+/* One rank creates the 128-byte NCCL id and the host hands it to every rank. */
+aihost_status aihost_attn_dist_unique_id(void* out_id);
+/* Collective over all ranks (blocks until every rank has called it). */
+aihost_status aihost_attn_dist_init(int32_t world, int32_t rank, const void* nccl_id, int32_t device,
+                                    aihost_attn_dist** out);
+aihost_status aihost_attn_dist_destroy(aihost_attn_dist* dist);
+/* aihost_attn_forward of this rank's heads (`local`: n_q_heads = Hq/N, n_kv_heads = Hkv/N and the
+ * local cache layout), written into this rank's slot of out_gathered, then one in-place
+ * all-gather on `stream`: out_gathered is [N][batch][n_new][Hq/N][head_dim] (rank-major) on every
+ * rank. Every rank must make the same calls in the same order. */
+aihost_status aihost_attn_forward_sharded(aihost_attn_dist* dist, aihost_attn_ctx* ctx,
+                                          const aihost_attn_desc* local, int32_t batch, int32_t n_new,
+                                          const void* q, const void* k_new, const void* v_new,
+                                          void* k_cache, void* v_cache, const int32_t* seq_len,
+                                          const int32_t* h_seq_len, void* out_gathered, void* stream);
+
 /* Synchronise the context's device and read-and-clear the device status word that kernels
  * set when a bounded wait expired (AIHOST_ETIMEOUT) or a device-side length exceeded
  * kv_capacity (AIHOST_EINVAL). *out_bits receives the raw bits (may be NULL). */

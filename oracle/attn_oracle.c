@@ -22,6 +22,14 @@ int32_t oracle_num_threads(void) {
 #endif
 }
 
+void oracle_set_num_threads(int32_t n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 /* ---------------------------------------------------------------- fp16 <-> fp32 (IEEE RNE) */
 
 float oracle_f16_to_f32(uint16_t h) {

@@ -38,6 +38,7 @@ extern "C" {
 enum { ORACLE_FAITHFUL = 0, ORACLE_EXACT = 1 };
 
 int32_t oracle_num_threads(void);
+void oracle_set_num_threads(int32_t n); /* OpenMP threads of later calls (n > 0) */
 
 /* IEEE binary16 <-> binary32, round-to-nearest-even. */
 float oracle_f16_to_f32(uint16_t h);

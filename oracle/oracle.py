@@ -32,6 +32,7 @@ def lib() -> ctypes.CDLL:
         L = ctypes.CDLL(str(LIB_PATH))
         vp, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
         L.oracle_num_threads.restype = i32
+        L.oracle_set_num_threads.argtypes = [i32]
         L.oracle_f16_to_f32.argtypes, L.oracle_f16_to_f32.restype = [ctypes.c_uint16], f32
         L.oracle_f32_to_f16.argtypes, L.oracle_f32_to_f16.restype = [f32], ctypes.c_uint16
         L.oracle_f16_to_f32_n.argtypes = [vp, vp, i64]
@@ -57,6 +58,11 @@ def _p(a: np.ndarray) -> int:
 
 def num_threads() -> int:
     return lib().oracle_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    """OpenMP threads of later oracle calls."""
+    lib().oracle_set_num_threads(int(n))
 
 
 def f32_to_f16(x: np.ndarray) -> np.ndarray:

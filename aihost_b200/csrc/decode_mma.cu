@@ -102,8 +102,9 @@ __device__ __forceinline__ void append_new_row(const DecodeArgs& p, int b, int k
 }
 
 // Counts this split's arrival on an epoch-tagged counter (high 32 bits: the call's epoch, low:
-// arrivals); true for the last of n_splits arrivals of this call. A counter still holding an
-// earlier epoch restarts at 1. Never waits on another CTA; the CAS retries only on contention.
+// arrivals); true for the last of n_splits arrivals of this call, which then resets the counter
+// to zero. A counter still holding another epoch (left by a call that did not finish) restarts
+// at 1. Never waits on another CTA; the CAS retries only on contention.
 __device__ __forceinline__ bool split_arrive(unsigned long long* c, uint32_t epoch, int n_splits, int32_t* status) {
   unsigned long long cur = atomicAdd(c, 0ull);
   for (uint32_t it = 0; it < kMaxWaitIters; ++it) {
@@ -160,10 +161,13 @@ __device__ __forceinline__ void decode_emit(const DecodeArgs& p, float* merge, i
   __shared__ int s_last;
   __threadfence();
   asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (threadIdx.x == 0)
-    s_last = split_arrive(&p.counters[static_cast<int64_t>(b) * gridDim.y + blockIdx.y], p.epoch, n_splits, p.status);
+  unsigned long long* counter = &p.counters[static_cast<int64_t>(b) * gridDim.y + blockIdx.y];
+  if (threadIdx.x == 0) s_last = split_arrive(counter, p.epoch, n_splits, p.status);
   asm volatile("bar.sync 1, 128;" ::: "memory");
   if (!s_last) return;
+  // every split of this call has arrived: reset the counter, so that a replay of the same launch
+  // (a CUDA graph keeps its epoch argument) starts from zero again
+  if (threadIdx.x == 0) atomicExch(counter, 0ull);
   __threadfence();
   // per-(head, split) weights 2^(m_s - m) / l first (one thread per head), then every output
   // element as a weighted sum of the splits' partial O, four columns per thread

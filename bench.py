@@ -45,6 +45,9 @@ def parse_args():
     ap.add_argument("--shard", default="seq", choices=["seq", "heads"],
                     help="N>1: seq = every rank runs its own sequences (weak scaling); heads = the KV heads "
                          "of one problem are split over the ranks and the head outputs all-gathered (strong)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decode configs: also time a CUDA graph of this many layers with distinct caches "
+                         "(rotating caches: HBM throughput instead of single-call latency); adds a `layers` object")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N untimed fused calls of --config and exit (the command profiled with ncu)")
     return ap.parse_args()
@@ -361,6 +364,49 @@ def profile_steps(cfg, n, device):
         print(f"profiled config {cfg.number}: {n} calls, mean |out| {out.float().abs().mean().item():.4f}")
 
 
+def bench_layers(cfg, layers, steps, warmup, device, ctx):
+    """Decode throughput with rotating caches: one step is `layers` fused calls, each on its own
+    layer's cache (together larger than L2, so the bytes come from HBM), captured once in a CUDA
+    graph and replayed. Returns (ms per step, algorithmic bytes per step)."""
+    import torch
+
+    from aihost_b200.ops import ComputeOps, KVCache
+
+    inp = device_inputs(cfg, device, 0)
+    cache = KVCache(ctx, cfg.spec(inp["capacity"]), batch=cfg.batch, n_layers=layers, device=device)
+    for l in range(layers):
+        cache.k[l].copy_(inp["k_cache"])
+        cache.v[l].copy_(inp["v_cache"])
+    cache.seq_len, cache.host_len = inp["seq_len"], list(inp["lengths"])
+    q, kn, vn = inp["q"], inp["k_new"], inp["v_new"]
+    ops = ComputeOps(ctx)
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        out = ops.attention_layer(q, kn, vn, cache, layer=0)  # scratch reserved outside the capture
+        for l in range(layers):
+            ops.attention_layer(q, kn, vn, cache, layer=l, out=out)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for l in range(layers):
+            ops.attention_layer(q, kn, vn, cache, layer=l, out=out)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        a.record()
+        graph.replay()
+        b.record()
+    torch.cuda.synchronize()
+    ctx.sync_status()
+    ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+    w = work(cfg, inp["lengths"])
+    return ms, w["kernel_bytes"] * layers
+
+
 def max_over_ranks(x: float, dist_on: bool) -> float:
     if not dist_on:
         return x
@@ -570,6 +616,14 @@ def main():
         main_res["gpu_launches_decode"] = dec.pop("gpu_launches")
     clk = clocks.stop()
     cpu = None
+    layers_res = None
+    if args.layers > 0 and cfg.n_new == 1 and ws == 1:
+        l_ms, l_bytes = bench_layers(cfg, args.layers, max(args.steps, 10), args.warmup, device, ctx)
+        layers_res = {"layers": args.layers, "ms_per_step": l_ms, "tokens_per_s": cfg.batch / (l_ms * 1e-3),
+                      "kv_read_gbs": l_bytes / (l_ms * 1e-3) * 1e-9,
+                      "frac_of_measured_hbm": l_bytes / (l_ms * 1e-3) * 1e-9 / pk["hbm_gbs"],
+                      "note": "one CUDA graph of `layers` fused calls on distinct caches (HBM-resident), "
+                              "replayed per step; bytes = algorithmic bytes of every layer's call"}
     if rank == 0 and ws == 1 and not args.no_cpu:
         cpu = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -587,6 +641,8 @@ def main():
                 "wall_s_timed_region": r["wall"]}
         if dec is not None:
             line["decode"] = dec
+        if layers_res is not None:
+            line["layers"] = layers_res
         print(json.dumps(line), flush=True)
     ctx.close()
     if dist_on:

@@ -82,6 +82,7 @@ __device__ __forceinline__ uint32_t sw_addr(uint32_t tile, int row, int col) {
 struct DecBars {
   uint64_t full[6], empty[6];
 };
+static_assert(sizeof(DecBars) <= 128, "decode_mma_kernel reserves 128 bytes for its barriers");
 
 // The new token's K (warp 0, rotated) or V (warp 1) row of KV head kvh, written into cache row
 // t the way the append kernel writes it, then made visible to this CTA's later TMA reads.
@@ -657,7 +658,7 @@ struct Q8Cfg {
   static constexpr int Q_OFF = F_OFF + 2 * NSF * F_TILE;
   static constexpr int Q_BYTES = 16 * QROW * 2;
   static constexpr int BAR_OFF = Q_OFF + Q_BYTES;
-  static constexpr int SMEM = BAR_OFF + 128 + 1024;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;  // barriers, then alignment slack
   static constexpr int MERGE_BYTES = kComputeWarps * 16 * (D + 8 + 2) * 4;
   static_assert(2 * NSF * F_TILE >= MERGE_BYTES, "merge buffer reuses the fp16 rings");
   static_assert(NSR <= 4 && NSF <= 4, "barrier arrays hold four stages");
@@ -665,7 +666,9 @@ struct Q8Cfg {
 
 struct Q8Bars {
   uint64_t raw_full[4], raw_empty[4], f_full[4], f_empty[4];
+  uint64_t appended;  // decode_q8k_kernel: the new token's rows are in the cache
 };
+static_assert(sizeof(Q8Bars) <= 256, "Q8_0 kernels reserve 256 bytes for their barriers");
 
 // Converts one raw row (words w, head slice starting OFFW words in) into 16-byte fp16 chunks
 // of the swizzled tile row `row` at `tile`.
@@ -842,7 +845,7 @@ struct Q8kCfg {
   static constexpr int F_OFF = (2 * NSR * B::RAW_TILE + 1023) / 1024 * 1024;  // V fp16 [NSF]
   static constexpr int Q_OFF = F_OFF + NSF * B::F_TILE;
   static constexpr int BAR_OFF = Q_OFF + B::Q_BYTES;
-  static constexpr int SMEM = BAR_OFF + 128 + 1024;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;  // barriers, then alignment slack
   static_assert(2 * NSR * B::RAW_TILE >= B::MERGE_BYTES, "merge buffer reuses the raw ring");
 };
 
@@ -889,12 +892,18 @@ __global__ void __launch_bounds__(kQ8kThreads, 2) decode_q8k_kernel(const __grid
       mbar_init(&bar.f_full[i], kQ8kConvWarps * 32);
       mbar_init(&bar.f_empty[i], kComputeWarps);
     }
+    mbar_init(&bar.appended, 64);
     fence_mbar_init();
   }
-  // the last split's CTA writes the new token's rows before any TMA reads them
-  if (p.fuse_append && t0 + p.chunk >= Lk && warp < 2) append_new_row<D>(p, b, kvh, Lk - 1, warp, lane);
-  load_q_rows<D>(p, q_s, b, h0, g_count, start, kQ8kThreads);
   __syncthreads();
+  // The producer starts streaming at once; the compute warps rotate Q meanwhile. The last
+  // split's CTA writes the new token's rows first (warps 0 and 1); the producer waits for them
+  // only before the one tile that holds that row.
+  const bool appends = p.fuse_append && t0 + p.chunk >= Lk;
+  if (appends && warp < 2) {
+    append_new_row<D>(p, b, kvh, Lk - 1, warp, lane);
+    mbar_arrive(&bar.appended);
+  }
 
   if (warp == kComputeWarps + kQ8kConvWarps) {
     // ------------------------------------------------------------------ TMA producer
@@ -903,6 +912,7 @@ __global__ void __launch_bounds__(kQ8kThreads, 2) decode_q8k_kernel(const __grid
       tma_prefetch_desc(&a.v_map);
       for (int i = 0; i < n_tiles; ++i) {
         const int s = i % C::NSR;
+        if (appends && i == (Lk - 1 - t0) / kTileRows && !mbar_wait(&bar.appended, 0, p.status)) break;
         if (!mbar_wait(&bar.raw_empty[s], ((i / C::NSR) & 1) ^ 1, p.status)) break;
         mbar_arrive_expect_tx(&bar.raw_full[s], 2 * B::RAW_TILE);  // bytes the two boxes deliver
         const int r = t0 + i * kTileRows;
@@ -956,6 +966,8 @@ __global__ void __launch_bounds__(kQ8kThreads, 2) decode_q8k_kernel(const __grid
   }
 
   // ------------------------------------------------------------------ compute warps
+  load_q_rows<D>(p, q_s, b, h0, g_count, start, kComputeWarps * 32);
+  asm volatile("bar.sync 1, 128;" ::: "memory");
   constexpr int QROW = D + 8;
   const int grp = lane >> 2, tig = lane & 3;
   const int mi = lane >> 3, r8 = lane & 7;

@@ -83,6 +83,7 @@ struct Barriers {
   uint64_t v_fix;  // last V tile's rows past the sequence end have been zeroed
   uint32_t tmem_base;
 };
+static_assert(sizeof(Barriers) <= 256, "prefill_kernel reserves 256 bytes for its barriers");
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);

@@ -99,6 +99,92 @@ class HeadShard:
         return gathered.permute(1, 2, 0, 3, 4).reshape(b, s, n * hq_l, d)
 
 
+@dataclasses.dataclass
+class RowShard:
+    """Rank `rank` of `world`'s query rows of one sequence's causal prefill: n_new new rows after
+    `cached` rows. For layers with fewer KV heads than ranks (Hkv < N), where head sharding runs
+    out of heads: every rank appends all new K/V rows (replicated, a small fraction of the work),
+    each rank attends its own contiguous block of query rows over the cache, and the row blocks
+    are all-gathered. Block boundaries split the causal work, sum over rows i of (cached + i + 1)
+    keys, into equal parts, rounded to the prefill kernel's 128-row tiles."""
+
+    n_new: int
+    cached: int
+    rank: int
+    world: int
+    tile: int = 128
+
+    def pairs(self, k: int) -> float:
+        """Causal (query, key) pairs of rank k's block."""
+        a, b = self.boundary(k), self.boundary(k + 1)
+        return float(sum(self.cached + i + 1 for i in range(a, b)))
+
+    def boundary(self, k: int) -> int:
+        """First row of rank k's block (k = world gives n_new)."""
+        if k <= 0:
+            return 0
+        if k >= self.world:
+            return self.n_new
+        p, s = float(self.cached), float(self.n_new)
+        total = s * p + s * (s + 1) / 2
+        target = total * k / self.world
+        r = -(p + 0.5) + ((p + 0.5) ** 2 + 2 * target) ** 0.5  # r*p + r(r+1)/2 = target
+        r = int(round(r / self.tile)) * self.tile
+        return max(0, min(self.n_new, r))
+
+    @property
+    def rows(self) -> tuple[int, int]:
+        return self.boundary(self.rank), self.boundary(self.rank + 1)
+
+    @property
+    def max_rows(self) -> int:
+        return max(self.boundary(k + 1) - self.boundary(k) for k in range(self.world))
+
+    def forward(self, ops, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, cache, layer: int = 0,
+                group=None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's rows of the fused step for batch-1 inputs q [1, S, Hq, d], k_new / v_new
+        [1, S, Hkv, d] with `cache` holding `cached` rows (device and host lengths). Appends every
+        new row (RoPE'd K) to the cache, then returns the full output [1, S, Hq, d], gathered
+        from every rank's rows (world 1: computed locally), into `out` when given. The cache
+        lengths are not advanced."""
+        import torch.distributed as dist
+
+        spec = cache.spec
+        S, hq, hkv, d = q.shape[1], q.shape[2], k_new.shape[2], q.shape[3]
+        P = self.cached
+        theta, mode = spec.rope_theta, spec.rope_mode
+        kr = k_new.contiguous().clone()
+        if mode != 2:  # ROPE_NONE
+            ops.apply_rope_full(kr.view(S, hkv * d), P, hkv, d, theta, mode)
+        cache.add(layer, kr, v_new.contiguous())
+        a, b = self.rows
+        width = self.max_rows
+        odt = torch.float32 if spec.out_dtype == 0 else torch.float16
+        mine = torch.zeros(width, hq * d, dtype=odt, device=q.device)
+        if b > a:
+            qa = q[0, a:b].contiguous().clone()
+            if mode != 2:
+                ops.apply_rope_full(qa.view(b - a, hq * d), P + a, hq, d, theta, mode)
+            rb = hkv * d * (4 if spec.kv_dtype == 0 else 2)
+            kc = cache.k[layer][: (P + b) * rb].view(P + b, hkv * d)
+            vc = cache.v[layer][: (P + b) * rb].view(P + b, hkv * d)
+            kt = torch.float32 if spec.kv_dtype == 0 else torch.float16
+            mine[: b - a] = ops.multi_head_attention(qa.view(b - a, hq * d), kc.view(kt), vc.view(kt), hq,
+                                                     start_position=P + a, out_dtype=odt)
+        if self.world == 1:
+            gathered = mine.unsqueeze(0)
+        else:
+            gathered = torch.empty((self.world, width, hq * d), dtype=odt, device=q.device)
+            dist.all_gather_into_tensor(gathered.view(-1), mine.view(-1), group=group)
+        if out is None:
+            out = torch.empty(1, S, hq, d, dtype=odt, device=q.device)
+        for k in range(self.world):
+            a_k, b_k = self.boundary(k), self.boundary(k + 1)
+            if b_k > a_k:
+                out[0, a_k:b_k] = gathered[k, : b_k - a_k].view(b_k - a_k, hq, d)
+        return out
+
+
 class NcclDist:
     """aihost_attn_dist: the library's NCCL communicator for one rank (one process per GPU)."""
 
@@ -137,4 +223,4 @@ class NcclDist:
             self._h = None
 
 
-__all__ = ["HeadShard", "NcclDist"]
+__all__ = ["HeadShard", "RowShard", "NcclDist"]

@@ -42,9 +42,11 @@ def parse_args():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode object")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time")
-    ap.add_argument("--shard", default="seq", choices=["seq", "heads"],
+    ap.add_argument("--shard", default="seq", choices=["seq", "heads", "rows"],
                     help="N>1: seq = every rank runs its own sequences (weak scaling); heads = the KV heads "
-                         "of one problem are split over the ranks and the head outputs all-gathered (strong)")
+                         "of one problem are split over the ranks and the head outputs all-gathered (strong); "
+                         "rows = prefill configs: the query rows of one sequence are split into causal-balanced "
+                         "blocks and the row blocks all-gathered (strong; for Hkv < N)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decode configs: also time a CUDA graph of this many layers with distinct caches "
                          "(rotating caches: HBM throughput instead of single-call latency); adds a `layers` object")
@@ -239,7 +241,7 @@ def shard_inputs(cfg, device, rank, world):
     return inp, spec, shard, local
 
 
-def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_heads=False):
+def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode="seq"):
     import torch
 
     import aihost_b200 as A
@@ -247,11 +249,21 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_head
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if shard_heads:
+    rows = None
+    if shard_mode == "heads":
         inp, spec, shard, local_cfg = shard_inputs(cfg, device, rank, world)
     else:
-        inp = device_inputs(cfg, device, rank)
-        spec, shard, local_cfg = cfg.spec(inp["capacity"]), None, cfg
+        shard = None
+        if shard_mode == "rows":
+            from aihost_b200.shard import RowShard
+
+            if cfg.n_new == 1 or cfg.batch != 1:
+                raise SystemExit("--shard rows needs a single-sequence prefill config")
+            inp = device_inputs(cfg, device, 0)  # one problem, the same seeded inputs on every rank
+            rows = RowShard(cfg.n_new, inp["lengths"][0], rank, world)
+        else:
+            inp = device_inputs(cfg, device, rank)
+        spec, local_cfg = cfg.spec(inp["capacity"]), cfg
     lengths = inp["lengths"]
     cache = KVCache(ctx, spec, batch=cfg.batch, n_layers=1, device=device)
     cache.k[0], cache.v[0] = inp["k_cache"], inp["v_cache"]
@@ -281,6 +293,8 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_head
     def step():
         if nccl is not None:
             shard.forward(nccl, ops, q, kn, vn, cache, out=result)
+        elif rows is not None:
+            rows.forward(ops, q, kn, vn, cache, out=result)
         else:
             ops.attention_layer(q, kn, vn, cache, out=out)
 
@@ -317,6 +331,8 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_head
              ("prefill", A.KERNEL_PREFILL), ("convert", A.KERNEL_CONVERT))}
     ctx.sync_status()
     launches = sum(n for n, _ in kern.values())
+    if rows is not None:
+        launches += 2 * steps  # the two aihost_rope_full calls (K rows, this rank's Q rows) per step
 
     # end to end: pinned host inputs -> device, fused call, result -> host, per step
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, kn, vn))
@@ -342,7 +358,9 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_head
         torch.cuda.synchronize()
         nccl.close()
     return dict(ms=ms, wall=wall, kern=kern, launches=launches, e2e_ms=e_ms, h2d=h2d, d2h=d2h, work=w,
-                lengths=lengths, flushed=need_flush, sharded=shard is not None)
+                lengths=lengths, flushed=need_flush, sharded=shard is not None or rows is not None,
+                rank_flops=(4.0 * cfg.n_q_heads * cfg.head_dim * rows.pairs(rank) if rows is not None else None),
+                rank_rows=(rows.rows if rows is not None else None))
 
 
 def profile_steps(cfg, n, device):
@@ -435,14 +453,24 @@ def summarize(cfg, r, n_gpus, dist_on, pk, pk_kind):
         unit, per_step = "TFLOP/s", w["flops"] * 1e-12
     else:
         unit, per_step = "tokens/s", float(w["tokens"])
-    # FLOPs and bytes add up over ranks; under head sharding every rank serves the same tokens
-    ranks = 1 if (r.get("sharded") and not prefill) else n_gpus
+    # FLOPs and bytes add up over ranks under sequence sharding; a sharded problem counts once
+    # (head sharding of a decode: every rank serves the same tokens; row sharding: one prefill)
+    ranks = 1 if (r.get("sharded") and (not prefill or r.get("rank_flops") is not None)) else n_gpus
     value = ranks * per_step / (ms_step * 1e-3)
     e2e_value = ranks * per_step / (e2e_ms * 1e-3)
     kname = "prefill" if prefill else "decode"
     n_k, tot = r["kern"][kname]
     k_ms = max_over_ranks(tot / max(n_k, 1), dist_on)
-    if prefill:
+    if prefill and r.get("rank_flops") is not None:
+        # row sharding: each rank's kernel over its own causal pairs; the slowest rank's rate
+        k_local = tot / max(n_k, 1)
+        achieved = -max_over_ranks(-r["rank_flops"] / (k_local * 1e-3) * 1e-12, dist_on)
+        roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / pk["bf16_tflops"], "traffic": None, "kernel": "prefill_kernel",
+                "kernel_ms": k_ms, "algorithmic_per_launch": r["rank_flops"],
+                "peak_source": f"{pk_kind} bf16 burst", "note": "min over ranks of (rank's causal-pair FLOPs / "
+                "rank's mean prefill launch); algorithmic_per_launch is rank 0's"}
+    elif prefill:
         achieved = w["flops"] / (k_ms * 1e-3) * 1e-12
         roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / pk["bf16_tflops"], "traffic": None, "kernel": "prefill_kernel",
@@ -605,7 +633,8 @@ def main():
     cfg = CONFIGS[args.config]
     flush_bytes = 512 << 20
     heads = args.shard == "heads"
-    r = bench_ours(cfg, args.steps, args.warmup, device, ctx, flush_bytes, dist_on, shard_heads=heads)
+    row_mode = args.shard == "rows"
+    r = bench_ours(cfg, args.steps, args.warmup, device, ctx, flush_bytes, dist_on, shard_mode=args.shard)
     main_res = summarize(cfg, r, ws, dist_on, pk, pk_kind)
     dec = None
     if args.config == 2 and not args.no_decode:
@@ -629,12 +658,16 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": main_res["value"], "unit": main_res["unit"], "n_gpus": ws,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": main_res["ms_per_step"],
-                "higher_is_better": True, "scaling": "strong" if heads else "weak", "vs_baseline": None,
+                "higher_is_better": True, "scaling": "strong" if (heads or row_mode) else "weak",
+                "vs_baseline": None,
                 "dtype": "f16 (fp32 accumulate)" if cfg.q_dtype == 1 else "f32",
                 "data": "synthetic (seeded SplitMix64 + Box-Muller, no model weights)",
                 "config": {**cfg_desc(cfg, r["lengths"], r["flushed"]),
                            "parallelism": (f"KV heads split over {ws} ranks + NCCL all-gather of head outputs"
-                                           if heads else "one independent sequence set per rank")
+                                           if heads else
+                                           f"query rows split over {ws} ranks (causal-balanced 128-row blocks, "
+                                           f"rank 0 rows {r['rank_rows']}) + NCCL all-gather of row blocks"
+                                           if row_mode else "one independent sequence set per rank")
                            if ws > 1 else "single GPU"},
                 "roofline": main_res["roofline"], "cpu_baseline": cpu, "e2e": main_res["e2e"],
                 "gpu_launches": main_res["gpu_launches"], "clocks": clk, "kernels": main_res["kernels"],

@@ -104,3 +104,83 @@ def test_sharded_two_gpus_match_oracle(kv):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     err = q.get(timeout=5)
     assert isinstance(err, float) and err <= 2e-3, err
+
+
+# ---------------------------------------------------------------- query-row sharding (Hkv < N)
+
+def _row_cfg():
+    return CONFIGS[2].scaled(n_new=700, n_q_heads=4, n_kv_heads=2, head_dim=64, cached=None, cached_list=[200])
+
+
+def _row_run(rank, world, device, group=None):
+    from aihost_b200.ops import ComputeOps, Context, KVCache
+    from aihost_b200.shard import RowShard
+
+    torch.cuda.set_device(device)
+    dev = torch.device("cuda", device)
+    cfg = _row_cfg()
+    inp = make_inputs(cfg, capacity=1024)
+    ctx = Context(device)
+    try:
+        cache = KVCache(ctx, cfg.spec(1024), batch=1, device=dev)
+        cache.k[0] = inp["k_cache"].to(dev).clone()
+        cache.v[0] = inp["v_cache"].to(dev).clone()
+        cache.seq_len = inp["seq_len"].to(dev)
+        cache.host_len = list(inp["lengths"])
+        out = RowShard(cfg.n_new, 200, rank, world).forward(ComputeOps(ctx), inp["q"].to(dev), inp["k_new"].to(dev),
+                                                            inp["v_new"].to(dev), cache, group=group)
+        torch.cuda.synchronize()
+        ctx.sync_status()
+        return out.cpu().float().numpy(), inp
+    finally:
+        ctx.close()
+
+
+def test_row_shard_world_one_matches_oracle():
+    from helpers import max_abs, oracle_forward
+
+    got, inp = _row_run(0, 1, 0)
+    ref, _, _ = oracle_forward(_row_cfg(), inp)
+    assert max_abs(got, ref) <= 2e-3
+
+
+def _row_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        got, inp = _row_run(rank, world, rank)
+        if rank == 0:
+            from helpers import max_abs, oracle_forward
+
+            ref, _, _ = oracle_forward(_row_cfg(), inp)
+            q.put(max_abs(got, ref))
+    except Exception as e:
+        q.put(f"rank {rank}: {e!r}")
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_row_shard_two_gpus_match_oracle():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    sock = socket.socket()
+    sock.bind(("127.0.0.1", 0))
+    port = sock.getsockname()[1]
+    sock.close()
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    procs = [mpc.Process(target=_row_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    err = q.get(timeout=5)
+    assert isinstance(err, float) and err <= 2e-3, err

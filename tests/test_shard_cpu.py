@@ -84,3 +84,67 @@ def test_local_spec_pads_q8_token_stride():
     assert ls.kv_head_stride == 136 and ls.kv_token_stride == 144
     with pytest.raises(ValueError):
         HeadShard(CONFIGS[2].spec(2048), 0, 4)  # 2 KV heads over 4 ranks
+
+
+# ---------------------------------------------------------------- query-row sharding (Hkv < N)
+
+def test_row_boundaries_cover_rows_and_balance_causal_work():
+    from aihost_b200.shard import RowShard
+
+    for n_new, cached, world in [(2048, 0, 2), (2048, 0, 8), (32768, 0, 8), (1000, 3000, 4), (150, 100, 2)]:
+        bounds = [RowShard(n_new, cached, 0, world).boundary(k) for k in range(world + 1)]
+        assert bounds[0] == 0 and bounds[-1] == n_new and bounds == sorted(bounds)
+        assert all(b % 128 == 0 for b in bounds[:-1])
+        work = [sum(cached + i + 1 for i in range(bounds[k], bounds[k + 1])) for k in range(world)]
+        if n_new >= 128 * world * 4:  # enough tiles for the rounding to stay small
+            assert max(work) <= 1.25 * sum(work) / world, work
+
+
+def _row_worker(rank, world, port, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from aihost_b200.shard import RowShard
+        from oracle import oracle as orc
+
+        cfg = CONFIGS[2].scaled(n_new=300, n_q_heads=4, n_kv_heads=2, head_dim=64, q_dtype=F32, kv_dtype=F32,
+                                out_dtype=F32, cached=None, cached_list=[77])
+        cap = 400
+        inp = make_inputs(cfg, capacity=cap)
+        S, hq, hkv, d, P = cfg.n_new, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, 77
+        theta = cfg.spec(cap).rope_theta
+        sh = RowShard(S, P, rank, world)
+        # the CPU oracle stands in for the kernels: RoPE(K) + append on every rank, then this rank's rows
+        k = orc.rope_full(inp["k_new"].numpy()[0].reshape(S, hkv * d), P, hkv, d, theta)
+        kc = inp["k_cache"].numpy().view(np.float32).reshape(cap, hkv * d).copy()
+        vc = inp["v_cache"].numpy().view(np.float32).reshape(cap, hkv * d).copy()
+        kc[P:P + S] = k
+        vc[P:P + S] = inp["v_new"].numpy()[0].reshape(S, hkv * d)
+        a, b = sh.rows
+        mine = np.zeros((sh.max_rows, hq * d), dtype=np.float32)
+        if b > a:
+            qa = orc.rope_full(inp["q"].numpy()[0, a:b].reshape(b - a, hq * d), P + a, hq, d, theta)
+            mine[:b - a] = orc.mha(qa, kc[:P + b], vc[:P + b], hq, P + a)
+        g = [torch.zeros(sh.max_rows, hq * d) for _ in range(world)]
+        dist.all_gather(g, torch.from_numpy(mine))
+        out = np.concatenate([g[r].numpy()[:sh.boundary(r + 1) - sh.boundary(r)] for r in range(world)])
+        if rank == 0:
+            ref = orc.attn_forward(cfg.spec(cap).desc(), inp["q"].numpy(), inp["k_new"].numpy(), inp["v_new"].numpy(),
+                                   inp["k_cache"].numpy().copy(), inp["v_cache"].numpy().copy(), inp["seq_len"].numpy())
+            result_q.put(float(np.abs(out - ref.reshape(S, hq * d)).max()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_gather_matches_unsharded():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_row_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    err = q.get(timeout=5)
+    assert err <= 1e-5, err

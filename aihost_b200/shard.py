@@ -104,8 +104,8 @@ class RowShard:
     """Rank `rank` of `world`'s query rows of one sequence's causal prefill: n_new new rows after
     `cached` rows. For layers with fewer KV heads than ranks (Hkv < N), where head sharding runs
     out of heads: every rank appends all new K/V rows (replicated, a small fraction of the work),
-    each rank attends its own contiguous block of query rows over the cache, and the row blocks
-    are all-gathered. Block boundaries split the causal work, sum over rows i of (cached + i + 1)
+    each rank attends its own contiguous block of query rows over the cache, and each block is
+    broadcast from its owner into every rank's output. Block boundaries split the causal work, sum over rows i of (cached + i + 1)
     keys, into equal parts, rounded to the prefill kernel's 128-row tiles."""
 
     n_new: int
@@ -142,47 +142,58 @@ class RowShard:
 
     def forward(self, ops, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, cache, layer: int = 0,
                 group=None, out: torch.Tensor | None = None) -> torch.Tensor:
-        """This rank's rows of the fused step for batch-1 inputs q [1, S, Hq, d], k_new / v_new
-        [1, S, Hkv, d] with `cache` holding `cached` rows (device and host lengths). Appends every
-        new row (RoPE'd K) to the cache, then returns the full output [1, S, Hq, d], gathered
-        from every rank's rows (world 1: computed locally), into `out` when given. The cache
-        lengths are not advanced."""
+        """The fused step for batch-1 inputs q [1, S, Hq, d], k_new / v_new [1, S, Hkv, d], with
+        `cache` holding `cached` rows (device and host lengths), split over the ranks by query
+        rows. Every rank appends all S new rows (RoPE'd K) to its cache, runs the fused op
+        (aihost_attn_forward: RoPE of its Q rows in the kernel, causal attention) on its block
+        [a, b) as a call that starts at row cached + a, and the blocks are then broadcast from
+        their owners into `out` [1, S, Hq, d] (allocated when None) on every rank. `group` must
+        list the ranks 0..world-1 in order (None: the default group). The cache lengths are not
+        advanced."""
         import torch.distributed as dist
 
         spec = cache.spec
+        if spec.kv_dtype not in (0, 1):
+            raise ValueError("row sharding supports fp32 / fp16 caches")
         S, hq, hkv, d = q.shape[1], q.shape[2], k_new.shape[2], q.shape[3]
+        if S != self.n_new or q.shape[0] != 1:
+            raise ValueError(f"expected q [1, {self.n_new}, Hq, d], got {tuple(q.shape)}")
         P = self.cached
-        theta, mode = spec.rope_theta, spec.rope_mode
-        kr = k_new.contiguous().clone()
-        if mode != 2:  # ROPE_NONE
-            ops.apply_rope_full(kr.view(S, hkv * d), P, hkv, d, theta, mode)
-        cache.add(layer, kr, v_new.contiguous())
-        a, b = self.rows
-        width = self.max_rows
-        odt = torch.float32 if spec.out_dtype == 0 else torch.float16
-        mine = torch.zeros(width, hq * d, dtype=odt, device=q.device)
-        if b > a:
-            qa = q[0, a:b].contiguous().clone()
-            if mode != 2:
-                ops.apply_rope_full(qa.view(b - a, hq * d), P + a, hq, d, theta, mode)
-            rb = hkv * d * (4 if spec.kv_dtype == 0 else 2)
-            kc = cache.k[layer][: (P + b) * rb].view(P + b, hkv * d)
-            vc = cache.v[layer][: (P + b) * rb].view(P + b, hkv * d)
-            kt = torch.float32 if spec.kv_dtype == 0 else torch.float16
-            mine[: b - a] = ops.multi_head_attention(qa.view(b - a, hq * d), kc.view(kt), vc.view(kt), hq,
-                                                     start_position=P + a, out_dtype=odt)
-        if self.world == 1:
-            gathered = mine.unsqueeze(0)
-        else:
-            gathered = torch.empty((self.world, width, hq * d), dtype=odt, device=q.device)
-            dist.all_gather_into_tensor(gathered.view(-1), mine.view(-1), group=group)
         if out is None:
+            odt = torch.float32 if spec.out_dtype == 0 else torch.float16
             out = torch.empty(1, S, hq, d, dtype=odt, device=q.device)
-        for k in range(self.world):
-            a_k, b_k = self.boundary(k), self.boundary(k + 1)
-            if b_k > a_k:
-                out[0, a_k:b_k] = gathered[k, : b_k - a_k].view(b_k - a_k, hq, d)
+        a, b = self.rows
+        if self.world > 1:
+            # rows outside this rank's block: rotated and appended here (the block's own rows are
+            # appended again, to the same bits, by the fused call below)
+            kr = k_new.contiguous().clone()
+            if spec.rope_mode != 2:  # ROPE_NONE
+                ops.apply_rope_full(kr.view(S, hkv * d), P, hkv, d, spec.rope_theta, spec.rope_mode)
+            cache.add(layer, kr, v_new.contiguous())
+        if b > a:
+            view = _CacheAt(cache, P + a, q.device)
+            ops.attention_layer(q[:, a:b].contiguous(), k_new[:, a:b].contiguous(), v_new[:, a:b].contiguous(), view,
+                                layer=layer, out=out[:, a:b])
+        if self.world > 1:
+            for k in range(self.world):
+                a_k, b_k = self.boundary(k), self.boundary(k + 1)
+                if b_k > a_k:
+                    dist.broadcast(out[0, a_k:b_k], src=k, group=group)
         return out
+
+
+class _CacheAt:
+    """A KVCache seen as holding `start` rows: the fused call for one rank's query block."""
+
+    _starts: dict = {}
+
+    def __init__(self, cache, start: int, device):
+        self.spec, self.k, self.v = cache.spec, cache.k, cache.v
+        key = (str(device), start)
+        if key not in _CacheAt._starts:
+            _CacheAt._starts[key] = torch.full((1,), start, dtype=torch.int32, device=device)
+        self.seq_len = _CacheAt._starts[key]
+        self.host_len = [start]
 
 
 class NcclDist:

@@ -121,13 +121,15 @@ def _row_worker(rank, world, port, result_q):
         kc[P:P + S] = k
         vc[P:P + S] = inp["v_new"].numpy()[0].reshape(S, hkv * d)
         a, b = sh.rows
-        mine = np.zeros((sh.max_rows, hq * d), dtype=np.float32)
+        out_t = torch.zeros(S, hq * d)
         if b > a:
             qa = orc.rope_full(inp["q"].numpy()[0, a:b].reshape(b - a, hq * d), P + a, hq, d, theta)
-            mine[:b - a] = orc.mha(qa, kc[:P + b], vc[:P + b], hq, P + a)
-        g = [torch.zeros(sh.max_rows, hq * d) for _ in range(world)]
-        dist.all_gather(g, torch.from_numpy(mine))
-        out = np.concatenate([g[r].numpy()[:sh.boundary(r + 1) - sh.boundary(r)] for r in range(world)])
+            out_t[a:b] = torch.from_numpy(orc.mha(qa, kc[:P + b], vc[:P + b], hq, P + a))
+        for r in range(world):  # each block broadcast from its owner, as RowShard.forward does
+            a_r, b_r = sh.boundary(r), sh.boundary(r + 1)
+            if b_r > a_r:
+                dist.broadcast(out_t[a_r:b_r], src=r)
+        out = out_t.numpy()
         if rank == 0:
             ref = orc.attn_forward(cfg.spec(cap).desc(), inp["q"].numpy(), inp["k_new"].numpy(), inp["v_new"].numpy(),
                                    inp["k_cache"].numpy().copy(), inp["v_cache"].numpy().copy(), inp["seq_len"].numpy())

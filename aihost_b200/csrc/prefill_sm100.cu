@@ -9,11 +9,11 @@
 // in 128-row tiles (flash attention, online softmax); scores never leave the SM:
 //   warp 0      TMA producer: both Q tiles once, then K and V tiles into 2-3 stage rings
 //               (no multicast anywhere)
-//   warp 1      TMEM owner and tcgen05.mma issuer. Per cache tile j the tensor pipe runs
-//               O_A += P_A V_j, S_A = Q_A K_{j+1}^T, O_B += P_B V_j, S_B = Q_B K_{j+1}^T, so one
-//               softmax group's exponentials overlap the other group's matrix products
-//               (ping-pong). S and O accumulate in TMEM (fp32); P (fp16) is written back over
-//               its own S columns and read by the P.V MMA straight from TMEM.
+//   warps 1, 2  TMEM owner (warp 1) and tcgen05.mma issuers: per cache tile j a group's
+//               O += P V_j and S = Q K_{j+1}^T, so one softmax group's exponentials overlap
+//               the other group's matrix products (ping-pong). D = 64: one issuing thread per
+//               group (warps 1 and 2); D = 128: warp 1 issues for both groups in turn. S and O accumulate in TMEM (fp32); P (fp16) goes back to TMEM and
+//               the P.V MMA reads it from there (A operand in TMEM, V from shared memory).
 //   warps 4-7   softmax group A (query tile A), warps 8-11 group B: one thread per query row.
 //               RoPE of the Q tile in shared memory; per tile tcgen05.ld of S, row max, lazy
 //               rescale of O (only when the running max grows by more than 2^8), exp2 on the
@@ -22,8 +22,12 @@
 // Tile pairing: a CTA takes adjacent query tiles 2x and 2x+1, so both softmax groups stay busy
 // for the CTA's whole life (the ping-pong needs two live groups); CTAs with the longest causal
 // ranges launch first. Cache tiles above a tile's diagonal are never loaded or multiplied.
-// For head_dim 64, P goes through shared memory (SS-form P.V MMA at full rate); for 128 it stays
-// in TMEM (no room for two P tiles next to the K/V rings).
+// For head_dim 64, P has its own TMEM columns, so the next QK^T can overwrite S as soon as the
+// softmax has read it, ahead of this tile's P.V; for 128 P is written over S (no spare columns).
+// One thread's stream of tcgen05.mma (M = 128, K = 16) advances about one instruction per
+// 100-120 cycles whatever N is up to 128, hence one issuing thread per softmax group.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -32,9 +36,8 @@ namespace {
 
 constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // cache rows per tile
-// Three warpgroups: WG0 = producer warp, MMA warp, two spare warps (56 registers each after
-// setmaxnreg); WG1 / WG2 = softmax groups A / B (224 registers: a full 128-column score row
-// stays in registers). 128*56 + 256*224 = 384*168 = the launch's register file.
+// Three warpgroups: WG0 = producer warp, MMA issuer warps, spare warps; WG1 / WG2 = softmax
+// groups A / B (a full 128-column score row stays in registers).
 constexpr int kThreads = 384;
 // setmaxnreg split of the 168 x 384 registers the CTA launches with: producer / MMA warpgroup
 // 72, each softmax warpgroup 216 (128 * 72 + 2 * 128 * 216 = 168 * 384).
@@ -53,17 +56,20 @@ struct PrefillCfg {
   static constexpr int QB_OFF = QA_OFF + TILE_BYTES;
   static constexpr int K_OFF = QB_OFF + TILE_BYTES;
   static constexpr int V_OFF = K_OFF + NS * TILE_BYTES;
-  // P.V from shared memory (both operands SS) runs at full rate; with P in TMEM (TS form) the
-  // MMA costs ~116 cycles per 16 keys whatever N is. D = 64 has room for two 32 KB P tiles.
-  static constexpr bool P_SMEM = D == 64;
-  static constexpr int P_BYTES = kBM * kBN * 2;  // [128 rows x 128 keys] fp16, two 64-key blocks
-  static constexpr int P_OFF = V_OFF + NS * TILE_BYTES;
-  static constexpr int BAR_OFF = P_OFF + (P_SMEM ? 2 * P_BYTES : 0);
+  // P in its own TMEM columns (D = 64: S 128 + P 64 + O 64 columns per group), else over S
+  static constexpr bool P_SEP = D == 64;
+  static constexpr int BAR_OFF = V_OFF + NS * TILE_BYTES;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t TMEM_COLS = 512;
-  // TMEM columns: S_A, S_B (fp32, P fp16 aliased onto their first 64 columns), O_A, O_B
+  // TMEM columns: S_A, S_B (fp32), then P_A, P_B (fp16 pairs) and O_A, O_B for D = 64; for
+  // D = 128, O_A, O_B after S, with P aliased onto the first 64 columns of its S
   static __device__ __forceinline__ uint32_t s_col(int t) { return t ? 128u : 0u; }
-  static __device__ __forceinline__ uint32_t o_col(int t) { return 256u + static_cast<uint32_t>(t * D); }
+  static __device__ __forceinline__ uint32_t p_col(int t) {
+    return P_SEP ? 256u + static_cast<uint32_t>(t * 64) : s_col(t);
+  }
+  static __device__ __forceinline__ uint32_t o_col(int t) {
+    return (P_SEP ? 384u : 256u) + static_cast<uint32_t>(t * D);
+  }
 };
 
 // Byte offset of fp16 element (row, col) inside a [rows x 64k] block stack written by TMA with
@@ -79,7 +85,7 @@ struct Barriers {
   uint64_t q_full;
   uint64_t q_ready[2], s_full[2], p_full[2], o_full[2];
   uint64_t k_full[3], k_empty[3], v_full[3], v_empty[3];
-  uint64_t s_free[2], pv_done[2];  // P in shared memory: S read into registers / P.V complete
+  uint64_t s_free[2], pv_done[2];  // separate P: S read into registers / P.V complete
   uint64_t v_fix;  // last V tile's rows past the sequence end have been zeroed
   uint32_t tmem_base;
 };
@@ -88,6 +94,30 @@ static_assert(sizeof(Barriers) <= 256, "prefill_kernel reserves 256 bytes for it
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Packed fp32 pairs (sm_100): one instruction for two lanes' worth of IEEE fma / add.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
+      " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n add.rn.f32x2 rd, ra, rb;\n"
+      " mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// max of three (sm_100 three-input form; a NaN operand is ignored like fmaxf)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 template <int D>
@@ -99,7 +129,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   uint8_t* q_s[2] = {smem + C::QA_OFF, smem + C::QB_OFF};
   uint8_t* k_s = smem + C::K_OFF;
   uint8_t* v_s = smem + C::V_OFF;
-  uint8_t* p_s[2] = {smem + C::P_OFF, smem + C::P_OFF + C::P_BYTES};
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (a.n_new + kBM - 1) / kBM;
@@ -149,11 +178,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       mbar_init(&bar.pv_done[t], 1);
     }
     mbar_init(&bar.v_fix, 1);
+    // a ring slot is free once every issuing thread that reads its tile is done with it: both
+    // issuers when two threads share the tiles (pair mode, D = 64; group B's one extra last
+    // tile is never reloaded), else one commit per slot use
+    const int readers = C::P_SEP && !split && has_b ? 2 : 1;
     for (int i = 0; i < C::NS; ++i) {
       mbar_init(&bar.k_full[i], 1);
-      mbar_init(&bar.k_empty[i], 1);
+      mbar_init(&bar.k_empty[i], readers);
       mbar_init(&bar.v_full[i], 1);
-      mbar_init(&bar.v_empty[i], 1);
+      mbar_init(&bar.v_empty[i], readers);
     }
     fence_mbar_init();
   }
@@ -222,162 +255,157 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.v_fix);
     }
-    } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------------ MMA issuers
+    // A thread's tcgen05.mma stream advances by about one M = 128, K = 16 instruction per
+    // 100-120 cycles whatever N is, so with P in its own columns (D = 64) each softmax group gets
+    // its own issuing thread (warp 1: A, warp 2: B). With P over S (D = 128) a group's next QK^T
+    // must follow its P.V anyway; there warp 1 alone issues both groups' products in turn, which
+    // keeps the groups half a step apart (one group's exponentials overlap the other's products).
+    // Each group's products stay in issue order on one thread.
+    constexpr bool kTwo = C::P_SEP;
+    if (lane == 0 && (kTwo || warp == 1)) {
+      const int t_lo = kTwo ? warp - 1 : 0;
       constexpr uint32_t idesc_qk = make_idesc_f16(kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_f16(kBM, D, 0, 1);
       const uint32_t k_addr = smem_u32(k_s), v_addr = smem_u32(v_s);
-      const uint32_t q_addr[2] = {smem_u32(q_s[0]), smem_u32(q_s[split ? 0 : 1])};
-      bool ok = mbar_wait(&bar.q_ready[0], 0, status);
-      if (ok && has_b && !split) ok = mbar_wait(&bar.q_ready[1], 0, status);
-      tc_fence_after();
+      const uint32_t q_addr0 = smem_u32(q_s[0]), q_addr1 = smem_u32(q_s[split ? 0 : 1]);
+      // per-group values by selection, not by indexing with a run-time t (no local memory on
+      // the issuing thread, whose latency paces the tensor pipe)
+      auto nkv = [&](int t) { return t ? n_kv[1] : n_kv[0]; };
       // S_t = Q_t K^T with the K tile in ring slot s
       auto issue_qk = [&](int t, int s) {
+        const uint32_t qa = t ? q_addr1 : q_addr0;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-          umma_f16_ss(tmem + C::s_col(t), make_sw128_desc(q_addr[t] + off, 16, 1024),
+          umma_f16_ss(tmem + C::s_col(t), make_sw128_desc(qa + off, 16, 1024),
                       make_sw128_desc(k_addr + s * C::TILE_BYTES + off, 16, 1024), idesc_qk, kk > 0);
         }
         umma_commit(&bar.s_full[t]);
       };
-      const uint32_t p_addr[2] = {smem_u32(p_s[0]), smem_u32(p_s[1])};
-      // O_t (+)= P_t V with the V tile in ring slot s; j = the group's tile count so far
+      // O_t (+)= P_t V with P in TMEM and the V tile in ring slot s; j = the group's tile count
       auto issue_pv = [&](int t, int j, int s) {
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint64_t vd = make_sw128_desc(v_addr + s * C::TILE_BYTES + kk * 2048, kBN * 128, 1024);
-          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-          if constexpr (C::P_SMEM)
-            umma_f16_ss(tmem + C::o_col(t),
-                        make_sw128_desc(p_addr[t] + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024), vd, idesc_pv,
-                        acc);
-          else
-            umma_f16_ts(tmem + C::o_col(t), tmem + C::s_col(t) + kk * 8, vd, idesc_pv, acc);
+          umma_f16_ts(tmem + C::o_col(t), tmem + C::p_col(t) + kk * 8, vd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
-      if (split) {
-        // each group walks its own cache tiles; slots follow the producer's load order
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (!ok || n_kv[t] == 0) continue;
-          const int g = load_index(t, 0);
-          ok = mbar_wait(&bar.k_full[g % C::NS], (g / C::NS) & 1, status);
-          tc_fence_after();
+      // wait for the K tile of group t's step j; its ring slot in s
+      auto k_ready = [&](int t, int j, int& s) -> bool {
+        const int g = load_index(t, j);
+        s = g % C::NS;
+        return mbar_wait(&bar.k_full[s], (g / C::NS) & 1, status);
+      };
+      if constexpr (kTwo) {
+        // this thread's group T: P.V of cache tile j and, as soon as the softmax has read S(j)
+        // (P has its own columns), the QK^T of tile j + 1 ahead of it
+        auto run_group = [&](auto T) {
+          constexpr int t = decltype(T)::value;
+          const int nk = nkv(t);
+          int s0 = 0;
+          bool ok = mbar_wait(&bar.q_ready[split ? 0 : t], 0, status) && k_ready(t, 0, s0);
           if (ok) {
-            issue_qk(t, g % C::NS);
-            umma_commit(&bar.k_empty[g % C::NS]);
-          }
-        }
-        const int steps = max(n_kv[0], n_kv[1]);
-        for (int j = 0; ok && C::P_SMEM && j < steps; ++j) {
-          // P in shared memory: each group's next QK^T as soon as it has read S(j), ahead of P.V(j)
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (!ok || j + 1 >= n_kv[t]) continue;
-            const int gk = load_index(t, j + 1), sk = gk % C::NS;
-            if (!mbar_wait(&bar.s_free[t], j & 1, status)) { ok = false; break; }
-            if (!mbar_wait(&bar.k_full[sk], (gk / C::NS) & 1, status)) { ok = false; break; }
             tc_fence_after();
-            issue_qk(t, sk);
-            umma_commit(&bar.k_empty[sk]);
+            issue_qk(t, s0);
+            umma_commit(&bar.k_empty[s0]);
           }
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (!ok || j >= n_kv[t]) continue;
+          for (int j = 0; ok && j < nk; ++j) {
             const int gv = load_index(t, j), sv = gv % C::NS;
-            if (!mbar_wait(&bar.v_full[sv], (gv / C::NS) & 1, status)) { ok = false; break; }
-            if (gv == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
-            if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
+            if (j + 1 < nk) {
+              int sk = 0;
+              if (!mbar_wait(&bar.s_free[t], j & 1, status) || !k_ready(t, j + 1, sk)) break;
+              tc_fence_after();
+              issue_qk(t, sk);
+              umma_commit(&bar.k_empty[sk]);
+            }
+            if (!mbar_wait(&bar.v_full[sv], (gv / C::NS) & 1, status)) break;
+            if (gv == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) break;
+            if (!mbar_wait(&bar.p_full[t], j & 1, status)) break;
             tc_fence_after();
             issue_pv(t, j, sv);
             umma_commit(&bar.pv_done[t]);
             umma_commit(&bar.v_empty[sv]);
-            if (j + 1 == n_kv[t]) umma_commit(&bar.o_full[t]);
+            if (j + 1 == nk) umma_commit(&bar.o_full[t]);
           }
+        };
+        if (nkv(t_lo) > 0) {
+          if (t_lo == 0) run_group(std::integral_constant<int, 0>{});
+          else run_group(std::integral_constant<int, 1>{});
         }
-        for (int j = 0; ok && !C::P_SMEM && j < steps; ++j) {
+      } else {
+        // one thread, both groups in turn; P over S, so a group's next QK^T follows its P.V
+        bool ok = mbar_wait(&bar.q_ready[0], 0, status);
+        if (ok && has_b && !split) ok = mbar_wait(&bar.q_ready[1], 0, status);
+        tc_fence_after();
+        if (split) {
+          // each group walks its own cache tiles; slots follow the producer's load order
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
-            if (!ok || j >= n_kv[t]) continue;
-            const int gv = load_index(t, j), sv = gv % C::NS;
-            const bool next = j + 1 < n_kv[t];
-            const int gk = next ? load_index(t, j + 1) : 0, sk = gk % C::NS;
-            if (!mbar_wait(&bar.v_full[sv], (gv / C::NS) & 1, status)) { ok = false; break; }
-            if (gv == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
-            if (next && !mbar_wait(&bar.k_full[sk], (gk / C::NS) & 1, status)) { ok = false; break; }
-            if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
+            int s0 = 0;
+            if (!ok || n_kv[t] == 0) continue;
+            ok = k_ready(t, 0, s0);
             tc_fence_after();
-            issue_pv(t, j, sv);
-            umma_commit(&bar.v_empty[sv]);
-            if (next) {
-              issue_qk(t, sk);
-              umma_commit(&bar.k_empty[sk]);
-            } else {
-              umma_commit(&bar.o_full[t]);
+            if (ok) {
+              issue_qk(t, s0);
+              umma_commit(&bar.k_empty[s0]);
             }
           }
-        }
-      }
-      if (!split && ok && n_load > 0) {
-        ok = mbar_wait(&bar.k_full[0], 0, status);
-        tc_fence_after();
-        if (ok && n_kv[0] > 0) issue_qk(0, 0);
-        if (ok && n_kv[1] > 0) issue_qk(1, 0);
-        if (ok) umma_commit(&bar.k_empty[0]);
-      }
-      for (int j = 0; !split && ok && C::P_SMEM && j < n_load; ++j) {
-        const int s = j % C::NS;
-        const int s1 = (j + 1) % C::NS;
-        // P in shared memory: the next QK^T (K tile j + 1, shared by both groups) as soon as each
-        // group has read S(j), ahead of P.V(j)
-        if (j + 1 < n_load) {
-          if (!mbar_wait(&bar.k_full[s1], ((j + 1) / C::NS) & 1, status)) { ok = false; break; }
+          const int steps = max(n_kv[0], n_kv[1]);
+          for (int j = 0; ok && j < steps; ++j) {
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (!ok || j + 1 >= n_kv[t]) continue;
-            if (!mbar_wait(&bar.s_free[t], j & 1, status)) { ok = false; break; }
-            tc_fence_after();
-            issue_qk(t, s1);
+            for (int t = 0; t < 2; ++t) {
+              if (!ok || j >= n_kv[t]) continue;
+              const int gv = load_index(t, j), sv = gv % C::NS;
+              const bool next = j + 1 < n_kv[t];
+              int sk = 0;
+              if (!mbar_wait(&bar.v_full[sv], (gv / C::NS) & 1, status)) { ok = false; break; }
+              if (gv == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
+              if (next && !k_ready(t, j + 1, sk)) { ok = false; break; }
+              if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
+              tc_fence_after();
+              issue_pv(t, j, sv);
+              umma_commit(&bar.v_empty[sv]);
+              if (next) {
+                issue_qk(t, sk);
+                umma_commit(&bar.k_empty[sk]);
+              } else {
+                umma_commit(&bar.o_full[t]);
+              }
+            }
           }
-          if (!ok) break;
-          umma_commit(&bar.k_empty[s1]);
-        }
-        if (!mbar_wait(&bar.v_full[s], (j / C::NS) & 1, status)) { ok = false; break; }
-        if (j == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
+        } else {
+          // pair mode: both groups read cache tile j from the same ring slot
+          if (ok && n_load > 0) {
+            ok = mbar_wait(&bar.k_full[0], 0, status);
+            tc_fence_after();
+            if (ok && n_kv[0] > 0) issue_qk(0, 0);
+            if (ok && n_kv[1] > 0) issue_qk(1, 0);
+            if (ok) umma_commit(&bar.k_empty[0]);
+          }
+          for (int j = 0; ok && j < n_load; ++j) {
+            const int s = j % C::NS;
+            const int s1 = (j + 1) % C::NS;
+            // operands first (normally long resident), then the softmax hand-offs
+            if (!mbar_wait(&bar.v_full[s], (j / C::NS) & 1, status)) { ok = false; break; }
+            if (j == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
+            if (j + 1 < n_load && !mbar_wait(&bar.k_full[s1], ((j + 1) / C::NS) & 1, status)) { ok = false; break; }
+            tc_fence_after();
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (!ok || j >= n_kv[t]) continue;
-          if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, j, s);
-          umma_commit(&bar.pv_done[t]);
-          if (j + 1 == n_kv[t]) umma_commit(&bar.o_full[t]);
+            for (int t = 0; t < 2; ++t) {
+              if (j >= n_kv[t]) continue;
+              if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
+              tc_fence_after();
+              issue_pv(t, j, s);
+              if (j + 1 < n_kv[t]) issue_qk(t, s1);
+              else umma_commit(&bar.o_full[t]);
+            }
+            if (!ok) break;
+            umma_commit(&bar.v_empty[s]);
+            if (j + 1 < n_load) umma_commit(&bar.k_empty[s1]);
+          }
         }
-        if (!ok) break;
-        umma_commit(&bar.v_empty[s]);
-      }
-      for (int j = 0; !split && ok && !C::P_SMEM && j < n_load; ++j) {
-        const int s = j % C::NS;
-        const int s1 = (j + 1) % C::NS;
-        // operands first (normally long resident), then the softmax hand-offs
-        if (!mbar_wait(&bar.v_full[s], (j / C::NS) & 1, status)) { ok = false; break; }
-        if (j == n_load - 1 && n_load * kBN > Lk && !mbar_wait(&bar.v_fix, 0, status)) { ok = false; break; }
-        if (j + 1 < n_load && !mbar_wait(&bar.k_full[s1], ((j + 1) / C::NS) & 1, status)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (j >= n_kv[t]) continue;
-          if (!mbar_wait(&bar.p_full[t], j & 1, status)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, j, s);
-          if (j + 1 < n_kv[t]) issue_qk(t, s1);
-          else umma_commit(&bar.o_full[t]);
-        }
-        if (!ok) break;
-        umma_commit(&bar.v_empty[s]);
-        if (j + 1 < n_load) umma_commit(&bar.k_empty[s1]);
       }
     }
     }
@@ -392,7 +420,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int kv_first = t ? kv_lo[1] : 0;
     const int q0 = (t ? qt[1] : qt[0]) * kBM;
     uint8_t* const q_tile = split || t == 0 ? q_s[0] : q_s[1];
-    uint8_t* const p_tile = t ? p_s[1] : p_s[0];
     const int32_t qpos = start + q0 + r;      // absolute position of this query row
     const int32_t limit = min(qpos, Lk - 1);  // last visible cache row
     const bool active = t == 0 || has_b;
@@ -458,6 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     float m = -1e30f, l = 0.0f;  // running max (log2 units) and denominator
     const uint32_t s_tmem = tmem + lane_base + C::s_col(t);
     const uint32_t o_tmem = tmem + lane_base + C::o_col(t);
+    const uint32_t p_tmem = tmem + lane_base + C::p_col(t);
     for (int j = 0; active && ok && j < nk; ++j) {
       if (!mbar_wait(&bar.s_full[t], j & 1, status)) { ok = false; break; }
       tc_fence_after();
@@ -465,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, sr[c]);
       tmem_wait_ld();
-      if constexpr (C::P_SMEM) {  // S is in registers: the next QK^T may overwrite it
+      if constexpr (C::P_SEP) {  // S is in registers: the next QK^T may overwrite it
         tc_fence_before();
         mbar_arrive(&bar.s_free[t]);
       }
@@ -478,16 +506,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
           for (int i = 0; i < 32; ++i)
             if (kv0 + c * 32 + i > limit) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      // row max with independent partial maxima (instruction-level parallelism)
+      // row max: three-input maxima into independent partials (instruction-level parallelism)
       float mxp[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sr[c][i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        for (int i = 0; i < 16; ++i)
+          mxp[i & 7] = fmax3(mxp[i & 7], __uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1]));
+      const float mx = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]));
       const float m_new = fmaxf(m, mx * sl2);
       const bool resc = m_new > m + kRescaleThreshold;
       const float f = resc ? ex2_approx(m - m_new) : 1.0f;
@@ -495,24 +523,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         l *= f;
         m = m_new;
       }
-      // P = 2^(s*scale*log2e - m) in fp16 (masked entries: 2^-inf = 0), from S in registers
-      const float neg_m = -m;
-      float rsp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // P = 2^(s*scale*log2e - m) in fp16 (masked entries: 2^-inf = 0), from S in registers; the
+      // scale-and-subtract and the row sums run on packed fp32 pairs
+      const float2 sl2x2 = make_float2(sl2, sl2), neg_m2 = make_float2(-m, -m);
+      float2 rsp[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                       make_float2(0.0f, 0.0f)};
       uint32_t pk[4][16];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i]), sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c][2 * i + 1]), sl2, neg_m));
-          rsp[i & 3] += p0 + p1;
-          pk[c][i] = pack_half2(p0, p1);
+          const float2 x = ffma2(make_float2(__uint_as_float(sr[c][2 * i]), __uint_as_float(sr[c][2 * i + 1])), sl2x2,
+                                 neg_m2);
+          const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          rsp[i & 3] = fadd2(rsp[i & 3], pp);
+          pk[c][i] = pack_half2(pp.x, pp.y);
         }
-      l += (rsp[0] + rsp[1]) + (rsp[2] + rsp[3]);
-      // O and (shared-memory) P of the previous tile: with P in shared memory the previous P.V may
-      // still be running (the next QK^T was issued ahead of it), so wait for it; otherwise this
-      // tile's S was committed after it, which already orders it.
-      if constexpr (C::P_SMEM) {
+      l += ((rsp[0].x + rsp[0].y) + (rsp[1].x + rsp[1].y)) + ((rsp[2].x + rsp[2].y) + (rsp[3].x + rsp[3].y));
+      // O and the separate P of the previous tile: the previous P.V may still be running (the next
+      // QK^T was issued ahead of it), so wait for it; with P over S, this tile's S was committed
+      // after it, which already orders it.
+      if constexpr (C::P_SEP) {
         if (j > 0 && !mbar_wait(&bar.pv_done[t], (j - 1) & 1, status)) { ok = false; break; }
         tc_fence_after();
       }
@@ -529,24 +560,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
       }
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if constexpr (C::P_SMEM) {
-          // row r of the K-major SW128 P tile: 16-byte chunk (c*2 + q) of key block c/2
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int ch = (c & 1) * 4 + q * 2;  // 16-byte chunk index within the 128-byte row
-            uint8_t* row = p_tile + (c >> 1) * (kBM * 128) + r * 128;
-            *reinterpret_cast<uint4*>(row + (((ch) ^ (r & 7)) << 4)) =
-                make_uint4(pk[c][8 * q], pk[c][8 * q + 1], pk[c][8 * q + 2], pk[c][8 * q + 3]);
-            *reinterpret_cast<uint4*>(row + (((ch + 1) ^ (r & 7)) << 4)) =
-                make_uint4(pk[c][8 * q + 4], pk[c][8 * q + 5], pk[c][8 * q + 6], pk[c][8 * q + 7]);
-          }
-        } else {
-          tmem_st16(s_tmem + c * 16, pk[c]);  // over the first 64 columns of this tile's S
-        }
-      }
-      if constexpr (C::P_SMEM) fence_proxy_async_smem();
-      tmem_wait_st();  // the O rescale (and TMEM P) complete before the next P.V reads them
+      for (int c = 0; c < 4; ++c) tmem_st16(p_tmem + c * 16, pk[c]);
+      tmem_wait_st();  // the O rescale and P complete before the next P.V reads them
       tc_fence_before();
       mbar_arrive(&bar.p_full[t]);
     }

@@ -305,11 +305,11 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
     torch.cuda.synchronize()
     ctx.sync_status()
 
-    # timed region: K steps, CUDA events per step on the launching stream (flushes excluded)
+    # timed region: K steps, CUDA events per step on the launching stream (flushes excluded).
+    # The library's per-launch profiler stays off here: its events between two launches would
+    # keep a programmatic launch from overlapping the kernel before it.
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ctx.profiler_reset()
-    ctx.profiler(True)
     if dist_on:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -324,8 +324,16 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
     wall = time.perf_counter() - wall0
     if dist_on:
         torch.distributed.barrier()
-    ctx.profiler(False)
     ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    # the same K steps again with the profiler on: per-kernel device times and launch counts
+    ctx.profiler_reset()
+    ctx.profiler(True)
+    for i in range(steps):
+        if flush is not None:
+            flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    ctx.profiler(False)
     kern = {name: ctx.profiler_read(k) for name, k in
             (("append", A.KERNEL_APPEND), ("decode", A.KERNEL_DECODE), ("combine", A.KERNEL_COMBINE),
              ("prefill", A.KERNEL_PREFILL), ("convert", A.KERNEL_CONVERT))}

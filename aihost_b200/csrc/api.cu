@@ -266,7 +266,8 @@ cudaError_t timed_launch(aihost_attn_ctx* ctx, int kind, cudaStream_t st, F&& fn
 aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const KvLayout& kv, float scale,
                          int32_t batch, const void* q, const void* kc, const void* vc, const int32_t* seq_len,
                          int32_t start_scalar, int32_t len_offset, int32_t rope_mode, void* out, cudaStream_t st,
-                         const void* k_new = nullptr, const void* v_new = nullptr) {
+                         const void* k_new = nullptr, const void* v_new = nullptr, const int32_t* q_pos = nullptr,
+                         float* lse = nullptr) {
   DecodePlan plan = plan_decode(d, batch, ctx->num_sms);
   const size_t need = decode_scratch_bytes(batch, d->n_q_heads, d->head_dim, plan.max_splits);
   if (need > ctx->scratch_bytes)
@@ -301,6 +302,8 @@ aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const 
   a.k_new = k_new;
   a.v_new = v_new;
   a.new_dtype = d->q_dtype;
+  a.q_pos = q_pos;
+  a.lse = lse;
   cudaError_t e = launch_decode_any(a, st, ctx);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return AIHOST_OK;
@@ -444,7 +447,7 @@ cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ct
     e = run(AIHOST_KERNEL_APPEND, [&] {
       return launch_kv_append(a.k_new, a.v_new, a.new_dtype, const_cast<void*>(a.k_cache), const_cast<void*>(a.v_cache),
                               a.kv, a.seq_len, a.batch, 1, a.n_kv_heads, a.head_dim, a.rope_mode, a.freqs, a.status,
-                              st);
+                              st, a.q_pos);
     });
     if (e != cudaSuccess) return e;
   }
@@ -635,6 +638,51 @@ aihost_status aihost_attn_mha(aihost_attn_ctx* ctx, const aihost_attn_desc* desc
     return run_decode(ctx, desc, kv, scale, 1, q, k, v, nullptr, 0, n_kv, AIHOST_ROPE_NONE, out, st);
   return run_prefill(ctx, desc, kv, scale, 1, n_q, q, k, v, nullptr, start_pos, n_kv - start_pos, n_kv,
                      AIHOST_ROPE_NONE, out, st, false);
+}
+
+aihost_status aihost_attn_decode_partial(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
+                                         const void* q, const void* k_new, const void* v_new, void* k_cache,
+                                         void* v_cache, const int32_t* seq_len, const int32_t* q_pos, void* out,
+                                         float* lse, void* stream) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  KvLayout kv;
+  float scale;
+  s = check_desc(desc, &kv, &scale);
+  if (s != AIHOST_OK) return s;
+  if (batch < 1) return fail(AIHOST_EINVAL, "batch (%d) must be >= 1", batch);
+  if (!q || !k_cache || !v_cache || !seq_len || !out)
+    return fail(AIHOST_EINVAL, "q, k_cache, v_cache, seq_len and out must be non-NULL");
+  if (!k_new != !v_new) return fail(AIHOST_EINVAL, "k_new and v_new must both be given or both be NULL");
+  if (k_new && !q_pos) return fail(AIHOST_EINVAL, "appending k_new needs q_pos (the new rows' global positions)");
+  if (!aligned(q, 16) || !aligned(out, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) ||
+      !aligned(k_new, 16) || !aligned(v_new, 16) || !aligned(seq_len, 4) || !aligned(q_pos, 4) || !aligned(lse, 4))
+    return fail(AIHOST_EINVAL, "tensor pointers must be 16-byte aligned (seq_len, q_pos and lse 4-byte)");
+  DeviceGuard g(ctx->device);
+  if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+  const int32_t rope = q_pos ? desc->rope_mode : AIHOST_ROPE_NONE;
+  return run_decode(ctx, desc, kv, scale, batch, q, k_cache, v_cache, seq_len, 0, k_new ? 1 : 0, rope, out,
+                    static_cast<cudaStream_t>(stream), k_new, v_new, q_pos, lse);
+}
+
+aihost_status aihost_attn_merge_partials(aihost_attn_ctx* ctx, int32_t n_parts, int32_t rows, int32_t head_dim,
+                                         int32_t dtype, const void* o_parts, const float* lse_parts, void* out,
+                                         float* lse_out, void* stream) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  if (n_parts < 1 || rows < 1) return fail(AIHOST_EINVAL, "n_parts (%d) and rows (%d) must be >= 1", n_parts, rows);
+  if (head_dim < 1 || head_dim > kMaxHeadDim)
+    return fail(AIHOST_EINVAL, "head_dim %d outside [1, %d]", head_dim, kMaxHeadDim);
+  if (dtype != AIHOST_F32 && dtype != AIHOST_F16) return fail(AIHOST_EINVAL, "dtype must be F32 or F16");
+  if (!o_parts || !lse_parts || !out) return fail(AIHOST_EINVAL, "o_parts, lse_parts and out must be non-NULL");
+  DeviceGuard g(ctx->device);
+  if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_COMBINE, st, [&] {
+    return launch_merge_partials(n_parts, rows, head_dim, dtype, o_parts, lse_parts, out, lse_out, st);
+  });
+  if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  return AIHOST_OK;
 }
 
 aihost_status aihost_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,

@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
   const int n_splits = (Lk + a.chunk - 1) / a.chunk;
 
   // ---- q rows of this group, rotated at the new token's position, kept as floats
-  const float pos = static_cast<float>(start + a.rope_pos_offset);
+  const float pos = static_cast<float>(a.q_pos ? a.q_pos[b] : start + a.rope_pos_offset);
   for (int idx = threadIdx.x; idx < GT * (D / 2); idx += kDecodeThreads) {
     const int g = idx / (D / 2), pair = idx % (D / 2);
     const int i1 = a.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
@@ -268,6 +268,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
       const int64_t oidx = (static_cast<int64_t>(b) * a.n_q_heads + h) * D + d;
       if (a.out_dtype == AIHOST_F32) static_cast<float*>(a.out)[oidx] = v;
       else static_cast<__half*>(a.out)[oidx] = __float2half_rn(v);
+      if (a.lse && d == 0) a.lse[static_cast<int64_t>(b) * a.n_q_heads + h] = (m_s[g] + log2f(l_s[g])) * kLn2;
     } else {
       const int64_t pidx = (static_cast<int64_t>(b) * a.n_q_heads + h) * a.max_splits + split;
       a.part_o[pidx * D + d] = o;
@@ -301,6 +302,28 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(DecodeArgs a) {
   const int64_t oidx = (static_cast<int64_t>(b) * a.n_q_heads + h) * D + d;
   if (a.out_dtype == AIHOST_F32) static_cast<float*>(a.out)[oidx] = v;
   else static_cast<__half*>(a.out)[oidx] = __float2half_rn(v);
+  if (a.lse && d == 0) a.lse[static_cast<int64_t>(b) * a.n_q_heads + h] = (m + log2f(l)) * kLn2;
+}
+
+// One CTA per query row (sequence x head), one thread per output element: the softmax-weighted
+// sum of the parts' normalised outputs. Parts with lse = -inf (no rows) get weight 0.
+template <typename T>
+__global__ void merge_partials_kernel(int32_t n_parts, int64_t rows, int32_t head_dim, const T* __restrict__ o_parts,
+                                      const float* __restrict__ lse_parts, T* __restrict__ out, float* lse_out) {
+  const int64_t r = blockIdx.x;
+  const int d = threadIdx.x;
+  float m = -INFINITY;
+  for (int p = 0; p < n_parts; ++p) m = fmaxf(m, lse_parts[p * rows + r]);
+  float s = 0.0f, acc = 0.0f;
+  if (m > -INFINITY) {
+    for (int p = 0; p < n_parts; ++p) {
+      const float w = expf(lse_parts[p * rows + r] - m);
+      s += w;
+      if (d < head_dim) acc = fmaf(w, ld_as_float(o_parts + (p * rows + r) * head_dim + d), acc);
+    }
+  }
+  if (d < head_dim) st_from_float(out + r * head_dim + d, s > 0.0f ? acc / s : 0.0f);
+  if (lse_out && d == 0) lse_out[r] = s > 0.0f ? m + logf(s) : -INFINITY;
 }
 
 template <typename KV, int D, int GT>
@@ -347,6 +370,19 @@ cudaError_t launch_decode_combine(const DecodeArgs& a, cudaStream_t st) {
   if (a.max_splits <= 1) return cudaSuccess;
   if (a.head_dim == 64) decode_combine_kernel<64><<<dim3(a.n_q_heads, a.batch), 64, 0, st>>>(a);
   else decode_combine_kernel<128><<<dim3(a.n_q_heads, a.batch), 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge_partials(int32_t n_parts, int64_t rows, int32_t head_dim, int32_t dtype,
+                                  const void* o_parts, const float* lse_parts, void* out, float* lse_out,
+                                  cudaStream_t st) {
+  const int threads = (head_dim + 31) / 32 * 32;
+  if (dtype == AIHOST_F32)
+    merge_partials_kernel<float><<<static_cast<unsigned>(rows), threads, 0, st>>>(
+        n_parts, rows, head_dim, static_cast<const float*>(o_parts), lse_parts, static_cast<float*>(out), lse_out);
+  else
+    merge_partials_kernel<__half><<<static_cast<unsigned>(rows), threads, 0, st>>>(
+        n_parts, rows, head_dim, static_cast<const __half*>(o_parts), lse_parts, static_cast<__half*>(out), lse_out);
   return cudaGetLastError();
 }
 

@@ -95,7 +95,8 @@ __device__ __forceinline__ void append_new_row(const DecodeArgs& p, int b, int k
   const uint8_t* src = static_cast<const uint8_t*>(is_k ? p.k_new : p.v_new) + row * D * esz;
   float x[E];
   load_row_warp<E>(src, p.new_dtype, lane, x);
-  if (is_k && p.rope_mode != AIHOST_ROPE_NONE) rope_row_warp<E>(x, lane, static_cast<float>(t), p.rope_mode, p.freqs);
+  if (is_k && p.rope_mode != AIHOST_ROPE_NONE)
+    rope_row_warp<E>(x, lane, static_cast<float>(p.q_pos ? p.q_pos[b] : t), p.rope_mode, p.freqs);
   uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(is_k ? p.k_cache : p.v_cache)) + b * p.kv.seq_stride +
                  static_cast<int64_t>(t) * p.kv.token_stride + static_cast<int64_t>(kvh) * p.kv.head_stride;
   store_row_warp<E>(x, lane, dst, p.kv.dtype);
@@ -148,6 +149,7 @@ __device__ __forceinline__ void decode_emit(const DecodeArgs& p, float* merge, i
       const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * D + d;
       if (p.out_dtype == AIHOST_F32) static_cast<float*>(p.out)[oidx] = v;
       else static_cast<__half*>(p.out)[oidx] = __float2half_rn(v);
+      if (p.lse && d == 0) p.lse[static_cast<int64_t>(b) * p.n_q_heads + h] = (m + log2f(l)) * kLn2;
     } else {
       const int64_t pidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * p.max_splits + split;
       p.part_o[pidx * D + d] = acc;
@@ -187,6 +189,7 @@ __device__ __forceinline__ void decode_emit(const DecodeArgs& p, float* merge, i
     }
     const float inv = 1.0f / l;
     for (int sp = 0; sp < n_splits; ++sp) wts[threadIdx.x * kMergeSplits + sp] *= inv;
+    if (p.lse) p.lse[static_cast<int64_t>(b) * p.n_q_heads + h0 + threadIdx.x] = (m + log2f(l)) * kLn2;
   }
   asm volatile("bar.sync 1, 128;" ::: "memory");
   for (int idx = threadIdx.x; idx < g_count * (D / 4); idx += kComputeWarps * 32) {
@@ -220,6 +223,7 @@ __device__ __forceinline__ void decode_emit(const DecodeArgs& p, float* merge, i
       acc.y *= inv;
       acc.z *= inv;
       acc.w *= inv;
+      if (p.lse && d == 0) p.lse[static_cast<int64_t>(b) * p.n_q_heads + h0 + g] = (m + log2f(l)) * kLn2;
     }
     const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h0 + g) * D + d;
     if (p.out_dtype == AIHOST_F32) {
@@ -521,7 +525,7 @@ template <int D>
 __device__ __forceinline__ void load_q_rows(const DecodeArgs& p, __half* q_s, int b, int h0, int g_count,
                                             int32_t start, int nthreads) {
   constexpr int QROW = D + 8;
-  const float pos = static_cast<float>(start + p.rope_pos_offset);
+  const float pos = static_cast<float>(p.q_pos ? p.q_pos[b] : start + p.rope_pos_offset);
   for (int idx = threadIdx.x; idx < 16 * (D / 2); idx += nthreads) {
     const int g = idx / (D / 2), pair = idx % (D / 2);
     const int i1 = p.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;

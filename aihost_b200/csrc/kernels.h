@@ -29,11 +29,13 @@ cudaError_t launch_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_head
                              int32_t start_pos, int32_t rope_mode, const RopeFreqs& freqs, cudaStream_t st);
 
 // Append k_new/v_new [batch][n_new][Hkv][d] into cache rows [seq_len[b], seq_len[b]+n_new),
-// rotating K when rope_mode != NONE. Records kStatusBadLength when a row would exceed capacity.
+// rotating K when rope_mode != NONE at position seq_len[b] + s, or rope_pos[b] + s when rope_pos
+// (device, per sequence) is given. Records kStatusBadLength when a row would exceed capacity.
 cudaError_t launch_kv_append(const void* k_new, const void* v_new, int32_t in_dtype, void* k_cache,
                              void* v_cache, const KvLayout& kv, const int32_t* seq_len, int32_t batch,
                              int32_t n_new, int32_t n_kv_heads, int32_t head_dim, int32_t rope_mode,
-                             const RopeFreqs& freqs, int32_t* status, cudaStream_t st);
+                             const RopeFreqs& freqs, int32_t* status, cudaStream_t st,
+                             const int32_t* rope_pos = nullptr);
 
 // fp16 staging for the prefill: q [batch][n_q][Hq][d] fp32 -> fp16, rotated at start_b + s
 // (start_b = seq_len[b], or start_scalar when seq_len is NULL) unless rope_mode is NONE.
@@ -78,7 +80,12 @@ struct DecodeArgs {
   // the call's epoch; the last split to arrive merges the partials. NULL: combine kernel.
   unsigned long long* counters;
   uint32_t epoch;
+  // Optional: q position per sequence (device; NULL -> seq_len[b] + rope_pos_offset), and
+  // lse[b][h] = ln sum_j exp(scale * q.k_j) over the attended rows, written with the output.
+  const int32_t* q_pos;
+  float* lse;
 };
+constexpr float kLn2 = 0.6931471805599453f;
 // Arrival counters a fused combine may use (per (sequence, KV head, head group)).
 constexpr int64_t kMaxSplitCounters = 1 << 16;
 size_t decode_scratch_bytes(int32_t batch, int32_t n_q_heads, int32_t head_dim, int32_t max_splits);
@@ -86,6 +93,12 @@ size_t decode_scratch_bytes(int32_t batch, int32_t n_q_heads, int32_t head_dim, 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t st);
 // Merge of the per-split partials (only needed when max_splits > 1).
 cudaError_t launch_decode_combine(const DecodeArgs& a, cudaStream_t st);
+// Merge of n_parts normalised partial outputs of the same query rows over disjoint key sets:
+// out[r] = sum_p o_p[r] * exp(lse_p[r] - lse[r]), lse[r] = ln sum_p exp(lse_p[r]).
+// o_parts [n_parts][rows][head_dim] and out [rows][head_dim] of dtype (F32 / F16).
+cudaError_t launch_merge_partials(int32_t n_parts, int64_t rows, int32_t head_dim, int32_t dtype,
+                                  const void* o_parts, const float* lse_parts, void* out, float* lse_out,
+                                  cudaStream_t st);
 
 // ---------------------------------------------------------------- decode_mma.cu
 // fp16-cache decode on the tensor cores: K/V maps over the cache with 64-row boxes.

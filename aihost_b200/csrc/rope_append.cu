@@ -50,7 +50,8 @@ template <typename Tin, int D>
 __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __restrict__ v_new,
                                  uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache, KvLayout kv,
                                  const int32_t* __restrict__ seq_len, int32_t batch, int32_t n_new,
-                                 int32_t n_kv_heads, int32_t rope_mode, RopeFreqs freqs, int32_t* status) {
+                                 int32_t n_kv_heads, int32_t rope_mode, RopeFreqs freqs, int32_t* status,
+                                 const int32_t* __restrict__ rope_pos) {
   constexpr int E = D / 32;
   griddep_launch_dependents();  // the prefill that follows may start its own set-up now
   const int32_t lane = threadIdx.x & 31;
@@ -72,7 +73,10 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
 #pragma unroll
   for (int e = 0; e < E; ++e) x[e] = load_in(src + e);
 
-  if (is_k && rope_mode != AIHOST_ROPE_NONE) rope_row_warp<E>(x, lane, static_cast<float>(t), rope_mode, freqs);
+  if (is_k && rope_mode != AIHOST_ROPE_NONE) {
+    const float pos = static_cast<float>(rope_pos ? rope_pos[b] + s : t);
+    rope_row_warp<E>(x, lane, pos, rope_mode, freqs);
+  }
 
   uint8_t* dst = (is_k ? k_cache : v_cache) + b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride +
                  static_cast<int64_t>(h) * kv.head_stride;
@@ -170,7 +174,7 @@ cudaError_t launch_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_head
 cudaError_t launch_kv_append(const void* k_new, const void* v_new, int32_t in_dtype, void* k_cache,
                              void* v_cache, const KvLayout& kv, const int32_t* seq_len, int32_t batch,
                              int32_t n_new, int32_t n_kv_heads, int32_t head_dim, int32_t rope_mode,
-                             const RopeFreqs& freqs, int32_t* status, cudaStream_t st) {
+                             const RopeFreqs& freqs, int32_t* status, cudaStream_t st, const int32_t* rope_pos) {
   const int64_t rows = static_cast<int64_t>(batch) * n_new * n_kv_heads;
   if (rows == 0) return cudaSuccess;
   const int warps = 8;
@@ -180,7 +184,7 @@ cudaError_t launch_kv_append(const void* k_new, const void* v_new, int32_t in_dt
 #define AIHOST_APPEND(TIN, DD)                                                                                   \
   kv_append_kernel<TIN, DD><<<grid, warps * 32, 0, st>>>(static_cast<const TIN*>(k_new),                         \
                                                          static_cast<const TIN*>(v_new), kc, vc, kv, seq_len, \
-                                                         batch, n_new, n_kv_heads, rope_mode, freqs, status)
+                                                         batch, n_new, n_kv_heads, rope_mode, freqs, status, rope_pos)
   if (in_dtype == AIHOST_F32) {
     if (head_dim == 64) AIHOST_APPEND(float, 64);
     else AIHOST_APPEND(float, 128);

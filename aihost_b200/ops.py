@@ -199,6 +199,39 @@ class ComputeOps:
                                     _ptr(K), _ptr(V), _ptr(out), _stream(self.stream)))
         return out
 
+    def decode_partial(self, spec: LayerSpec, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                       seq_len: torch.Tensor, q_pos: torch.Tensor | None = None, k_new: torch.Tensor | None = None,
+                       v_new: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """One query row per sequence (q [B, Hq, d]) over this part's cache rows [0, seq_len[b]),
+        plus the new rows k_new / v_new [B, Hkv, d] appended at row seq_len[b] (K rotated at
+        q_pos[b]) when given; q rotated at q_pos[b] when given (spec.rope_mode), else used as is.
+        Returns (out [B, Hq, d] normalised over these rows, lse [B, Hq] fp32 =
+        ln sum_j exp(scale * q.k_j)). Cache lengths are not advanced."""
+        B = q.shape[0]
+        if out is None:
+            odt = torch.float32 if spec.out_dtype == F32 else torch.float16
+            out = torch.empty(B, spec.n_q_heads, spec.head_dim, dtype=odt, device=q.device)
+        lse = torch.empty(B, spec.n_q_heads, dtype=torch.float32, device=q.device)
+        self.ctx.reserve_for(spec, B, 1)
+        d = spec.desc()
+        check(lib().aihost_attn_decode_partial(self.ctx.handle, ctypes.byref(d), B, _ptr(q), _ptr(k_new),
+                                               _ptr(v_new), _ptr(k_cache), _ptr(v_cache), _ptr(seq_len), _ptr(q_pos),
+                                               _ptr(out), _ptr(lse), _stream(self.stream)))
+        return out, lse
+
+    def merge_partials(self, o_parts: torch.Tensor, lse_parts: torch.Tensor,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+        """Combine n partial results o_parts [n, ..., d] / lse_parts [n, ...] of the same query rows
+        over disjoint key sets into the result over all of them."""
+        n, d = o_parts.shape[0], o_parts.shape[-1]
+        rows = o_parts[0].numel() // d
+        if out is None:
+            out = torch.empty(o_parts.shape[1:], dtype=o_parts.dtype, device=o_parts.device)
+        check(lib().aihost_attn_merge_partials(self.ctx.handle, n, rows, d, dtype_code(o_parts), _ptr(o_parts),
+                                               _ptr(lse_parts), _ptr(out), None, _stream(self.stream)))
+        return out
+
     def fused_mha_generate(self, Q, K, V, num_q_heads: int, num_kv_heads: int, head_dim: int,
                            scale: float) -> torch.Tensor:
         """FusedMHAGenerate (ComputeOps.cs:1015-1043): one query row, every cached row visible."""

@@ -196,6 +196,61 @@ class _CacheAt:
         self.host_len = [start]
 
 
+@dataclasses.dataclass
+class ContextShard:
+    """Rank `rank` of `world`'s share of a decode step split by cache rows (context parallelism),
+    for layers with fewer KV heads than ranks (e.g. 4 KV heads on 8 GPUs: each head group's rows
+    over 2 ranks). Rank r holds rows [r*L/N, (r+1)*L/N) of every sequence's cache in its own local
+    cache (local row i = global row r*L/N + i); the last rank also appends the new token. Each rank
+    attends its rows (aihost_attn_decode_partial: q rotated at the global position), the ranks
+    all-gather (out, lse), and aihost_attn_merge_partials combines them."""
+
+    rank: int
+    world: int
+
+    def chunk(self, length: int, k: int | None = None) -> tuple[int, int]:
+        """Global rows [lo, hi) of a sequence of `length` cached rows held by rank k (default: this rank)."""
+        k = self.rank if k is None else k
+        return length * k // self.world, length * (k + 1) // self.world
+
+    @property
+    def appends(self) -> bool:
+        return self.rank == self.world - 1
+
+    def partial(self, ops, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, cache, q_pos: torch.Tensor,
+                layer: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+        """This rank's part of one decode step: q [B, 1, Hq, d], k_new / v_new [B, 1, Hkv, d];
+        `cache` holds this rank's rows (device and host lengths = local rows, each >= 1); q_pos
+        (device int32 [B]) = each sequence's cached rows over all ranks, the new token's position.
+        The last rank appends the new rows in the same call (K rotated at q_pos). Returns
+        (out [B, Hq, d] normalised over this rank's rows, lse [B, Hq]). Cache lengths are not
+        advanced."""
+        spec = cache.spec
+        B, d = q.shape[0], q.shape[3]
+        if self.appends and any(n + 1 > spec.kv_capacity for n in cache.host_len):
+            raise ValueError("KV cache capacity exceeded")
+        kn = k_new.reshape(B, k_new.shape[2], d) if self.appends else None
+        vn = v_new.reshape(B, v_new.shape[2], d) if self.appends else None
+        return ops.decode_partial(spec, q.reshape(B, spec.n_q_heads, d), cache.k[layer], cache.v[layer],
+                                  cache.seq_len, q_pos, k_new=kn, v_new=vn)
+
+    def forward(self, ops, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, cache, q_pos: torch.Tensor,
+                layer: int = 0, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode step (arguments as `partial`): every rank's part, all-gathered over `group`
+        and merged. Returns the full output [B, Hq, d] on every rank."""
+        import torch.distributed as dist
+
+        o, lse = self.partial(ops, q, k_new, v_new, cache, q_pos, layer)
+        if self.world == 1:
+            o_all, lse_all = o.unsqueeze(0), lse.unsqueeze(0)
+        else:
+            o_all = torch.empty((self.world,) + tuple(o.shape), dtype=o.dtype, device=o.device)
+            lse_all = torch.empty((self.world,) + tuple(lse.shape), dtype=lse.dtype, device=lse.device)
+            dist.all_gather_into_tensor(o_all.view(-1), o.view(-1), group=group)
+            dist.all_gather_into_tensor(lse_all.view(-1), lse.view(-1), group=group)
+        return ops.merge_partials(o_all, lse_all, out=out)
+
+
 class NcclDist:
     """aihost_attn_dist: the library's NCCL communicator for one rank (one process per GPU)."""
 
@@ -234,4 +289,4 @@ class NcclDist:
             self._h = None
 
 
-__all__ = ["HeadShard", "RowShard", "NcclDist"]
+__all__ = ["HeadShard", "RowShard", "ContextShard", "NcclDist"]

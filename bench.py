@@ -42,11 +42,13 @@ def parse_args():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode object")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time")
-    ap.add_argument("--shard", default="seq", choices=["seq", "heads", "rows"],
+    ap.add_argument("--shard", default="seq", choices=["seq", "heads", "rows", "context"],
                     help="N>1: seq = every rank runs its own sequences (weak scaling); heads = the KV heads "
                          "of one problem are split over the ranks and the head outputs all-gathered (strong); "
                          "rows = prefill configs: the query rows of one sequence are split into causal-balanced "
-                         "blocks and the row blocks all-gathered (strong; for Hkv < N)")
+                         "blocks and the row blocks all-gathered (strong; for Hkv < N); context = decode "
+                         "configs: every sequence's cached rows split into N chunks, partial results merged "
+                         "(strong; for Hkv < N)")
     ap.add_argument("--layers", type=int, default=0,
                     help="decode configs: also time a CUDA graph of this many layers with distinct caches "
                          "(rotating caches: HBM throughput instead of single-call latency); adds a `layers` object")
@@ -215,6 +217,35 @@ def device_inputs(cfg, device, rank):
     return inp
 
 
+def context_inputs(cfg, device, rank, world):
+    """Rank `rank`'s chunk of every sequence's cached rows of `cfg` (the same seeded problem on
+    every rank), in a local cache with the same capacity; seq_len = local rows."""
+    import torch
+
+    from aihost_b200.ops import row_bytes
+    from aihost_b200.shard import ContextShard
+
+    inp = device_inputs(cfg, device, 0)
+    sh = ContextShard(rank, world)
+    cap = inp["capacity"]
+    rb = row_bytes(cfg.kv_dtype, cfg.head_dim) * cfg.n_kv_heads
+    local_rows = []
+    for name in ("k_cache", "v_cache"):
+        full = inp[name].view(cfg.batch, cap, rb)
+        local = torch.zeros_like(full)
+        local_rows = []
+        for b, length in enumerate(inp["lengths"]):
+            lo, hi = sh.chunk(length)
+            local[b, : hi - lo] = full[b, lo:hi]
+            local_rows.append(hi - lo)
+        inp[name] = local.reshape(-1)
+    inp["global_lengths"] = list(inp["lengths"])
+    inp["q_pos"] = inp["seq_len"]
+    inp["lengths"] = local_rows
+    inp["seq_len"] = torch.tensor(local_rows, dtype=torch.int32, device=device)
+    return inp, sh
+
+
 def shard_inputs(cfg, device, rank, world):
     """This rank's share of `cfg` under KV-head sharding: its Q / new K / V heads and its local
     cache slice (seeded per rank), laid out with the shard's (16-byte padded) token stride."""
@@ -250,6 +281,7 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rows = None
+    ctxs = None
     if shard_mode == "heads":
         inp, spec, shard, local_cfg = shard_inputs(cfg, device, rank, world)
     else:
@@ -261,6 +293,10 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
                 raise SystemExit("--shard rows needs a single-sequence prefill config")
             inp = device_inputs(cfg, device, 0)  # one problem, the same seeded inputs on every rank
             rows = RowShard(cfg.n_new, inp["lengths"][0], rank, world)
+        elif shard_mode == "context":
+            if cfg.n_new != 1:
+                raise SystemExit("--shard context needs a decode config")
+            inp, ctxs = context_inputs(cfg, device, rank, world)
         else:
             inp = device_inputs(cfg, device, rank)
         spec, local_cfg = cfg.spec(inp["capacity"]), cfg
@@ -270,8 +306,11 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
     cache.seq_len, cache.host_len = inp["seq_len"], list(lengths)
     q, kn, vn = inp["q"], inp["k_new"], inp["v_new"]
     ops = ComputeOps(ctx)
-    out = ops.attention_layer(q, kn, vn, cache)  # also reserves scratch
-    w = work(local_cfg, lengths)  # this rank's work
+    if ctxs is not None:  # every rank serves all B tokens
+        out = ctxs.forward(ops, q, kn, vn, cache, inp["q_pos"])
+    else:
+        out = ops.attention_layer(q, kn, vn, cache)  # also reserves scratch
+    w = work(local_cfg, lengths)  # this rank's work (context mode: its chunk of the rows)
     need_flush = w["bytes"] < 2 * 126e6  # L2 is 126 MB: flush unless the step streams more than 2x that
     flush = torch.empty(flush_bytes, dtype=torch.uint8, device=device) if need_flush else None
 
@@ -295,6 +334,8 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
             shard.forward(nccl, ops, q, kn, vn, cache, out=result)
         elif rows is not None:
             rows.forward(ops, q, kn, vn, cache, out=result)
+        elif ctxs is not None:
+            ctxs.forward(ops, q, kn, vn, cache, inp["q_pos"], out=result)
         else:
             ops.attention_layer(q, kn, vn, cache, out=out)
 
@@ -366,7 +407,8 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
         torch.cuda.synchronize()
         nccl.close()
     return dict(ms=ms, wall=wall, kern=kern, launches=launches, e2e_ms=e_ms, h2d=h2d, d2h=d2h, work=w,
-                lengths=lengths, flushed=need_flush, sharded=shard is not None or rows is not None,
+                lengths=inp.get("global_lengths", lengths), flushed=need_flush,
+                sharded=shard is not None or rows is not None or ctxs is not None,
                 rank_flops=(4.0 * cfg.n_q_heads * cfg.head_dim * rows.pairs(rank) if rows is not None else None),
                 rank_rows=(rows.rows if rows is not None else None))
 
@@ -642,6 +684,7 @@ def main():
     flush_bytes = 512 << 20
     heads = args.shard == "heads"
     row_mode = args.shard == "rows"
+    cp_mode = args.shard == "context"
     r = bench_ours(cfg, args.steps, args.warmup, device, ctx, flush_bytes, dist_on, shard_mode=args.shard)
     main_res = summarize(cfg, r, ws, dist_on, pk, pk_kind)
     dec = None
@@ -666,7 +709,7 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": main_res["value"], "unit": main_res["unit"], "n_gpus": ws,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": main_res["ms_per_step"],
-                "higher_is_better": True, "scaling": "strong" if (heads or row_mode) else "weak",
+                "higher_is_better": True, "scaling": "strong" if (heads or row_mode or cp_mode) else "weak",
                 "vs_baseline": None,
                 "dtype": "f16 (fp32 accumulate)" if cfg.q_dtype == 1 else "f32",
                 "data": "synthetic (seeded SplitMix64 + Box-Muller, no model weights)",
@@ -675,7 +718,10 @@ def main():
                                            if heads else
                                            f"query rows split over {ws} ranks (causal-balanced 128-row blocks, "
                                            f"rank 0 rows {r['rank_rows']}) + NCCL all-gather of row blocks"
-                                           if row_mode else "one independent sequence set per rank")
+                                           if row_mode else
+                                           f"every sequence's cached rows split into {ws} chunks (context "
+                                           f"parallel) + NCCL all-gather of (out, lse) + merge kernel"
+                                           if cp_mode else "one independent sequence set per rank")
                            if ws > 1 else "single GPU"},
                 "roofline": main_res["roofline"], "cpu_baseline": cpu, "e2e": main_res["e2e"],
                 "gpu_launches": main_res["gpu_launches"], "clocks": clk, "kernels": main_res["kernels"],

@@ -191,6 +191,33 @@ aihost_status aihost_attn_forward_sharded(aihost_attn_dist* dist, aihost_attn_ct
                                           void* k_cache, void* v_cache, const int32_t* seq_len,
                                           const int32_t* h_seq_len, void* out_gathered, void* stream);
 
+/* ---- Context parallelism for decode (layers with fewer KV heads than ranks). No counterpart
+ * in the reference, which decodes a sequence on one device (ComputeOps.cs:1015-1043). Each rank
+ * holds a contiguous chunk of every sequence's cached rows; it attends its chunk with
+ * aihost_attn_decode_partial, the ranks exchange (out, lse) with their own collective, and
+ * aihost_attn_merge_partials combines them into the unsharded result.
+ *
+ * One query row per sequence over this part's cache rows with every row visible. seq_len
+ * (device int32[batch]) holds this part's cached rows per sequence. With k_new / v_new
+ * [batch][Hkv][d] (the part that stores the new token; both or neither), the new rows are
+ * appended at row seq_len[b] first, K rotated at q_pos[b], and rows [0, seq_len[b] + 1) are
+ * attended; without them rows [0, seq_len[b]). q [batch][Hq][d]: rotated in the kernel at
+ * position q_pos[b] (device int32[batch], the token's global position) when q_pos is non-NULL
+ * and desc->rope_mode is not NONE, else used as given (q_pos is required with k_new). out
+ * [batch][Hq][d] in out_dtype, normalised over this part's rows; lse (device float[batch][Hq],
+ * may be NULL) receives ln sum_j exp(scale * q.k_j) over those rows. */
+aihost_status aihost_attn_decode_partial(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
+                                         const void* q, const void* k_new, const void* v_new, void* k_cache,
+                                         void* v_cache, const int32_t* seq_len, const int32_t* q_pos, void* out,
+                                         float* lse, void* stream);
+/* out[r] = sum_p o_parts[p][r] * exp(lse_parts[p][r] - lse[r]), lse[r] = ln sum_p exp(lse_parts[p][r]),
+ * for rows r < rows (= batch * Hq) of head_dim elements; o_parts [n_parts][rows][head_dim] and
+ * out in dtype (F32 or F16), lse_parts [n_parts][rows] fp32 (a part with lse = -inf adds
+ * nothing). lse_out (may be NULL) receives lse. */
+aihost_status aihost_attn_merge_partials(aihost_attn_ctx* ctx, int32_t n_parts, int32_t rows, int32_t head_dim,
+                                         int32_t dtype, const void* o_parts, const float* lse_parts, void* out,
+                                         float* lse_out, void* stream);
+
 /* Synchronise the context's device and read-and-clear the device status word that kernels
  * set when a bounded wait expired (AIHOST_ETIMEOUT) or a device-side length exceeded
  * kv_capacity (AIHOST_EINVAL). *out_bits receives the raw bits (may be NULL). */

@@ -150,3 +150,40 @@ def test_row_sharded_gather_matches_unsharded():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     err = q.get(timeout=5)
     assert err <= 1e-5, err
+
+
+def test_context_chunks_cover_rows_and_balance():
+    from aihost_b200.shard import ContextShard
+
+    for length in (1, 2, 7, 512, 513, 16384):
+        for world in (1, 2, 4, 8):
+            if length < world:
+                continue
+            spans = [ContextShard(r, world).chunk(length) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == length
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            sizes = [hi - lo for lo, hi in spans]
+            assert min(sizes) >= 1 and max(sizes) - min(sizes) <= 1
+    assert ContextShard(3, 4).appends and not ContextShard(0, 4).appends
+
+
+def test_context_merge_of_partials_equals_full_softmax():
+    """The merge the kernel implements: out = sum_p o_p exp(lse_p - lse), lse = ln sum_p exp(lse_p)."""
+    from aihost_b200.shard import ContextShard
+
+    rng = np.random.default_rng(7)
+    for n_rows, world in ((513, 2), (1000, 4), (9, 8)):
+        s = rng.normal(0, 3, n_rows)
+        v = rng.normal(0, 1, (n_rows, 16))
+        full = (np.exp(s - s.max()) / np.exp(s - s.max()).sum()) @ v
+        o, lse = [], []
+        for r in range(world):
+            lo, hi = ContextShard(r, world).chunk(n_rows)
+            m = s[lo:hi].max()
+            e = np.exp(s[lo:hi] - m)
+            o.append(e @ v[lo:hi] / e.sum())
+            lse.append(m + np.log(e.sum()))
+        lse = np.array(lse)
+        w = np.exp(lse - lse.max())
+        merged = (w[:, None] * np.array(o)).sum(0) / w.sum()
+        assert np.abs(merged - full).max() < 1e-12

@@ -702,6 +702,28 @@ aihost_status aihost_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_he
   return AIHOST_OK;
 }
 
+aihost_status aihost_qk_norm_rope(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
+                                  const float* weight, float eps, int32_t start_pos, float theta, int32_t rope_mode,
+                                  void* stream) {
+  if (!x || !weight) return fail(AIHOST_EINVAL, "x and weight must be non-NULL");
+  if (dtype != AIHOST_F32 && dtype != AIHOST_F16) return fail(AIHOST_EINVAL, "dtype %d must be F32 or F16", dtype);
+  if (seq < 0 || n_heads < 1 || head_dim < 2 || head_dim % 2 || head_dim > kMaxHeadDim)
+    return fail(AIHOST_EINVAL, "bad shape seq=%d n_heads=%d head_dim=%d", seq, n_heads, head_dim);
+  if (!aligned(x, dtype == AIHOST_F32 ? 4 : 2) || !aligned(weight, 4))
+    return fail(AIHOST_EINVAL, "x and weight must be aligned to their element size");
+  if (start_pos < 0) return fail(AIHOST_EINVAL, "start_pos must be >= 0");
+  if (!(eps >= 0.0f && isfinite(eps))) return fail(AIHOST_EINVAL, "eps must be a non-negative finite number");
+  if (rope_mode != AIHOST_ROPE_INTERLEAVED && rope_mode != AIHOST_ROPE_NEOX && rope_mode != AIHOST_ROPE_NONE)
+    return fail(AIHOST_EINVAL, "rope_mode %d is not a valid aihost_rope_mode", rope_mode);
+  if (rope_mode != AIHOST_ROPE_NONE && !(theta > 0.0f && isfinite(theta)))
+    return fail(AIHOST_EINVAL, "theta must be a positive finite number");
+  const RopeFreqs freqs = make_freqs(rope_mode != AIHOST_ROPE_NONE ? theta : 1.0f, head_dim);
+  cudaError_t e = launch_qk_norm_rope(x, dtype, seq, n_heads, head_dim, weight, eps, start_pos, rope_mode, freqs,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "qk norm + rope launch");
+  return AIHOST_OK;
+}
+
 aihost_status aihost_kv_append(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
                                const void* k_new, const void* v_new, void* k_cache, void* v_cache,
                                const int32_t* seq_len, void* stream) {

@@ -28,6 +28,12 @@ struct KvLayout {
 cudaError_t launch_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
                              int32_t start_pos, int32_t rope_mode, const RopeFreqs& freqs, cudaStream_t st);
 
+// In-place RMS norm of each row of x [seq, n_heads * head_dim] over the whole row (weight w
+// [head_dim] device fp32, tiled over the heads), then RoPE at start_pos + s (Qwen TypeB prologue).
+cudaError_t launch_qk_norm_rope(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
+                                const float* w, float eps, int32_t start_pos, int32_t rope_mode, const RopeFreqs& freqs,
+                                cudaStream_t st);
+
 // Append k_new/v_new [batch][n_new][Hkv][d] into cache rows [seq_len[b], seq_len[b]+n_new),
 // rotating K when rope_mode != NONE at position seq_len[b] + s, or rope_pos[b] + s when rope_pos
 // (device, per sequence) is given. Records kStatusBadLength when a row would exceed capacity.

@@ -155,6 +155,64 @@ __global__ void stage_kv_kernel(const uint8_t* __restrict__ k_cache, const uint8
 
 }  // namespace
 
+// Qwen TypeB Q/K prologue (Compute/Formats/QwenHybridFormat.cs:141-142): one CTA per token row
+// of x [seq, n_heads * head_dim]. The reference's LayerNorm (ComputeShaders.cs:249-277) takes the
+// RMS over the whole row, all heads together, and multiplies by a head_dim weight tiled over the
+// heads (TransformerBase.cs:301-319); ApplyRoPEFull then rotates each head. Here both happen in
+// one pass over the row: sum of squares (block reduction), then per rotation pair
+// x / rms * w and the rotation, stored in place with one rounding.
+template <typename T>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(T* __restrict__ x, int32_t n_heads, int32_t head_dim,
+                                                           const float* __restrict__ w, float eps, int32_t start_pos,
+                                                           int32_t rope_mode, RopeFreqs freqs) {
+  __shared__ float part[8];
+  const int32_t cols = n_heads * head_dim;
+  T* row = x + static_cast<int64_t>(blockIdx.x) * cols;
+  float acc = 0.0f;
+  for (int32_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    const float v = ld_as_float(row + i);
+    acc = fmaf(v, v, acc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) total += part[i];
+  const float rms = sqrtf(total / static_cast<float>(cols) + eps);
+  const int32_t half = head_dim / 2;
+  const float pos = static_cast<float>(start_pos + static_cast<int32_t>(blockIdx.x));
+  for (int32_t p = threadIdx.x; p < n_heads * half; p += blockDim.x) {
+    const int32_t h = p / half, i = p % half;
+    const int32_t i1 = rope_mode == AIHOST_ROPE_NEOX ? i : 2 * i;
+    const int32_t i2 = rope_mode == AIHOST_ROPE_NEOX ? i + half : 2 * i + 1;
+    T* base = row + static_cast<int64_t>(h) * head_dim;
+    float x1 = ld_as_float(base + i1) / rms * w[i1];
+    float x2 = ld_as_float(base + i2) / rms * w[i2];
+    if (rope_mode != AIHOST_ROPE_NONE) {
+      float sn, cs;
+      sincosf(__fmul_rn(pos, freqs.f[i]), &sn, &cs);
+      rotate_pair(x1, x2, cs, sn);
+    }
+    st_from_float(base + i1, x1);
+    st_from_float(base + i2, x2);
+  }
+}
+
+cudaError_t launch_qk_norm_rope(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
+                                const float* w, float eps, int32_t start_pos, int32_t rope_mode, const RopeFreqs& freqs,
+                                cudaStream_t st) {
+  if (seq == 0) return cudaSuccess;
+  if (dtype == AIHOST_F32)
+    qk_norm_rope_kernel<float><<<seq, 256, 0, st>>>(static_cast<float*>(x), n_heads, head_dim, w, eps, start_pos,
+                                                     rope_mode, freqs);
+  else
+    qk_norm_rope_kernel<__half><<<seq, 256, 0, st>>>(static_cast<__half*>(x), n_heads, head_dim, w, eps, start_pos,
+                                                      rope_mode, freqs);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
                              int32_t start_pos, int32_t rope_mode, const RopeFreqs& freqs, cudaStream_t st) {
   const int64_t total = static_cast<int64_t>(seq) * n_heads * (head_dim / 2);

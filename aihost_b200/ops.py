@@ -183,6 +183,15 @@ class ComputeOps:
         check(lib().aihost_rope_full(_ptr(tensor), dtype_code(tensor), seq, num_heads, head_dim, int(start_position),
                                      float(theta), rope_mode, _stream(self.stream)))
 
+    def qk_norm_rope(self, tensor: torch.Tensor, weight: torch.Tensor, start_position: int, num_heads: int,
+                     head_dim: int, theta: float = 10000.0, eps: float = 1e-5,
+                     rope_mode: int = ROPE_INTERLEAVED) -> None:
+        """Qwen TypeB prologue (QwenHybridFormat.cs:141-142) in place on tensor [seq, num_heads*head_dim]:
+        LayerNorm over each whole row with weight [head_dim] (fp32) tiled over the heads, then RoPE."""
+        seq = tensor.shape[0]
+        check(lib().aihost_qk_norm_rope(_ptr(tensor), dtype_code(tensor), seq, num_heads, head_dim, _ptr(weight),
+                                        float(eps), int(start_position), float(theta), rope_mode, _stream(self.stream)))
+
     def multi_head_attention(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, num_heads: int,
                              start_position: int = 0, out_dtype: torch.dtype | None = None) -> torch.Tensor:
         """MultiHeadAttention (ComputeOps.cs:1055-1102) over rotated Q [S, Hq*d], K/V [Lk, Hkv*d]."""

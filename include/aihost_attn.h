@@ -131,6 +131,16 @@ aihost_status aihost_rope_full(void* x, int32_t dtype, int32_t seq, int32_t n_he
                                int32_t head_dim, int32_t start_pos, float theta, int32_t rope_mode,
                                void* stream);
 
+/* Qwen TypeB Q/K prologue (Compute/Formats/QwenHybridFormat.cs:141-142) in one pass, in place on
+ * x [seq, n_heads*head_dim] (F32 or F16): ComputeOps.LayerNorm (ComputeOps.cs:517-542) of each
+ * token row over the whole row, all heads together (rms = sqrt(mean(x^2) + eps), x = x / rms *
+ * w[i % head_dim], the head_dim weight tiled over the heads as TransformerBase.cs:301-319 does),
+ * then ApplyRoPEFull at start_pos + s. weight: device fp32 [head_dim]; the reference's eps is
+ * 1e-5. Call it on Q and on the new K before aihost_attn_forward with rope_mode NONE. */
+aihost_status aihost_qk_norm_rope(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
+                                  const float* weight, float eps, int32_t start_pos, float theta, int32_t rope_mode,
+                                  void* stream);
+
 /* KVCache.Add(layer, K, V) (Inference/InferenceEngine.cs:598-622) without the per-token
  * reallocation: copies (and converts / Q8_0-quantises) k_new, v_new [batch][n_new][Hkv][d]
  * into cache rows [seq_len[b], seq_len[b] + n_new). No rotation. */

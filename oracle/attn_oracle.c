@@ -142,6 +142,25 @@ static void rope_row(float* x, int32_t head_dim, int32_t pos, float theta, int32
   }
 }
 
+void oracle_qk_norm_rope(float* x, int32_t seq, int32_t n_heads, int32_t head_dim, const float* w, float eps,
+                         int32_t start_pos, float theta, int32_t rope_mode) {
+  const int32_t cols = n_heads * head_dim;
+  for (int32_t s = 0; s < seq; ++s) {
+    float* row = x + (int64_t)s * cols;
+    float part[256];
+    for (int t = 0; t < 256; ++t) {  /* thread t of the workgroup: elements t, t + 256, ... */
+      float acc = 0.0f;
+      for (int32_t i = t; i < cols; i += 256) acc += row[i] * row[i];
+      part[t] = acc;
+    }
+    for (int h = 128; h > 0; h >>= 1)
+      for (int t = 0; t < h; ++t) part[t] += part[t + h];
+    const float rms = sqrtf(part[0] / (float)cols + eps);
+    for (int32_t i = 0; i < cols; ++i) row[i] = (row[i] / rms) * w[i % head_dim];
+  }
+  oracle_rope_full(x, seq, n_heads, head_dim, start_pos, theta, rope_mode);
+}
+
 void oracle_rope_full(float* x, int32_t seq, int32_t n_heads, int32_t head_dim, int32_t start_pos,
                       float theta, int32_t rope_mode) {
   if (rope_mode == AIHOST_ROPE_NONE) return;

@@ -56,6 +56,14 @@ float oracle_rope_freq(float theta, int32_t pair, int32_t head_dim);
 void oracle_rope_full(float* x, int32_t seq, int32_t n_heads, int32_t head_dim, int32_t start_pos,
                       float theta, int32_t rope_mode);
 
+/* Qwen TypeB Q/K prologue (Compute/Formats/QwenHybridFormat.cs:141-142): ComputeOps.LayerNorm
+ * (ComputeOps.cs:517-542, shader ComputeShaders.cs:249-277) of each token row of x
+ * [seq, n_heads*head_dim] over the whole row, with the per-head weight w [head_dim] tiled over the
+ * heads (TransformerBase.cs:301-319), then ApplyRoPEFull at start_pos. The sum of squares follows
+ * the shader's order: 256 strided partial sums, then a halving tree. */
+void oracle_qk_norm_rope(float* x, int32_t seq, int32_t n_heads, int32_t head_dim, const float* w, float eps,
+                         int32_t start_pos, float theta, int32_t rope_mode);
+
 /* MultiHeadAttention over fp32 K/V that are already rotated.
  * q [n_q, Hq*d], out [n_q, Hq*d]; k/v row r, head h at k[r*kv_row_stride + h*d].
  * n_q == 1: FusedMHAGenerate; n_q > 1: per-head causal chain with j > start_pos + i masked. */

@@ -41,6 +41,7 @@ def lib() -> ctypes.CDLL:
         L.oracle_q8_0_dequantize.argtypes = [vp, i64, vp]
         L.oracle_rope_freq.argtypes, L.oracle_rope_freq.restype = [f32, i32, i32], f32
         L.oracle_rope_full.argtypes = [vp, i32, i32, i32, i32, f32, i32]
+        L.oracle_qk_norm_rope.argtypes = [vp, i32, i32, i32, vp, f32, i32, f32, i32]
         L.oracle_mha.argtypes = [vp, vp, vp, i64, i32, i32, i32, i32, i32, i32, f32, i32, vp]
         L.oracle_mha.restype = i32
         L.oracle_attn_forward.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, i32]
@@ -90,6 +91,16 @@ def rope_full(x: np.ndarray, start_pos: int, n_heads: int, head_dim: int, theta:
     """ApplyRoPEFull on a copy of x [seq, n_heads*head_dim] (fp32)."""
     y = np.ascontiguousarray(x, dtype=np.float32).copy()
     lib().oracle_rope_full(_p(y), y.shape[0], n_heads, head_dim, start_pos, theta, mode)
+    return y
+
+
+def qk_norm_rope(x: np.ndarray, w: np.ndarray, start_pos: int, n_heads: int, head_dim: int, theta: float,
+                 eps: float = 1e-5, mode: int = 0) -> np.ndarray:
+    """Qwen TypeB prologue on a copy of x [seq, n_heads*head_dim] (fp32): RMS over each whole
+    row with the per-head weight w [head_dim] tiled over the heads, then ApplyRoPEFull."""
+    y = np.ascontiguousarray(x, dtype=np.float32).copy()
+    wf = np.ascontiguousarray(w, dtype=np.float32)
+    lib().oracle_qk_norm_rope(_p(y), y.shape[0], n_heads, head_dim, _p(wf), eps, start_pos, theta, mode)
     return y
 
 

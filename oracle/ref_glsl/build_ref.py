@@ -35,6 +35,7 @@ SHADERS = {
     "rowwise_softmax": "_inlineRowwiseSoftmax",
     "slice_cols": "_inlineSliceCols",
     "scatter_cols": "_inlineScatterCols",
+    "layernorm": "_inlineLayerNorm",
 }
 
 BLOCK_RE = re.compile(

@@ -27,6 +27,7 @@ AIHOST_SHADER(causal_mask)
 AIHOST_SHADER(rowwise_softmax)
 AIHOST_SHADER(slice_cols)
 AIHOST_SHADER(scatter_cols)
+AIHOST_SHADER(layernorm)
 #undef AIHOST_SHADER
 
 namespace {
@@ -46,6 +47,15 @@ void ApplyRoPEFull(float* x, int seqLen, int numHeads, int headDim, uint32_t sta
   sh_rope_full::bind(1, p);
   const uint32_t total = uint32_t(seqLen * numHeads * headDim / 2);
   sh_rope_full::run((total + 255u) / 256u, 1, 1);
+}
+
+// LayerNorm (ComputeOps.cs:517-542): params {rows, cols, eps}, one workgroup per row.
+void LayerNorm(float* x, int rows, int cols, const float* w, float eps) {
+  uint32_t p[3] = {uint32_t(rows), uint32_t(cols), fbits(eps)};
+  sh_layernorm::bind(0, x);
+  sh_layernorm::bind(1, const_cast<float*>(w));
+  sh_layernorm::bind(2, p);
+  sh_layernorm::run(uint32_t(rows), 1, 1);
 }
 
 // Concat axis 0 (ComputeOps.cs:424-453): params {rows_a, rows_b, cols}.
@@ -172,6 +182,18 @@ extern "C" {
 
 // ApplyRoPEFull on x [seq, n_heads * head_dim] in place.
 int ref_rope_full(float* x, int seq, int n_heads, int head_dim, int start, float theta) {
+  ApplyRoPEFull(x, seq, n_heads, head_dim, uint32_t(start), theta);
+  return 0;
+}
+
+// Qwen TypeB Q/K prologue (QwenHybridFormat.cs:141-142): LayerNorm of each row of
+// x [seq, n_heads * head_dim] with the head_dim weight tiled over the heads
+// (TransformerBase.GetOrBuildTiledNorm), then ApplyRoPEFull at start.
+int ref_qk_norm_rope(float* x, int seq, int n_heads, int head_dim, const float* w_head, float eps, int start,
+                     float theta) {
+  std::vector<float> tiled(size_t(n_heads) * head_dim);
+  for (int h = 0; h < n_heads; ++h) std::memcpy(tiled.data() + size_t(h) * head_dim, w_head, sizeof(float) * head_dim);
+  LayerNorm(x, seq, n_heads * head_dim, tiled.data(), eps);
   ApplyRoPEFull(x, seq, n_heads, head_dim, uint32_t(start), theta);
   return 0;
 }

@@ -25,6 +25,7 @@ def lib():
         L = ctypes.CDLL(str(LIB_PATH))
         vp, i32, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
         L.ref_rope_full.argtypes = [vp, i32, i32, i32, i32, f32]
+        L.ref_qk_norm_rope.argtypes = [vp, i32, i32, i32, vp, f32, i32, f32]
         L.ref_mha.argtypes = [vp, i32, vp, vp, i32, i32, i32, i32, i32, vp]
         L.ref_layer_attention.argtypes = [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32, vp, vp, vp]
         _LIB = L
@@ -38,6 +39,13 @@ def _f(a):
 def rope_full(x, start, n_heads, head_dim, theta):
     y = _f(x).copy()
     lib().ref_rope_full(y.ctypes.data, y.shape[0], n_heads, head_dim, start, theta)
+    return y
+
+
+def qk_norm_rope(x, w, start, n_heads, head_dim, theta, eps=1e-5):
+    y = _f(x).copy()
+    wf = _f(w)
+    lib().ref_qk_norm_rope(y.ctypes.data, y.shape[0], n_heads, head_dim, wf.ctypes.data, eps, start, theta)
     return y
 
 

@@ -70,3 +70,34 @@ def test_live_pin_against_reference_shaders():
         o2 = orc.mha(qr, np.concatenate([kc, kr]), np.concatenate([vc, vn]), hq, P, mode=orc.FAITHFUL)
         assert np.array_equal(k_all[P:], kr)
         assert np.array_equal(out, o2)
+
+
+def _qk_golden():
+    import json
+    from pathlib import Path
+
+    z = np.load(Path(__file__).resolve().parent / "golden" / "qk_norm_golden.npz")
+    return z, json.loads(bytes(z["meta"]).decode())
+
+
+def test_qk_norm_rope_oracle_matches_reference_shader_golden():
+    """The oracle's Qwen TypeB prologue equals the reference's layer_norm + rope_full shaders bit for bit."""
+    from oracle import oracle as orc
+
+    z, meta = _qk_golden()
+    for i, m in enumerate(meta):
+        y = orc.qk_norm_rope(z[f"x{i}"], z[f"w{i}"], m["start"], m["n_heads"], m["head_dim"], m["theta"], m["eps"])
+        assert np.array_equal(y, z[f"y{i}"]), (i, float(np.abs(y - z[f"y{i}"]).max()))
+
+
+def test_qk_norm_rope_oracle_matches_live_reference_shader():
+    from oracle import oracle as orc
+    from oracle.ref_glsl import ref
+
+    if not ref.available():
+        pytest.skip("reference-shader harness not built (no reference checkout)")
+    rng = np.random.default_rng(5)
+    for seq, h, d, start in [(2, 3, 64, 4), (6, 8, 128, 100), (3, 5, 256, 2047), (2, 40, 128, 31)]:
+        x = rng.normal(0, 2.0, (seq, h * d)).astype(np.float32)
+        w = rng.normal(1.0, 0.3, d).astype(np.float32)
+        assert np.array_equal(orc.qk_norm_rope(x, w, start, h, d, 1e6), ref.qk_norm_rope(x, w, start, h, d, 1e6))

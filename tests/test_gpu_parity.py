@@ -294,3 +294,46 @@ def test_device_length_over_capacity_reports_status(ctx):
     with pytest.raises(AttnError) as ei:
         gpu_forward(ctx, cfg, inp, pass_host_len=False)
     assert ei.value.status == EINVAL
+
+
+# ---------------------------------------------------------------- Qwen TypeB Q/K prologue
+
+def test_qk_norm_rope_matches_reference_shader_golden(ctx):
+    """aihost_qk_norm_rope (fp32) against the reference's layer_norm + rope_full shaders (golden)."""
+    import json
+    from pathlib import Path
+
+    from aihost_b200.ops import ComputeOps
+
+    z = np.load(Path(__file__).resolve().parent / "golden" / "qk_norm_golden.npz")
+    meta = json.loads(bytes(z["meta"]).decode())
+    dev = torch.device("cuda", 0)
+    for i, m in enumerate(meta):
+        x = torch.from_numpy(z[f"x{i}"]).to(dev)
+        w = torch.from_numpy(z[f"w{i}"]).to(dev)
+        ComputeOps(ctx).qk_norm_rope(x, w, m["start"], m["n_heads"], m["head_dim"], m["theta"], m["eps"])
+        torch.cuda.synchronize()
+        ref = z[f"y{i}"]
+        err = float(np.abs(x.cpu().numpy() - ref).max())
+        assert err <= 2e-5 * max(1.0, float(np.abs(ref).max())), (i, err)
+
+
+@pytest.mark.parametrize("mode", [ROPE_INTERLEAVED, ROPE_NEOX, ROPE_NONE])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_qk_norm_rope_matches_oracle(ctx, mode, dtype):
+    from aihost_b200.ops import ComputeOps
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(11)
+    dev = torch.device("cuda", 0)
+    for seq, h, d, start in [(33, 14, 64, 0), (5, 32, 128, 4000), (300, 2, 64, 17), (3, 16, 256, 99)]:
+        x = rng.normal(0, 1.5, (seq, h * d)).astype(np.float32)
+        w = rng.normal(1.0, 0.2, d).astype(np.float32)
+        xt = torch.from_numpy(x).to(dtype).to(dev)
+        x_in = xt.float().cpu().numpy()  # the input as the kernel sees it (fp16-rounded for fp16), before the in-place call
+        ComputeOps(ctx).qk_norm_rope(xt, torch.from_numpy(w).to(dev), start, h, d, 1e6, 1e-5, mode)
+        torch.cuda.synchronize()
+        ref = orc.qk_norm_rope(x_in, w, start, h, d, 1e6, 1e-5, mode)
+        tol = 2e-5 if dtype == torch.float32 else 2e-3
+        err = float(np.abs(xt.float().cpu().numpy() - ref).max())
+        assert err <= tol * max(1.0, float(np.abs(ref).max())), (seq, h, d, err)

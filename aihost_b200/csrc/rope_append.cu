@@ -54,6 +54,9 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
                                  const int32_t* __restrict__ rope_pos) {
   constexpr int E = D / 32;
   griddep_launch_dependents();  // the prefill that follows may start its own set-up now
+  __shared__ float s_f[D / 2];  // RoPE frequencies, read below by lane-dependent index
+  for (int i = threadIdx.x; i < D / 2; i += blockDim.x) s_f[i] = freqs.f[i];
+  __syncthreads();
   const int32_t lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t rows = static_cast<int64_t>(batch) * n_new * n_kv_heads;
@@ -75,7 +78,7 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
 
   if (is_k && rope_mode != AIHOST_ROPE_NONE) {
     const float pos = static_cast<float>(rope_pos ? rope_pos[b] + s : t);
-    rope_row_warp<E>(x, lane, pos, rope_mode, freqs);
+    rope_row_warp<E>(x, lane, pos, rope_mode, static_cast<const float*>(s_f));
   }
 
   uint8_t* dst = (is_k ? k_cache : v_cache) + b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride +
@@ -92,6 +95,9 @@ __global__ void stage_q_kernel(const float* __restrict__ q, __half* __restrict__
                                RopeFreqs freqs) {
   constexpr int E = D / 32;
   griddep_launch_dependents();  // the prefill that follows may start its own set-up now
+  __shared__ float s_f[D / 2];  // RoPE frequencies, read below by lane-dependent index
+  for (int i = threadIdx.x; i < D / 2; i += blockDim.x) s_f[i] = freqs.f[i];
+  __syncthreads();
   const int32_t lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= static_cast<int64_t>(batch) * n_q * n_heads) return;
@@ -103,7 +109,7 @@ __global__ void stage_q_kernel(const float* __restrict__ q, __half* __restrict__
   for (int e = 0; e < E; ++e) x[e] = src[e];
   if (rope_mode != AIHOST_ROPE_NONE) {
     const int32_t start = seq_len ? seq_len[b] : start_scalar;
-    rope_row_warp<E>(x, lane, static_cast<float>(start + s), rope_mode, freqs);
+    rope_row_warp<E>(x, lane, static_cast<float>(start + s), rope_mode, static_cast<const float*>(s_f));
   }
   __half2* d2 = reinterpret_cast<__half2*>(dst + row * D + lane * E);
 #pragma unroll
@@ -200,10 +206,132 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(T* __restrict__ x, in
   }
 }
 
+__device__ __forceinline__ void load8(const float* p, float* v) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __half* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8(__half* p, const float* v) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// The same prologue with the row held in registers: a unit is the two 8-element chunks at
+// within-head offsets o and o + head_dim/2 (o < head_dim/2), so a NeoX pair never leaves its
+// thread; every thread loads its units with 16- or 32-byte loads before the reduction, then
+// normalises, rotates and stores them. Needs head_dim % 16 == 0 and at most 256*K units per row.
+// The angles go through the reduced-range sincos (absolute error ~5e-7, positions up to ~4e5).
+template <typename T, int K>
+__global__ void __launch_bounds__(256, K == 1 ? 6 : 3) qk_norm_rope_vec_kernel(T* __restrict__ x, int32_t n_heads, int32_t head_dim,
+                                                               const float* __restrict__ w, float eps,
+                                                               int32_t start_pos, int32_t rope_mode, RopeFreqs freqs) {
+  __shared__ float part[8];
+  // the weight and the RoPE frequencies, read by lane-dependent index below: from shared memory
+  // rather than from the kernel parameters (divergent constant reads serialise per address)
+  __shared__ __align__(16) float s_w[kMaxHeadDim];
+  __shared__ float s_f[kMaxHeadDim / 2];
+  const int32_t cols = n_heads * head_dim, half = head_dim / 2, per_head = head_dim / 16;
+  const int32_t units = n_heads * per_head;
+  if (threadIdx.x < head_dim) s_w[threadIdx.x] = w[threadIdx.x];
+  if (threadIdx.x < half) s_f[threadIdx.x] = freqs.f[threadIdx.x];
+  T* row = x + static_cast<int64_t>(blockIdx.x) * cols;
+  float v[K][16];
+  float acc = 0.0f;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int32_t u = threadIdx.x + 256 * k;
+    if (u < units) {
+      const int32_t a = (u / per_head) * head_dim + (u % per_head) * 8;
+      load8(row + a, v[k]);
+      load8(row + a + half, v[k] + 8);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc = fmaf(v[k][e], v[k][e], acc);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) total += part[i];
+  // x * (1 / rms) instead of the reference's x / rms: at most one ulp apart, and the division
+  // dominated this kernel's instruction count
+  const float inv_rms = __frcp_rn(sqrtf(total / static_cast<float>(cols) + eps));
+  const float pos = static_cast<float>(start_pos + static_cast<int32_t>(blockIdx.x));
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int32_t u = threadIdx.x + 256 * k;
+    if (u >= units) continue;
+    const int32_t o = (u % per_head) * 8;
+    const int32_t a = (u / per_head) * head_dim + o;
+    float wa[8], wb[8];
+    load8(s_w + o, wa);
+    load8(s_w + half + o, wb);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      v[k][e] = v[k][e] * inv_rms * wa[e];
+      v[k][8 + e] = v[k][8 + e] * inv_rms * wb[e];
+    }
+    if (rope_mode == AIHOST_ROPE_INTERLEAVED) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float sn, cs;
+        sincos_reduced(__fmul_rn(pos, s_f[o / 2 + q]), &sn, &cs);
+        rotate_pair(v[k][2 * q], v[k][2 * q + 1], cs, sn);
+        sincos_reduced(__fmul_rn(pos, s_f[half / 2 + o / 2 + q]), &sn, &cs);
+        rotate_pair(v[k][8 + 2 * q], v[k][8 + 2 * q + 1], cs, sn);
+      }
+    } else if (rope_mode == AIHOST_ROPE_NEOX) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float sn, cs;
+        sincos_reduced(__fmul_rn(pos, s_f[o + e]), &sn, &cs);
+        rotate_pair(v[k][e], v[k][8 + e], cs, sn);
+      }
+    }
+    store8(row + a, v[k]);
+    store8(row + a + half, v[k] + 8);
+  }
+}
+
 cudaError_t launch_qk_norm_rope(void* x, int32_t dtype, int32_t seq, int32_t n_heads, int32_t head_dim,
                                 const float* w, float eps, int32_t start_pos, int32_t rope_mode, const RopeFreqs& freqs,
                                 cudaStream_t st) {
   if (seq == 0) return cudaSuccess;
+  const int64_t units = static_cast<int64_t>(n_heads) * (head_dim / 16);
+  if (head_dim % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && units <= 1024) {
+#define AIHOST_QKN(T, K)                                                                                           \
+  qk_norm_rope_vec_kernel<T, K><<<seq, 256, 0, st>>>(static_cast<T*>(x), n_heads, head_dim, w, eps, start_pos, \
+                                                    rope_mode, freqs)
+    if (dtype == AIHOST_F32) {
+      if (units <= 256) AIHOST_QKN(float, 1);
+      else if (units <= 512) AIHOST_QKN(float, 2);
+      else AIHOST_QKN(float, 4);
+    } else {
+      if (units <= 256) AIHOST_QKN(__half, 1);
+      else if (units <= 512) AIHOST_QKN(__half, 2);
+      else AIHOST_QKN(__half, 4);
+    }
+#undef AIHOST_QKN
+    return cudaGetLastError();
+  }
   if (dtype == AIHOST_F32)
     qk_norm_rope_kernel<float><<<seq, 256, 0, st>>>(static_cast<float*>(x), n_heads, head_dim, w, eps, start_pos,
                                                      rope_mode, freqs);

@@ -19,17 +19,22 @@ __device__ __forceinline__ void rotate_pair(float& x1, float& x2, float c, float
   x2 = b;
 }
 
+__device__ __forceinline__ float freq_at(const RopeFreqs& f, int i) { return f.f[i]; }
+__device__ __forceinline__ float freq_at(const float* f, int i) { return f[i]; }
+
 // RoPE of the row at position `pos` (ComputeShaders.cs:517-543). Interleaved pairs (2i, 2i+1)
-// sit in one lane; NEOX pairs (i, i + D/2) sit in lanes l and l ^ 16.
-template <int E>
+// sit in one lane; NEOX pairs (i, i + D/2) sit in lanes l and l ^ 16. `freqs` is the kernel's
+// RopeFreqs or a copy of it in shared memory; the lanes read different pairs, and divergent
+// reads of kernel parameters serialise per address, so hot kernels pass the shared copy.
+template <int E, typename F>
 __device__ __forceinline__ void rope_row_warp(float (&x)[E], int32_t lane, float pos, int32_t rope_mode,
-                                              const RopeFreqs& freqs) {
+                                              const F& freqs) {
   if (rope_mode == AIHOST_ROPE_INTERLEAVED) {
 #pragma unroll
     for (int e = 0; e < E; e += 2) {
       const int pair = (lane * E + e) >> 1;
       float sn, cs;
-      sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
+      sincosf(__fmul_rn(pos, freq_at(freqs, pair)), &sn, &cs);
       rotate_pair(x[e], x[e + 1], cs, sn);
     }
   } else if (rope_mode == AIHOST_ROPE_NEOX) {
@@ -39,7 +44,7 @@ __device__ __forceinline__ void rope_row_warp(float (&x)[E], int32_t lane, float
       const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
       const int pair = (lane & 15) * E + e;
       float sn, cs;
-      sincosf(__fmul_rn(pos, freqs.f[pair]), &sn, &cs);
+      sincosf(__fmul_rn(pos, freq_at(freqs, pair)), &sn, &cs);
       float x1 = lo ? x[e] : other, x2 = lo ? other : x[e];
       rotate_pair(x1, x2, cs, sn);
       x[e] = lo ? x1 : x2;

@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="decode configs: also time a CUDA graph of this many layers with distinct caches "
                          "(rotating caches: HBM throughput instead of single-call latency); adds a `layers` object")
+    ap.add_argument("--op", default="attention", choices=["attention", "qk-norm-rope"],
+                    help="qk-norm-rope: time the Qwen TypeB Q/K prologue kernel alone (one GPU; GB/s of HBM)")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N untimed fused calls of --config and exit (the command profiled with ncu)")
     return ap.parse_args()
@@ -654,6 +656,80 @@ def _rerun(cfg, meta):
                      inp["v_cache"].numpy(), inp["seq_len"].numpy(), mode=orc.FAITHFUL, part=part)
 
 
+def bench_qk_norm(args, device, pk, pk_kind):
+    """aihost_qk_norm_rope on a Qwen TypeB-shaped Q block larger than L2: 32768 token rows of
+    16 heads x 256, fp16, in place. Algorithmic bytes per launch: the block read and written once."""
+    import torch
+
+    from aihost_b200.ops import ComputeOps, Context
+
+    seq, heads, d, theta = 32768, 16, 256, 1e7
+    g = torch.Generator(device=device).manual_seed(1234)
+    x = torch.randn(seq, heads * d, device=device, generator=g).half()
+    w = (1.0 + 0.1 * torch.randn(d, device=device, generator=g)).float()
+    nbytes = 2 * x.numel() * x.element_size()
+    clocks = ClockSampler(device.index).start()
+    with Context(device.index) as ctx:
+        ops = ComputeOps(ctx)
+        for _ in range(args.warmup):
+            ops.qk_norm_rope(x, w, 0, heads, d, theta)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in ev:
+            a.record()
+            ops.qk_norm_rope(x, w, 0, heads, d, theta)
+            b.record()
+        torch.cuda.synchronize()
+        ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+        hx = x.cpu().pin_memory()
+        e_ms = []
+        for i in range(args.steps + args.warmup):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            x.copy_(hx, non_blocking=True)
+            ops.qk_norm_rope(x, w, 0, heads, d, theta)
+            hx.copy_(x, non_blocking=True)
+            b.record()
+            b.synchronize()
+            if i >= args.warmup:
+                e_ms.append(a.elapsed_time(b))
+        ctx.sync_status()
+    clk = clocks.stop()
+    gbs = nbytes / (ms * 1e-3) * 1e-9
+    cpu = None
+    if not args.no_cpu:
+        from oracle import oracle as orc
+
+        rows = 512
+        xs = x[:rows].float().cpu().numpy()
+        wn = w.cpu().numpy()
+        t0 = time.perf_counter()
+        runs = 0
+        while True:
+            orc.qk_norm_rope(xs, wn, 0, heads, d, theta)
+            runs += 1
+            if time.perf_counter() - t0 > min(args.cpu_seconds, 5.0):
+                break
+        t = time.perf_counter() - t0
+        cpu = {"value": runs * rows * heads * d * 2 * 2 / t * 1e-9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"{rows} token rows x {heads} heads x {d}, {runs} run(s) (oracle, single-threaded fp32; "
+                         "bytes counted at the fp16 sizes)"}
+    line = {"metric": "Qwen TypeB Q/K norm + RoPE prologue, HBM GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 (fp32 math)", "data": "synthetic (torch normal)",
+            "config": {"workload": "aihost_qk_norm_rope on x [32768, 16*256] fp16, in place, theta 1e7",
+                       "l2": "inputs larger than L2 (268 MB per step)"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / pk["hbm_gbs"], "traffic": None, "kernel": "qk_norm_rope_kernel",
+                         "kernel_ms": ms, "algorithmic_per_launch": nbytes, "peak_source": f"{pk_kind} copy"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": nbytes / (statistics.mean(e_ms) * 1e-3) * 1e-9, "unit": "GB/s",
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                    "ms_per_step": statistics.mean(e_ms)},
+            "gpu_launches": args.steps, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.warmup < 3:
@@ -678,6 +754,10 @@ def main():
         profile_steps(CONFIGS[args.config], args.profile_steps, device)
         return
     pk, pk_kind = peaks()
+    if args.op == "qk-norm-rope":
+        if ws == 1:
+            bench_qk_norm(args, device, pk, pk_kind)
+        return
     ctx = Context(local)
     clocks = ClockSampler(local).start()
     cfg = CONFIGS[args.config]

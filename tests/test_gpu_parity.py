@@ -326,7 +326,9 @@ def test_qk_norm_rope_matches_oracle(ctx, mode, dtype):
 
     rng = np.random.default_rng(11)
     dev = torch.device("cuda", 0)
-    for seq, h, d, start in [(33, 14, 64, 0), (5, 32, 128, 4000), (300, 2, 64, 17), (3, 16, 256, 99)]:
+    # register-resident kernel with 1, 2 and 4 units per thread, and the scalar kernel (head_dim 40)
+    for seq, h, d, start in [(33, 14, 64, 0), (5, 32, 128, 4000), (300, 2, 64, 17), (3, 16, 256, 99), (4, 64, 128, 7),
+                             (2, 64, 256, 5), (9, 6, 40, 3)]:
         x = rng.normal(0, 1.5, (seq, h * d)).astype(np.float32)
         w = rng.normal(1.0, 0.2, d).astype(np.float32)
         xt = torch.from_numpy(x).to(dtype).to(dev)

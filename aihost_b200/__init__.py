@@ -26,7 +26,7 @@ EXPORTS = (
     "aihost_rope_full", "aihost_kv_append", "aihost_attn_sync_status", "aihost_attn_profiler_enable",
     "aihost_attn_profiler_read", "aihost_attn_profiler_reset", "aihost_attn_decode_noalloc",
     "aihost_attn_dist_unique_id", "aihost_attn_dist_init", "aihost_attn_dist_destroy", "aihost_attn_forward_sharded",
-    "aihost_attn_decode_partial", "aihost_attn_merge_partials", "aihost_qk_norm_rope",
+    "aihost_attn_decode_partial", "aihost_attn_merge_partials", "aihost_qk_norm_rope", "aihost_attn_forward_paged",
 )
 # aihost_kernel ids of the device-time profiler
 KERNEL_APPEND, KERNEL_DECODE, KERNEL_COMBINE, KERNEL_PREFILL, KERNEL_CONVERT = range(5)
@@ -84,6 +84,7 @@ def lib() -> ctypes.CDLL:
     L.aihost_attn_forward_sharded.argtypes = [vp, vp, dp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.aihost_attn_decode_partial.argtypes = [vp, dp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.aihost_attn_merge_partials.argtypes = [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]
+    L.aihost_attn_forward_paged.argtypes = [vp, dp, i32, i32, vp, vp, vp, vp, vp, i32, i32, vp, i32, vp, vp, vp, vp]
     L.aihost_qk_norm_rope.argtypes = [vp, i32, i32, i32, i32, vp, ctypes.c_float, i32, ctypes.c_float, i32, vp]
     for name in EXPORTS:
         fn = getattr(L, name)

@@ -91,6 +91,7 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 // Validates the static description; fills the resolved cache layout and scale.
 aihost_status check_desc(const aihost_attn_desc* d, KvLayout* kv, float* scale) {
+  memset(kv, 0, sizeof(*kv));  // contiguous layout: no block table
   if (!d) return fail(AIHOST_EINVAL, "desc is NULL");
   if (d->n_q_heads < 1 || d->n_kv_heads < 1)
     return fail(AIHOST_EINVAL, "n_q_heads (%d) and n_kv_heads (%d) must be >= 1", d->n_q_heads, d->n_kv_heads);
@@ -377,12 +378,20 @@ aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const
   aihost_status s = encode_f16_map(&a.q_map, q, d->head_dim, Hq, n_q, batch, D * 2, Hq * D * 2,
                                    static_cast<int64_t>(n_q) * Hq * D * 2, "q");
   if (s != AIHOST_OK) return s;
-  s = encode_f16_map(&a.k_map, kc, d->head_dim, d->n_kv_heads, kv.capacity, batch, kv.head_stride, kv.token_stride,
-                     kv.seq_stride ? kv.seq_stride : kv.token_stride * kv.capacity, "k_cache");
+  // a paged cache is one pool "sequence" of n_pages * page_rows rows; otherwise one per sequence
+  const int64_t map_rows = kv.block_table ? static_cast<int64_t>(kv.n_pages) * kv.page_rows : kv.capacity;
+  const int64_t map_seqs = kv.block_table ? 1 : batch;
+  const int64_t map_seq_stride =
+      kv.block_table ? kv.token_stride * map_rows : (kv.seq_stride ? kv.seq_stride : kv.token_stride * kv.capacity);
+  s = encode_f16_map(&a.k_map, kc, d->head_dim, d->n_kv_heads, map_rows, map_seqs, kv.head_stride, kv.token_stride,
+                     map_seq_stride, "k_cache");
   if (s != AIHOST_OK) return s;
-  s = encode_f16_map(&a.v_map, vc, d->head_dim, d->n_kv_heads, kv.capacity, batch, kv.head_stride, kv.token_stride,
-                     kv.seq_stride ? kv.seq_stride : kv.token_stride * kv.capacity, "v_cache");
+  s = encode_f16_map(&a.v_map, vc, d->head_dim, d->n_kv_heads, map_rows, map_seqs, kv.head_stride, kv.token_stride,
+                     map_seq_stride, "v_cache");
   if (s != AIHOST_OK) return s;
+  a.block_table = kv.block_table;
+  a.max_pages = kv.max_pages;
+  a.page_rows = kv.page_rows;
   a.q = q;
   a.seq_len = seq_len;
   a.start_scalar = start_scalar;
@@ -420,16 +429,21 @@ cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ct
   char saved[sizeof(g_err)];
   memcpy(saved, g_err, sizeof(g_err));
   if (a.kv.dtype == AIHOST_F16) {
-    const int64_t seq_stride = a.kv.seq_stride ? a.kv.seq_stride : a.kv.token_stride * a.kv.capacity;
-    mma = encode_f16_map(&m.k_map, a.k_cache, a.head_dim, a.n_kv_heads, a.kv.capacity, a.batch, a.kv.head_stride,
+    // a paged cache is one pool "sequence" of n_pages * page_rows rows; otherwise one per sequence
+    const int64_t rows = a.kv.block_table ? static_cast<int64_t>(a.kv.n_pages) * a.kv.page_rows : a.kv.capacity;
+    const int64_t seqs = a.kv.block_table ? 1 : a.batch;
+    const int64_t seq_stride = a.kv.block_table ? a.kv.token_stride * rows
+                                                : (a.kv.seq_stride ? a.kv.seq_stride : a.kv.token_stride * a.kv.capacity);
+    mma = encode_f16_map(&m.k_map, a.k_cache, a.head_dim, a.n_kv_heads, rows, seqs, a.kv.head_stride,
                          a.kv.token_stride, seq_stride, "k_cache", 64) == AIHOST_OK &&
-          encode_f16_map(&m.v_map, a.v_cache, a.head_dim, a.n_kv_heads, a.kv.capacity, a.batch, a.kv.head_stride,
+          encode_f16_map(&m.v_map, a.v_cache, a.head_dim, a.n_kv_heads, rows, seqs, a.kv.head_stride,
                          a.kv.token_stride, seq_stride, "v_cache", 64) == AIHOST_OK;
   } else if (a.kv.dtype == AIHOST_Q8_0) {
     const uint32_t bw = q8_box_words(a.head_dim, a.kv.head_stride);
     mma = bw && encode_q8_map(&m.k_map, a.k_cache, a.kv, a.batch, bw) == AIHOST_OK &&
           encode_q8_map(&m.v_map, a.v_cache, a.kv, a.batch, bw) == AIHOST_OK;
   }
+  if (!mma && a.kv.block_table) return cudaErrorInvalidValue;  // paged caches need the tensor-core path
   if (!mma) memcpy(g_err, saved, sizeof(g_err));  // strides TMA cannot describe: CUDA-core kernel instead
   // One CTA per <= 16 query heads: with a single head group per KV head, the CTA of the last
   // split appends the new rows itself and the last split to finish merges the partials.
@@ -572,16 +586,34 @@ aihost_status aihost_attn_reserve(aihost_attn_ctx* ctx, size_t bytes) {
   return AIHOST_OK;
 }
 
-aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
-                                  int32_t n_new, const void* q, const void* k_new, const void* v_new,
-                                  void* k_cache, void* v_cache, const int32_t* seq_len,
-                                  const int32_t* h_seq_len, void* out, void* stream) {
+// The fused op over a contiguous cache (paging NULL) or a paged fp16 pool (paging carries the
+// block table and page geometry; validated by the caller).
+static aihost_status forward_common(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, const KvLayout* paging,
+                                    int32_t batch, int32_t n_new, const void* q, const void* k_new, const void* v_new,
+                                    void* k_cache, void* v_cache, const int32_t* seq_len, const int32_t* h_seq_len,
+                                    void* out, void* stream) {
   aihost_status s = check_ctx(ctx);
   if (s != AIHOST_OK) return s;
   KvLayout kv;
   float scale;
   s = check_desc(desc, &kv, &scale);
   if (s != AIHOST_OK) return s;
+  if (paging) {
+    kv.block_table = paging->block_table;
+    kv.max_pages = paging->max_pages;
+    kv.page_rows = paging->page_rows;
+    kv.n_pages = paging->n_pages;
+    kv.seq_stride = 0;
+    // the pools must be describable by the tensor maps the kernels read them through
+    const int64_t rows = static_cast<int64_t>(kv.n_pages) * kv.page_rows;
+    CUtensorMap probe;
+    s = encode_f16_map(&probe, k_cache, desc->head_dim, desc->n_kv_heads, rows, 1, kv.head_stride, kv.token_stride,
+                       kv.token_stride * rows, "k_pool", 64);
+    if (s != AIHOST_OK) return s;
+    s = encode_f16_map(&probe, v_cache, desc->head_dim, desc->n_kv_heads, rows, 1, kv.head_stride, kv.token_stride,
+                       kv.token_stride * rows, "v_pool", 64);
+    if (s != AIHOST_OK) return s;
+  }
   if (batch < 1 || n_new < 1) return fail(AIHOST_EINVAL, "batch (%d) and n_new (%d) must be >= 1", batch, n_new);
   if (!q || !k_new || !v_new || !k_cache || !v_cache || !seq_len || !out)
     return fail(AIHOST_EINVAL, "q, k_new, v_new, k_cache, v_cache, seq_len and out must be non-NULL");
@@ -613,6 +645,41 @@ aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* 
   }
   return run_prefill(ctx, desc, kv, scale, batch, n_new, q, k_cache, v_cache, seq_len, 0, n_new, kv_rows,
                      desc->rope_mode, out, st, true);
+}
+
+aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
+                                  int32_t n_new, const void* q, const void* k_new, const void* v_new,
+                                  void* k_cache, void* v_cache, const int32_t* seq_len,
+                                  const int32_t* h_seq_len, void* out, void* stream) {
+  return forward_common(ctx, desc, nullptr, batch, n_new, q, k_new, v_new, k_cache, v_cache, seq_len, h_seq_len, out,
+                        stream);
+}
+
+aihost_status aihost_attn_forward_paged(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
+                                        int32_t n_new, const void* q, const void* k_new, const void* v_new,
+                                        void* k_pool, void* v_pool, int32_t n_pages, int32_t page_rows,
+                                        const int32_t* block_table, int32_t max_pages, const int32_t* seq_len,
+                                        const int32_t* h_seq_len, void* out, void* stream) {
+  if (!desc) return fail(AIHOST_EINVAL, "desc is NULL");
+  if (desc->kv_dtype != AIHOST_F16) return fail(AIHOST_EUNSUPPORTED, "paged caches are fp16 (kv_dtype F16)");
+  if (page_rows < 128 || page_rows % 128) return fail(AIHOST_EINVAL, "page_rows %d must be a positive multiple of 128",
+                                                      page_rows);
+  if (n_pages < 1 || max_pages < 1) return fail(AIHOST_EINVAL, "n_pages (%d) and max_pages (%d) must be >= 1", n_pages,
+                                                max_pages);
+  if (static_cast<int64_t>(n_pages) * page_rows > INT32_MAX)
+    return fail(AIHOST_EINVAL, "the pool (%d pages of %d rows) exceeds 2^31 rows", n_pages, page_rows);
+  if (desc->kv_capacity > static_cast<int64_t>(max_pages) * page_rows)
+    return fail(AIHOST_EINVAL, "kv_capacity %d exceeds max_pages * page_rows = %lld", desc->kv_capacity,
+                static_cast<long long>(max_pages) * page_rows);
+  if (!block_table || !aligned(block_table, 4)) return fail(AIHOST_EINVAL, "block_table must be a non-NULL int32 array");
+  KvLayout paging;
+  memset(&paging, 0, sizeof(paging));
+  paging.block_table = block_table;
+  paging.max_pages = max_pages;
+  paging.page_rows = page_rows;
+  paging.n_pages = n_pages;
+  return forward_common(ctx, desc, &paging, batch, n_new, q, k_new, v_new, k_pool, v_pool, seq_len, h_seq_len, out,
+                        stream);
 }
 
 aihost_status aihost_attn_mha(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t n_q, int32_t n_kv,

@@ -97,9 +97,13 @@ __device__ __forceinline__ void append_new_row(const DecodeArgs& p, int b, int k
   load_row_warp<E>(src, p.new_dtype, lane, x);
   if (is_k && p.rope_mode != AIHOST_ROPE_NONE)
     rope_row_warp<E>(x, lane, static_cast<float>(p.q_pos ? p.q_pos[b] : t), p.rope_mode, p.freqs);
-  uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(is_k ? p.k_cache : p.v_cache)) + b * p.kv.seq_stride +
-                 static_cast<int64_t>(t) * p.kv.token_stride + static_cast<int64_t>(kvh) * p.kv.head_stride;
-  store_row_warp<E>(x, lane, dst, p.kv.dtype);
+  if (!kv_row_ok(p.kv, b, t)) {  // a paged cache's block table points outside the pool
+    if (lane == 0) atomicOr(p.status, kStatusBadLength);
+  } else {
+    uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(is_k ? p.k_cache : p.v_cache)) + kv_row_offset(p.kv, b, t) +
+                   static_cast<int64_t>(kvh) * p.kv.head_stride;
+    store_row_warp<E>(x, lane, dst, p.kv.dtype);
+  }
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
@@ -605,12 +609,13 @@ __global__ void __launch_bounds__(kThreads) decode_mma_kernel(const __grid_const
         const int s = i % C::NS;
         if (!mbar_wait(&bar.empty[s], ((i / C::NS) & 1) ^ 1, p.status)) break;
         mbar_arrive_expect_tx(&bar.full[s], 2 * C::TILE_BYTES);
-        const int row = t0 + i * kTileRows;
+        // a paged cache keeps 64-row tiles inside a page: pool row and sequence coordinate 0
+        const int row = kv_phys_row(p.kv, b, t0 + i * kTileRows), bc = p.kv.block_table ? 0 : b;
         for (int kb = 0; kb < C::KB; ++kb) {
           tma_load_4d(smem + C::K_OFF + s * C::TILE_BYTES + kb * kTileRows * 128, &a.k_map, &bar.full[s], kb * 64,
-                      kvh, row, b);
+                      kvh, row, bc);
           tma_load_4d(smem + C::V_OFF + s * C::TILE_BYTES + kb * kTileRows * 128, &a.v_map, &bar.full[s], kb * 64,
-                      kvh, row, b);
+                      kvh, row, bc);
         }
       }
     }

@@ -21,7 +21,32 @@ struct KvLayout {
   int64_t seq_stride, token_stride, head_stride;
   int32_t capacity;
   int32_t dtype;  // aihost_dtype
+  // Paged cache (block_table non-NULL): row t of sequence b lives in the shared pool at row
+  // block_table[b * max_pages + t / page_rows] * page_rows + t % page_rows; seq_stride unused.
+  const int32_t* block_table;
+  int32_t max_pages, page_rows, n_pages;
 };
+
+#ifdef __CUDACC__
+// Pool row of (sequence b, row t) for a paged cache; t itself otherwise.
+__device__ __forceinline__ int32_t kv_phys_row(const KvLayout& kv, int b, int32_t t) {
+  return kv.block_table ? kv.block_table[static_cast<int64_t>(b) * kv.max_pages + t / kv.page_rows] * kv.page_rows +
+                              t % kv.page_rows
+                        : t;
+}
+// False when a paged cache's block table maps (b, t) outside the pool (the writers then skip the
+// row and record a status bit; TMA reads of such rows return zeros).
+__device__ __forceinline__ bool kv_row_ok(const KvLayout& kv, int b, int32_t t) {
+  if (!kv.block_table) return true;
+  const int32_t pg = kv.block_table[static_cast<int64_t>(b) * kv.max_pages + t / kv.page_rows];
+  return pg >= 0 && pg < kv.n_pages;
+}
+// Byte offset of (sequence b, row t, head 0) from the cache base.
+__device__ __forceinline__ int64_t kv_row_offset(const KvLayout& kv, int b, int32_t t) {
+  return kv.block_table ? static_cast<int64_t>(kv_phys_row(kv, b, t)) * kv.token_stride
+                        : b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride;
+}
+#endif
 
 // ---------------------------------------------------------------- rope_append.cu
 // In-place RoPE of x [seq, n_heads, head_dim] (ApplyRoPEFull).
@@ -147,6 +172,11 @@ struct PrefillArgs {
   int32_t* status;
   int32_t split_kv;         // 1: the CTA's two softmax groups split one query tile's cache range
   int32_t q_early;          // 1: q is not written by the kernel launched just before this one
+  // Paged cache (block_table non-NULL; page_rows a multiple of 128): k_map / v_map cover the
+  // pool as one sequence, and cache tile j of sequence b is pool row
+  // block_table[b * max_pages + j * 128 / page_rows] * page_rows + (j * 128) % page_rows.
+  const int32_t* block_table;
+  int32_t max_pages, page_rows;
 };
 bool prefill_supported(int32_t head_dim);
 // Split mode pays off when pairing query tiles would leave SMs idle (about one wave or less).

@@ -224,16 +224,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const int tile = !split ? g : g < 2 * n_kv[0] ? ((g & 1) ? kv_lo[1] : 0) + (g >> 1) : g;
         const int s = g % C::NS;
         const uint32_t par = ((g / C::NS) & 1) ^ 1;
+        // paged cache: the 128-row tile lies inside one page of the pool (sequence coordinate 0)
+        const int row = a.block_table ? a.block_table[static_cast<int64_t>(b) * a.max_pages + tile * kBN / a.page_rows] *
+                                                a.page_rows + (tile * kBN) % a.page_rows
+                                      : tile * kBN;
+        const int bc = a.block_table ? 0 : b;
         if (!mbar_wait(&bar.k_empty[s], par, status)) break;
         mbar_arrive_expect_tx(&bar.k_full[s], C::TILE_BYTES);
         for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d(k_s + s * C::TILE_BYTES + kb * kBN * 128, &a.k_map, &bar.k_full[s], kb * 64, kvh, tile * kBN,
-                      b);
+          tma_load_4d(k_s + s * C::TILE_BYTES + kb * kBN * 128, &a.k_map, &bar.k_full[s], kb * 64, kvh, row, bc);
         if (!mbar_wait(&bar.v_empty[s], par, status)) break;
         mbar_arrive_expect_tx(&bar.v_full[s], C::TILE_BYTES);
         for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d(v_s + s * C::TILE_BYTES + kb * kBN * 128, &a.v_map, &bar.v_full[s], kb * 64, kvh, tile * kBN,
-                      b);
+          tma_load_4d(v_s + s * C::TILE_BYTES + kb * kBN * 128, &a.v_map, &bar.v_full[s], kb * 64, kvh, row, bc);
       }
     }
     // Cache rows >= Lk in the last V tile may hold stale bits (NaN patterns included); P is 0

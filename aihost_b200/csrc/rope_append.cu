@@ -67,8 +67,8 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
   const int32_t b = static_cast<int32_t>(row / (static_cast<int64_t>(n_kv_heads) * n_new));
   const int32_t start = seq_len[b];
   const int32_t t = start + s;
-  if (start < 0 || t >= kv.capacity) {
-    if (lane == 0 && is_k && s == 0 && h == 0) atomicOr(status, kStatusBadLength);
+  if (start < 0 || t >= kv.capacity || !kv_row_ok(kv, b, t)) {
+    if (lane == 0 && is_k && h == 0) atomicOr(status, kStatusBadLength);
     return;
   }
   const Tin* src = (is_k ? k_new : v_new) + row * D + lane * E;
@@ -81,8 +81,7 @@ __global__ void kv_append_kernel(const Tin* __restrict__ k_new, const Tin* __res
     rope_row_warp<E>(x, lane, pos, rope_mode, static_cast<const float*>(s_f));
   }
 
-  uint8_t* dst = (is_k ? k_cache : v_cache) + b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride +
-                 static_cast<int64_t>(h) * kv.head_stride;
+  uint8_t* dst = (is_k ? k_cache : v_cache) + kv_row_offset(kv, b, t) + static_cast<int64_t>(h) * kv.head_stride;
   store_row_warp<E>(x, lane, dst, kv.dtype);
 }
 

@@ -22,7 +22,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import (F16, F32, Q8_0, ROPE_INTERLEAVED, ROPE_NONE, AttnDesc, AttnError, EINVAL, check, lib)
+from . import (F16, F32, Q8_0, ROPE_INTERLEAVED, ROPE_NONE, AttnDesc, AttnError, EINVAL, ENOMEM, check, lib)
 
 _TORCH_CODES = {torch.float32: F32, torch.float16: F16}
 
@@ -170,6 +170,59 @@ class KVCache:
         return self.k[layer], self.v[layer]
 
 
+class PagedKVCache:
+    """Preallocated paged KV cache (fp16): one pool of `n_pages` pages of `page_rows` rows per layer
+    for K and one for V, shared by all sequences, and a block table mapping each sequence's row
+    blocks to pages. Replaces KVCache.Add's per-token Concat (InferenceEngine.cs:598-622) with a
+    page allocation every `page_rows` tokens; memory follows the sequences' actual lengths.
+
+    `reserve(b, rows)` takes pages from the free list until sequence b can hold `rows` rows;
+    `release(b)` returns its pages. Lengths advance as in KVCache (`advance`)."""
+
+    def __init__(self, ctx: Context, spec: LayerSpec, n_pages: int, page_rows: int = 128, batch: int = 1,
+                 n_layers: int = 1, device=None):
+        if spec.kv_dtype != F16:
+            raise AttnError(EINVAL, "paged caches are fp16")
+        if page_rows < 128 or page_rows % 128:
+            raise AttnError(EINVAL, "page_rows must be a positive multiple of 128")
+        self.ctx, self.spec, self.batch, self.n_pages, self.page_rows = ctx, spec, batch, n_pages, page_rows
+        self.max_pages = -(-spec.kv_capacity // page_rows)
+        dev = device if device is not None else torch.device("cuda", ctx.device)
+        nbytes = n_pages * page_rows * spec.n_kv_heads * row_bytes(F16, spec.head_dim)
+        self.k = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(n_layers)]
+        self.v = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(n_layers)]
+        self.table_host = torch.full((batch, self.max_pages), -1, dtype=torch.int32)
+        self.block_table = self.table_host.to(dev)
+        self.pages = [[] for _ in range(batch)]
+        self.free = list(range(n_pages))
+        self.seq_len = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.host_len = [0] * batch
+
+    def reserve(self, b: int, rows: int) -> None:
+        need = -(-rows // self.page_rows)
+        if need > self.max_pages:
+            raise AttnError(EINVAL, f"{rows} rows exceed kv_capacity {self.spec.kv_capacity}")
+        if need - len(self.pages[b]) > len(self.free):
+            raise AttnError(ENOMEM, "the page pool is exhausted")
+        while len(self.pages[b]) < need:
+            pg = self.free.pop(0)
+            self.table_host[b, len(self.pages[b])] = pg
+            self.pages[b].append(pg)
+        self.block_table.copy_(self.table_host)
+
+    def release(self, b: int) -> None:
+        self.free.extend(self.pages[b])
+        self.pages[b] = []
+        self.table_host[b] = -1
+        self.block_table.copy_(self.table_host)
+        self.host_len[b] = 0
+        self.seq_len[b] = 0
+
+    def advance(self, n_new: int) -> None:
+        self.host_len = [n + n_new for n in self.host_len]
+        self.seq_len += n_new
+
+
 class ComputeOps:
     """The attention subset of the reference's ComputeOps, executed by libaihost_attn."""
 
@@ -251,6 +304,26 @@ class ComputeOps:
         d = spec.desc()
         check(lib().aihost_attn_mha(self.ctx.handle, ctypes.byref(d), 1, K.shape[0], 0, _ptr(Q), _ptr(K), _ptr(V),
                                     _ptr(out), _stream(self.stream)))
+        return out
+
+    def attention_layer_paged(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, cache: PagedKVCache,
+                              layer: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+        """attention_layer over a PagedKVCache: pages for the new rows are reserved first."""
+        B, S = q.shape[0], q.shape[1]
+        spec = cache.spec
+        for b in range(B):
+            cache.reserve(b, cache.host_len[b] + S)
+        if out is None:
+            odt = torch.float32 if spec.out_dtype == F32 else torch.float16
+            out = torch.empty(B, S, spec.n_q_heads, spec.head_dim, dtype=odt, device=q.device)
+        self.ctx.reserve_for(spec, B, S)
+        d = spec.desc()
+        hl = (ctypes.c_int32 * B)(*cache.host_len)
+        check(lib().aihost_attn_forward_paged(self.ctx.handle, ctypes.byref(d), B, S, _ptr(q), _ptr(k_new), _ptr(v_new),
+                                              _ptr(cache.k[layer]), _ptr(cache.v[layer]), cache.n_pages,
+                                              cache.page_rows, _ptr(cache.block_table), cache.max_pages,
+                                              _ptr(cache.seq_len), ctypes.cast(hl, ctypes.c_void_p), _ptr(out),
+                                              _stream(self.stream)))
         return out
 
     def attention_layer(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, cache: KVCache,

@@ -117,6 +117,20 @@ aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* 
                                   void* k_cache, void* v_cache, const int32_t* seq_len,
                                   const int32_t* h_seq_len, void* out, void* stream);
 
+/* aihost_attn_forward over a paged fp16 cache instead of one contiguous cache per sequence: the
+ * preallocated manager that replaces KVCache.Add's per-token Concat (InferenceEngine.cs:598-622).
+ * k_pool / v_pool hold n_pages pages of page_rows rows (a positive multiple of 128) in the layout
+ * desc gives per row (kv_token_stride / kv_head_stride; kv_seq_stride is ignored). Row t of
+ * sequence b is pool row block_table[b * max_pages + t / page_rows] * page_rows + t % page_rows
+ * (block_table: device int32[batch][max_pages]; entries for the pages that rows [0, seq_len[b] +
+ * n_new) touch must be valid page indices, distinct across sequences). desc->kv_capacity, the
+ * per-sequence row limit, is at most max_pages * page_rows. kv_dtype must be F16. */
+aihost_status aihost_attn_forward_paged(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
+                                        int32_t n_new, const void* q, const void* k_new, const void* v_new,
+                                        void* k_pool, void* v_pool, int32_t n_pages, int32_t page_rows,
+                                        const int32_t* block_table, int32_t max_pages, const int32_t* seq_len,
+                                        const int32_t* h_seq_len, void* out, void* stream);
+
 /* ComputeOps.MultiHeadAttention(Q, K, V, numHeads, startPosition) (ComputeOps.cs:1055-1102):
  * attention only, for one sequence, over K/V rows [0, n_kv) that are already rotated.
  * q/out [n_q, Hq*d]; k/v laid out as desc (kv_capacity >= n_kv). rope_mode is ignored.

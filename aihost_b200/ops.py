@@ -204,6 +204,8 @@ class PagedKVCache:
             raise AttnError(EINVAL, f"{rows} rows exceed kv_capacity {self.spec.kv_capacity}")
         if need - len(self.pages[b]) > len(self.free):
             raise AttnError(ENOMEM, "the page pool is exhausted")
+        if len(self.pages[b]) >= need:
+            return
         while len(self.pages[b]) < need:
             pg = self.free.pop(0)
             self.table_host[b, len(self.pages[b])] = pg

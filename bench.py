@@ -52,6 +52,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0,
                     help="decode configs: also time a CUDA graph of this many layers with distinct caches "
                          "(rotating caches: HBM throughput instead of single-call latency); adds a `layers` object")
+    ap.add_argument("--paged", type=int, default=0, metavar="PAGE_ROWS",
+                    help="fp16 configs: keep the cache in a shared pool of PAGE_ROWS-row pages (shuffled order) and "
+                         "time aihost_attn_forward_paged instead")
     ap.add_argument("--op", default="attention", choices=["attention", "qk-norm-rope"],
                     help="qk-norm-rope: time the Qwen TypeB Q/K prologue kernel alone (one GPU; GB/s of HBM)")
     ap.add_argument("--profile-steps", type=int, default=0,
@@ -274,7 +277,35 @@ def shard_inputs(cfg, device, rank, world):
     return inp, spec, shard, local
 
 
-def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode="seq"):
+def paged_cache(ctx, cfg, inp, page_rows, device):
+    """PagedKVCache holding inp's cached rows in shuffled pages of a pool (room for every
+    sequence's capacity), plus the step function over it."""
+    import numpy as np
+    import torch
+
+    from aihost_b200.ops import PagedKVCache, row_bytes
+
+    cap = inp["capacity"]
+    max_pages = -(-cap // page_rows)
+    n_pages = cfg.batch * max_pages
+    cache = PagedKVCache(ctx, cfg.spec(cap), n_pages=n_pages, page_rows=page_rows, batch=cfg.batch, device=device)
+    cache.free = [int(p) for p in np.random.default_rng(7).permutation(n_pages)]
+    rb = row_bytes(cfg.kv_dtype, cfg.head_dim) * cfg.n_kv_heads
+    for b, length in enumerate(inp["lengths"]):
+        cache.reserve(b, length + cfg.n_new)
+    for name, pool in (("k_cache", cache.k[0]), ("v_cache", cache.v[0])):
+        full = inp[name].view(cfg.batch, cap, rb)
+        pv = pool.view(-1, rb)
+        for b, length in enumerate(inp["lengths"]):
+            t = torch.arange(length, device=device)
+            pages = torch.tensor(cache.pages[b], device=device)
+            pv[pages[t // page_rows] * page_rows + t % page_rows] = full[b, :length]
+    cache.seq_len = inp["seq_len"]
+    cache.host_len = list(inp["lengths"])
+    return cache
+
+
+def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode="seq", paged=0):
     import torch
 
     import aihost_b200 as A
@@ -303,13 +334,18 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
             inp = device_inputs(cfg, device, rank)
         spec, local_cfg = cfg.spec(inp["capacity"]), cfg
     lengths = inp["lengths"]
-    cache = KVCache(ctx, spec, batch=cfg.batch, n_layers=1, device=device)
-    cache.k[0], cache.v[0] = inp["k_cache"], inp["v_cache"]
-    cache.seq_len, cache.host_len = inp["seq_len"], list(lengths)
+    if paged:
+        cache = paged_cache(ctx, cfg, inp, paged, device)
+    else:
+        cache = KVCache(ctx, spec, batch=cfg.batch, n_layers=1, device=device)
+        cache.k[0], cache.v[0] = inp["k_cache"], inp["v_cache"]
+        cache.seq_len, cache.host_len = inp["seq_len"], list(lengths)
     q, kn, vn = inp["q"], inp["k_new"], inp["v_new"]
     ops = ComputeOps(ctx)
     if ctxs is not None:  # every rank serves all B tokens
         out = ctxs.forward(ops, q, kn, vn, cache, inp["q_pos"])
+    elif paged:
+        out = ops.attention_layer_paged(q, kn, vn, cache)
     else:
         out = ops.attention_layer(q, kn, vn, cache)  # also reserves scratch
     w = work(local_cfg, lengths)  # this rank's work (context mode: its chunk of the rows)
@@ -338,6 +374,8 @@ def bench_ours(cfg, steps, warmup, device, ctx, flush_bytes, dist_on, shard_mode
             rows.forward(ops, q, kn, vn, cache, out=result)
         elif ctxs is not None:
             ctxs.forward(ops, q, kn, vn, cache, inp["q_pos"], out=result)
+        elif paged:
+            ops.attention_layer_paged(q, kn, vn, cache, out=result)
         else:
             ops.attention_layer(q, kn, vn, cache, out=out)
 
@@ -765,7 +803,8 @@ def main():
     heads = args.shard == "heads"
     row_mode = args.shard == "rows"
     cp_mode = args.shard == "context"
-    r = bench_ours(cfg, args.steps, args.warmup, device, ctx, flush_bytes, dist_on, shard_mode=args.shard)
+    r = bench_ours(cfg, args.steps, args.warmup, device, ctx, flush_bytes, dist_on, shard_mode=args.shard,
+                   paged=args.paged)
     main_res = summarize(cfg, r, ws, dist_on, pk, pk_kind)
     dec = None
     if args.config == 2 and not args.no_decode:
@@ -804,6 +843,8 @@ def main():
                                            if cp_mode else "one independent sequence set per rank")
                            if ws > 1 else "single GPU"},
                 "roofline": main_res["roofline"], "cpu_baseline": cpu, "e2e": main_res["e2e"],
+                "kv_layout": (f"paged: {args.paged}-row pages of a shared pool, shuffled order, block table"
+                              if args.paged else "contiguous per sequence"),
                 "gpu_launches": main_res["gpu_launches"], "clocks": clk, "kernels": main_res["kernels"],
                 "wall_s_timed_region": r["wall"]}
         if dec is not None:

@@ -213,10 +213,14 @@ aihost_status encode_q8_map(CUtensorMap* map, const void* base, const KvLayout& 
                             uint32_t box_words) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const int64_t seq_stride = kv.seq_stride ? kv.seq_stride : kv.token_stride * kv.capacity;
+  // a paged cache is one pool "sequence" of n_pages * page_rows rows
+  const int64_t rows = kv.block_table ? static_cast<int64_t>(kv.n_pages) * kv.page_rows : kv.capacity;
+  if (kv.block_table) batch = 1;
+  const int64_t seq_stride =
+      kv.block_table ? kv.token_stride * rows : (kv.seq_stride ? kv.seq_stride : kv.token_stride * kv.capacity);
   if (!aligned(base, 16) || kv.token_stride % 16 || seq_stride % 16 || kv.head_stride % 4)
     return fail(AIHOST_EINVAL, "Q8_0 cache strides are not TMA-compatible");
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kv.token_stride / 4), static_cast<cuuint64_t>(kv.capacity),
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kv.token_stride / 4), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(batch), 1};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(kv.token_stride), static_cast<cuuint64_t>(seq_stride),
                            static_cast<cuuint64_t>(seq_stride) * static_cast<cuuint64_t>(batch)};
@@ -370,6 +374,7 @@ aihost_status run_prefill(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const
       kv.seq_stride = kv.token_stride * kv_rows;
       kv.capacity = kv_rows;
       kv.dtype = AIHOST_F16;
+      kv.block_table = nullptr;  // the staged copies are dense per sequence, whatever the cache was
     }
   }
   PrefillArgs a;
@@ -607,11 +612,17 @@ static aihost_status forward_common(aihost_attn_ctx* ctx, const aihost_attn_desc
     // the pools must be describable by the tensor maps the kernels read them through
     const int64_t rows = static_cast<int64_t>(kv.n_pages) * kv.page_rows;
     CUtensorMap probe;
-    s = encode_f16_map(&probe, k_cache, desc->head_dim, desc->n_kv_heads, rows, 1, kv.head_stride, kv.token_stride,
-                       kv.token_stride * rows, "k_pool", 64);
-    if (s != AIHOST_OK) return s;
-    s = encode_f16_map(&probe, v_cache, desc->head_dim, desc->n_kv_heads, rows, 1, kv.head_stride, kv.token_stride,
-                       kv.token_stride * rows, "v_pool", 64);
+    if (kv.dtype == AIHOST_F16) {
+      s = encode_f16_map(&probe, k_cache, desc->head_dim, desc->n_kv_heads, rows, 1, kv.head_stride, kv.token_stride,
+                         kv.token_stride * rows, "k_pool", 64);
+      if (s == AIHOST_OK)
+        s = encode_f16_map(&probe, v_cache, desc->head_dim, desc->n_kv_heads, rows, 1, kv.head_stride,
+                           kv.token_stride, kv.token_stride * rows, "v_pool", 64);
+    } else {
+      const uint32_t bw = q8_box_words(desc->head_dim, kv.head_stride);
+      s = bw ? encode_q8_map(&probe, k_cache, kv, 1, bw) : fail(AIHOST_EINVAL, "Q8_0 head stride is not TMA-compatible");
+      if (s == AIHOST_OK) s = encode_q8_map(&probe, v_cache, kv, 1, bw);
+    }
     if (s != AIHOST_OK) return s;
   }
   if (batch < 1 || n_new < 1) return fail(AIHOST_EINVAL, "batch (%d) and n_new (%d) must be >= 1", batch, n_new);
@@ -661,7 +672,8 @@ aihost_status aihost_attn_forward_paged(aihost_attn_ctx* ctx, const aihost_attn_
                                         const int32_t* block_table, int32_t max_pages, const int32_t* seq_len,
                                         const int32_t* h_seq_len, void* out, void* stream) {
   if (!desc) return fail(AIHOST_EINVAL, "desc is NULL");
-  if (desc->kv_dtype != AIHOST_F16) return fail(AIHOST_EUNSUPPORTED, "paged caches are fp16 (kv_dtype F16)");
+  if (desc->kv_dtype != AIHOST_F16 && desc->kv_dtype != AIHOST_Q8_0)
+    return fail(AIHOST_EUNSUPPORTED, "paged caches are fp16 or Q8_0");
   if (page_rows < 128 || page_rows % 128) return fail(AIHOST_EINVAL, "page_rows %d must be a positive multiple of 128",
                                                       page_rows);
   if (n_pages < 1 || max_pages < 1) return fail(AIHOST_EINVAL, "n_pages (%d) and max_pages (%d) must be >= 1", n_pages,

@@ -773,9 +773,9 @@ __global__ void __launch_bounds__(kQ8Threads, 2) decode_q8_kernel(const __grid_c
       const int s = i % C::NSR;
       if (!mbar_wait(&bar.raw_empty[s], ((i / C::NSR) & 1) ^ 1, p.status)) return false;
       mbar_arrive_expect_tx(&bar.raw_full[s], 2 * C::RAW_TILE);  // bytes the two boxes deliver
-      const int r = t0 + i * kTileRows;
-      tma_load_4d(smem + C::RAW_OFF + s * C::RAW_TILE, &a.k_map, &bar.raw_full[s], box_x, r, b, 0);
-      tma_load_4d(smem + C::RAW_OFF + (C::NSR + s) * C::RAW_TILE, &a.v_map, &bar.raw_full[s], box_x, r, b, 0);
+      const int r = kv_phys_row(p.kv, b, t0 + i * kTileRows), bc = p.kv.block_table ? 0 : b;  // paged: pool row
+      tma_load_4d(smem + C::RAW_OFF + s * C::RAW_TILE, &a.k_map, &bar.raw_full[s], box_x, r, bc, 0);
+      tma_load_4d(smem + C::RAW_OFF + (C::NSR + s) * C::RAW_TILE, &a.v_map, &bar.raw_full[s], box_x, r, bc, 0);
       return true;
     };
     bool feed = issuer;
@@ -924,9 +924,9 @@ __global__ void __launch_bounds__(kQ8kThreads, 2) decode_q8k_kernel(const __grid
         if (appends && i == (Lk - 1 - t0) / kTileRows && !mbar_wait(&bar.appended, 0, p.status)) break;
         if (!mbar_wait(&bar.raw_empty[s], ((i / C::NSR) & 1) ^ 1, p.status)) break;
         mbar_arrive_expect_tx(&bar.raw_full[s], 2 * B::RAW_TILE);  // bytes the two boxes deliver
-        const int r = t0 + i * kTileRows;
-        tma_load_4d(smem + C::RAW_OFF + s * B::RAW_TILE, &a.k_map, &bar.raw_full[s], box_x, r, b, 0);
-        tma_load_4d(smem + C::RAW_OFF + (C::NSR + s) * B::RAW_TILE, &a.v_map, &bar.raw_full[s], box_x, r, b, 0);
+        const int r = kv_phys_row(p.kv, b, t0 + i * kTileRows), bc = p.kv.block_table ? 0 : b;  // paged: pool row
+        tma_load_4d(smem + C::RAW_OFF + s * B::RAW_TILE, &a.k_map, &bar.raw_full[s], box_x, r, bc, 0);
+        tma_load_4d(smem + C::RAW_OFF + (C::NSR + s) * B::RAW_TILE, &a.v_map, &bar.raw_full[s], box_x, r, bc, 0);
       }
     }
     return;

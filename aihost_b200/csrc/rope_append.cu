@@ -134,8 +134,7 @@ __global__ void stage_kv_kernel(const uint8_t* __restrict__ k_cache, const uint8
   const int32_t len = (seq_len ? seq_len[b] : start_scalar) + len_offset;
   if (t >= len || t >= kv.capacity) return;
   const bool is_k = blockIdx.y == 0;
-  const uint8_t* src = (is_k ? k_cache : v_cache) + b * kv.seq_stride + static_cast<int64_t>(t) * kv.token_stride +
-                       static_cast<int64_t>(h) * kv.head_stride;
+  const uint8_t* src = (is_k ? k_cache : v_cache) + kv_row_offset(kv, b, t) + static_cast<int64_t>(h) * kv.head_stride;
   float x[E];
   if (kv.dtype == AIHOST_F32) {
     const float* f = reinterpret_cast<const float*>(src) + lane * E;

@@ -1,4 +1,4 @@
-"""Paged fp16 KV cache (aihost_attn_forward_paged, PagedKVCache).
+"""Paged fp16 / Q8_0 KV cache (aihost_attn_forward_paged, PagedKVCache).
 
 Each sequence's cached rows are scattered over pages of a shared pool in shuffled order. A decode
 step and a chunked prefill over the paged cache must give the contiguous path's output bit for
@@ -55,6 +55,12 @@ CASES = {
                                           cached_list=[0, 77]), 256),
     "prefill_d128": (CONFIGS[4].scaled(batch=1, n_new=200, n_q_heads=8, n_kv_heads=2, cached=None, cached_list=[390]),
                      128),
+    # Q8_0 pools: head groups of 8 (K-direct kernel) and 16, and a prefill through the fp16 staging
+    "q8_decode_g8": (CONFIGS[5].scaled(batch=2, n_q_heads=16, n_kv_heads=2, cached=None, cached_list=[777, 130]), 128),
+    "q8_decode_g16": (CONFIGS[5].scaled(batch=2, n_q_heads=32, n_kv_heads=2, cached=None, cached_list=[300, 1500]),
+                      256),
+    "q8_prefill": (CONFIGS[5].scaled(batch=2, n_new=150, n_q_heads=8, n_kv_heads=2, cached=None, cached_list=[0, 260]),
+                   128),
 }
 
 
@@ -129,10 +135,10 @@ def test_paged_arguments_are_validated(ctx):
                                            None) == EINVAL  # page_rows not a multiple of 128
     assert lib().aihost_attn_forward_paged(ctx.handle, ctypes.byref(d), 1, 1, z, z, z, z, z, 4, 128, z, 2, z, None, z,
                                            None) == EINVAL  # kv_capacity beyond max_pages * page_rows
-    from aihost_b200 import Q8_0
-
     import dataclasses
 
-    d8 = dataclasses.replace(spec, kv_dtype=Q8_0).desc()
-    assert lib().aihost_attn_forward_paged(ctx.handle, ctypes.byref(d8), 1, 1, z, z, z, z, z, 4, 128, z, 9, z, None, z,
-                                           None) == EUNSUPPORTED
+    from aihost_b200 import F32
+
+    d32 = dataclasses.replace(spec, kv_dtype=F32).desc()
+    assert lib().aihost_attn_forward_paged(ctx.handle, ctypes.byref(d32), 1, 1, z, z, z, z, z, 4, 128, z, 9, z, None,
+                                           z, None) == EUNSUPPORTED

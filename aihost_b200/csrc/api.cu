@@ -448,7 +448,6 @@ cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ct
     mma = bw && encode_q8_map(&m.k_map, a.k_cache, a.kv, a.batch, bw) == AIHOST_OK &&
           encode_q8_map(&m.v_map, a.v_cache, a.kv, a.batch, bw) == AIHOST_OK;
   }
-  if (!mma && a.kv.block_table) return cudaErrorInvalidValue;  // paged caches need the tensor-core path
   if (!mma) memcpy(g_err, saved, sizeof(g_err));  // strides TMA cannot describe: CUDA-core kernel instead
   // One CTA per <= 16 query heads: with a single head group per KV head, the CTA of the last
   // split appends the new rows itself and the last split to finish merges the partials.
@@ -612,7 +611,9 @@ static aihost_status forward_common(aihost_attn_ctx* ctx, const aihost_attn_desc
     // the pools must be describable by the tensor maps the kernels read them through
     const int64_t rows = static_cast<int64_t>(kv.n_pages) * kv.page_rows;
     CUtensorMap probe;
-    if (kv.dtype == AIHOST_F16) {
+    if (kv.dtype == AIHOST_F32) {
+      // read row by row by the CUDA-core decode kernel and the prefill staging: no tensor map
+    } else if (kv.dtype == AIHOST_F16) {
       s = encode_f16_map(&probe, k_cache, desc->head_dim, desc->n_kv_heads, rows, 1, kv.head_stride, kv.token_stride,
                          kv.token_stride * rows, "k_pool", 64);
       if (s == AIHOST_OK)
@@ -672,8 +673,8 @@ aihost_status aihost_attn_forward_paged(aihost_attn_ctx* ctx, const aihost_attn_
                                         const int32_t* block_table, int32_t max_pages, const int32_t* seq_len,
                                         const int32_t* h_seq_len, void* out, void* stream) {
   if (!desc) return fail(AIHOST_EINVAL, "desc is NULL");
-  if (desc->kv_dtype != AIHOST_F16 && desc->kv_dtype != AIHOST_Q8_0)
-    return fail(AIHOST_EUNSUPPORTED, "paged caches are fp16 or Q8_0");
+  if (desc->kv_dtype != AIHOST_F16 && desc->kv_dtype != AIHOST_Q8_0 && desc->kv_dtype != AIHOST_F32)
+    return fail(AIHOST_EUNSUPPORTED, "kv_dtype %d cannot be paged", desc->kv_dtype);
   if (page_rows < 128 || page_rows % 128) return fail(AIHOST_EINVAL, "page_rows %d must be a positive multiple of 128",
                                                       page_rows);
   if (n_pages < 1 || max_pages < 1) return fail(AIHOST_EINVAL, "n_pages (%d) and max_pages (%d) must be >= 1", n_pages,

@@ -167,8 +167,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
 #pragma unroll
     for (int e = 0; e < E; ++e) qr[g][e] = q_s[g * D + lane * E + e];
 
-  const uint8_t* kbase = static_cast<const uint8_t*>(a.k_cache) + b * a.kv.seq_stride + kvh * a.kv.head_stride;
-  const uint8_t* vbase = static_cast<const uint8_t*>(a.v_cache) + b * a.kv.seq_stride + kvh * a.kv.head_stride;
+  // row t of this sequence: base + kv_row_offset(kv, b, t) (through the block table for a paged cache)
+  const uint8_t* kbase = static_cast<const uint8_t*>(a.k_cache) + kvh * a.kv.head_stride;
+  const uint8_t* vbase = static_cast<const uint8_t*>(a.v_cache) + kvh * a.kv.head_stride;
   const float sl2 = a.scale * kLog2e;
 
   // ---- scores: warp w takes rows t0 + w, t0 + w + 8, ...
@@ -178,7 +179,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * kDecodeWarps;
-      if (j < n) RowLoader<KV, E>::load(kbase + static_cast<int64_t>(t0 + j) * a.kv.token_stride, lane * E, kx[u]);
+      if (j < n) RowLoader<KV, E>::load(kbase + kv_row_offset(a.kv, b, t0 + j), lane * E, kx[u]);
       else {
 #pragma unroll
         for (int e = 0; e < E; ++e) kx[u][e] = 0.0f;
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * kDecodeWarps;
-      if (j < n) RowLoader<KV, E>::load(vbase + static_cast<int64_t>(t0 + j) * a.kv.token_stride, lane * E, vx[u]);
+      if (j < n) RowLoader<KV, E>::load(vbase + kv_row_offset(a.kv, b, t0 + j), lane * E, vx[u]);
       else {
 #pragma unroll
         for (int e = 0; e < E; ++e) vx[u][e] = 0.0f;

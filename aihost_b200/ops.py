@@ -171,7 +171,7 @@ class KVCache:
 
 
 class PagedKVCache:
-    """Preallocated paged KV cache (fp16 or Q8_0): one pool of `n_pages` pages of `page_rows` rows per layer
+    """Preallocated paged KV cache (fp32, fp16 or Q8_0): one pool of `n_pages` pages of `page_rows` rows per layer
     for K and one for V, shared by all sequences, and a block table mapping each sequence's row
     blocks to pages. Replaces KVCache.Add's per-token Concat (InferenceEngine.cs:598-622) with a
     page allocation every `page_rows` tokens; memory follows the sequences' actual lengths.
@@ -181,8 +181,8 @@ class PagedKVCache:
 
     def __init__(self, ctx: Context, spec: LayerSpec, n_pages: int, page_rows: int = 128, batch: int = 1,
                  n_layers: int = 1, device=None):
-        if spec.kv_dtype not in (F16, Q8_0):
-            raise AttnError(EINVAL, "paged caches are fp16 or Q8_0")
+        if spec.kv_dtype not in (F32, F16, Q8_0):
+            raise AttnError(EINVAL, "unsupported kv_dtype for a paged cache")
         if page_rows < 128 or page_rows % 128:
             raise AttnError(EINVAL, "page_rows must be a positive multiple of 128")
         self.ctx, self.spec, self.batch, self.n_pages, self.page_rows = ctx, spec, batch, n_pages, page_rows

@@ -117,15 +117,15 @@ aihost_status aihost_attn_forward(aihost_attn_ctx* ctx, const aihost_attn_desc* 
                                   void* k_cache, void* v_cache, const int32_t* seq_len,
                                   const int32_t* h_seq_len, void* out, void* stream);
 
-/* aihost_attn_forward over a paged fp16 or Q8_0 cache instead of one contiguous cache per sequence: the
+/* aihost_attn_forward over a paged cache instead of one contiguous cache per sequence: the
  * preallocated manager that replaces KVCache.Add's per-token Concat (InferenceEngine.cs:598-622).
  * k_pool / v_pool hold n_pages pages of page_rows rows (a positive multiple of 128) in the layout
  * desc gives per row (kv_token_stride / kv_head_stride; kv_seq_stride is ignored). Row t of
  * sequence b is pool row block_table[b * max_pages + t / page_rows] * page_rows + t % page_rows
  * (block_table: device int32[batch][max_pages]; entries for the pages that rows [0, seq_len[b] +
  * n_new) touch must be valid page indices, distinct across sequences). desc->kv_capacity, the
- * per-sequence row limit, is at most max_pages * page_rows. kv_dtype F16 or Q8_0 (Q8_0 token rows
- * 16-byte aligned, as for the tensor-core decode of a contiguous Q8_0 cache). */
+ * per-sequence row limit, is at most max_pages * page_rows. kv_dtype F32, F16 or Q8_0 (fp16 and
+ * Q8_0 pools must be TMA-describable, as for the tensor-core decode of a contiguous cache). */
 aihost_status aihost_attn_forward_paged(aihost_attn_ctx* ctx, const aihost_attn_desc* desc, int32_t batch,
                                         int32_t n_new, const void* q, const void* k_new, const void* v_new,
                                         void* k_pool, void* v_pool, int32_t n_pages, int32_t page_rows,

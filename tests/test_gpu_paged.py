@@ -1,4 +1,4 @@
-"""Paged fp16 / Q8_0 KV cache (aihost_attn_forward_paged, PagedKVCache).
+"""Paged fp32 / fp16 / Q8_0 KV cache (aihost_attn_forward_paged, PagedKVCache).
 
 Each sequence's cached rows are scattered over pages of a shared pool in shuffled order. A decode
 step and a chunked prefill over the paged cache must give the contiguous path's output bit for
@@ -61,7 +61,12 @@ CASES = {
                       256),
     "q8_prefill": (CONFIGS[5].scaled(batch=2, n_new=150, n_q_heads=8, n_kv_heads=2, cached=None, cached_list=[0, 260]),
                    128),
+    # fp32 pools (the reference's dtype): CUDA-core decode and a staged prefill
+    "fp32_decode": (CONFIGS[1].scaled(batch=2, cached=None, cached_list=[512, 200]), 128),
+    "fp32_prefill": (CONFIGS[1].scaled(batch=2, n_new=150, n_q_heads=8, n_kv_heads=2, cached=None,
+                                       cached_list=[0, 100]), 128),
 }
+TOL = {"fp32_decode": 2e-4, "fp32_prefill": 1e-3}
 
 
 @pytest.mark.parametrize("case", list(CASES))
@@ -79,7 +84,7 @@ def test_paged_equals_contiguous_and_oracle(ctx, case):
     out_c, kc_c, vc_c = gpu_forward(ctx, cfg, inp)
     assert torch.equal(out.cpu(), out_c), case
     ref, _, _ = oracle_forward(cfg, inp)
-    assert max_abs(out.cpu().float().numpy(), ref) <= 2e-3
+    assert max_abs(out.cpu().float().numpy(), ref) <= TOL.get(case, 2e-3)
     cap = inp["capacity"]
     for b, length in enumerate(inp["lengths"]):
         rows = length + cfg.n_new
@@ -137,8 +142,6 @@ def test_paged_arguments_are_validated(ctx):
                                            None) == EINVAL  # kv_capacity beyond max_pages * page_rows
     import dataclasses
 
-    from aihost_b200 import F32
-
-    d32 = dataclasses.replace(spec, kv_dtype=F32).desc()
-    assert lib().aihost_attn_forward_paged(ctx.handle, ctypes.byref(d32), 1, 1, z, z, z, z, z, 4, 128, z, 9, z, None,
+    d9 = dataclasses.replace(spec, kv_dtype=9).desc()
+    assert lib().aihost_attn_forward_paged(ctx.handle, ctypes.byref(d9), 1, 1, z, z, z, z, z, 4, 128, z, 9, z, None,
                                            z, None) == EUNSUPPORTED

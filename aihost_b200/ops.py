@@ -199,9 +199,9 @@ class PagedKVCache:
         self.host_len = [0] * batch
 
     def reserve(self, b: int, rows: int) -> None:
-        need = -(-rows // self.page_rows)
-        if need > self.max_pages:
+        if rows > self.spec.kv_capacity:
             raise AttnError(EINVAL, f"{rows} rows exceed kv_capacity {self.spec.kv_capacity}")
+        need = -(-rows // self.page_rows)
         if need - len(self.pages[b]) > len(self.free):
             raise AttnError(ENOMEM, "the page pool is exhausted")
         if len(self.pages[b]) >= need:

@@ -187,3 +187,31 @@ def test_context_merge_of_partials_equals_full_softmax():
         w = np.exp(lse - lse.max())
         merged = (w[:, None] * np.array(o)).sum(0) / w.sum()
         assert np.abs(merged - full).max() < 1e-12
+
+
+def test_paged_cache_allocator_host_logic():
+    """PagedKVCache's page bookkeeping (host side; pools in host memory, no kernels)."""
+    from aihost_b200 import EINVAL, ENOMEM, F16, AttnError
+    from aihost_b200.ops import LayerSpec, PagedKVCache
+
+    spec = LayerSpec(8, 2, 128, kv_dtype=F16, q_dtype=F16, out_dtype=F16, kv_capacity=1000)
+    cache = PagedKVCache(None, spec, n_pages=10, page_rows=128, batch=3, device=torch.device("cpu"))
+    assert cache.max_pages == 8 and cache.k[0].numel() == 10 * 128 * 2 * 128 * 2
+    cache.reserve(0, 300)   # 3 pages
+    cache.reserve(1, 128)   # 1 page
+    cache.reserve(0, 300)   # nothing new
+    assert cache.pages[0] == [0, 1, 2] and cache.pages[1] == [3]
+    assert cache.block_table[0, :4].tolist() == [0, 1, 2, -1] and cache.block_table[1, 0] == 3
+    with pytest.raises(AttnError) as ei:
+        cache.reserve(2, 1001)   # beyond kv_capacity
+    assert ei.value.status == EINVAL
+    cache.reserve(2, 6 * 128)    # the last 6 pages
+    with pytest.raises(AttnError) as ei:
+        cache.reserve(1, 2 * 128)  # pool exhausted
+    assert ei.value.status == ENOMEM
+    cache.release(0)
+    assert sorted(cache.free) == [0, 1, 2] and cache.block_table[0].tolist() == [-1] * 8
+    cache.reserve(1, 2 * 128)
+    assert cache.pages[1] == [3, 0]
+    with pytest.raises(AttnError):
+        PagedKVCache(None, spec, n_pages=4, page_rows=100, device=torch.device("cpu"))

@@ -10,7 +10,7 @@ oracle/_ref/libref_glsl.so together with harness.cpp (the ComputeOps dispatch se
 glsl_runtime.cpp. Nothing from the reference is copied into the repository: the generated
 translation unit and the library live only in oracle/_ref/ (git-ignored).
 
-Usage: python oracle/ref_glsl/build_ref.py [--reference /root/reference]
+Usage: python oracle/ref_glsl/build_ref.py [--reference PATH_TO_REFERENCE_CHECKOUT]
 """
 from __future__ import annotations
 

@@ -27,6 +27,7 @@ EXPORTS = (
     "aihost_attn_profiler_read", "aihost_attn_profiler_reset", "aihost_attn_decode_noalloc",
     "aihost_attn_dist_unique_id", "aihost_attn_dist_init", "aihost_attn_dist_destroy", "aihost_attn_forward_sharded",
     "aihost_attn_decode_partial", "aihost_attn_merge_partials", "aihost_qk_norm_rope", "aihost_attn_forward_paged",
+    "aihost_attn_noalloc_sync_status", "aihost_attn_dist_init_bounded", "aihost_attn_dist_sync",
 )
 # aihost_kernel ids of the device-time profiler
 KERNEL_APPEND, KERNEL_DECODE, KERNEL_COMBINE, KERNEL_PREFILL, KERNEL_CONVERT = range(5)
@@ -78,9 +79,12 @@ def lib() -> ctypes.CDLL:
     L.aihost_attn_profiler_read.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_double)]
     L.aihost_attn_profiler_reset.argtypes = [vp]
     L.aihost_attn_decode_noalloc.argtypes = [dp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]
+    L.aihost_attn_noalloc_sync_status.argtypes = [vp, ctypes.POINTER(i32)]
     L.aihost_attn_dist_unique_id.argtypes = [vp]
     L.aihost_attn_dist_init.argtypes = [i32, i32, vp, i32, ctypes.POINTER(vp)]
+    L.aihost_attn_dist_init_bounded.argtypes = [i32, i32, vp, i32, i32, ctypes.POINTER(vp)]
     L.aihost_attn_dist_destroy.argtypes = [vp]
+    L.aihost_attn_dist_sync.argtypes = [vp, vp, i32]
     L.aihost_attn_forward_sharded.argtypes = [vp, vp, dp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.aihost_attn_decode_partial.argtypes = [vp, dp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.aihost_attn_merge_partials.argtypes = [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]

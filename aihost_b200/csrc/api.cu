@@ -479,6 +479,8 @@ cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ct
   return run(AIHOST_KERNEL_COMBINE, [&] { return launch_decode_combine(a, st); });
 }
 
+int32_t ctx_device(const aihost_attn_ctx* ctx) { return ctx ? ctx->device : -1; }
+
 // Validation, split plan and RoPE table of a one-token decode, for aihost_attn_decode_noalloc.
 aihost_status noalloc_prepare(const aihost_attn_desc* desc, int32_t batch, KvLayout* kv, float* scale,
                               int32_t* chunk, int32_t* max_splits, RopeFreqs* freqs, int32_t num_sms) {

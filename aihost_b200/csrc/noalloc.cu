@@ -21,9 +21,11 @@
 //   - all calls share the one array: calls whose kernels overlap on the GPU (different streams,
 //     different host threads) race on it. Serialise them, e.g. one stream per device;
 //   - the array keeps the last call's contents. Two fields must start at zero: the device
-//     status word, cleared (cudaMemsetAsync) at the start of every call, and the split-merge
-//     arrival counters, zero when the module loads and tagged with a per-device call epoch
-//     afterwards, so stale counts of earlier calls are never mistaken for this call's.
+//     status word and the split-merge arrival counters, both zero when the module loads. The
+//     status word then collects the error bits of every call (a device-side length past
+//     kv_capacity, a bounded wait that ran out) until aihost_attn_noalloc_sync_status reads and
+//     clears it, so an error is never lost to a later call. The counters are tagged with a
+//     per-device call epoch, so stale counts of earlier calls are never mistaken for this call's.
 #include <string.h>
 
 #include <mutex>
@@ -86,8 +88,11 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return api_fail(AIHOST_EUNSUPPORTED, "device index %d >= %d", dev, kMaxDevices);
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess || sms < 1)
+    return api_fail(AIHOST_ECUDA, "cudaDeviceGetAttribute(multiprocessor count) on device %d: %s", dev,
+                    cudaGetErrorString(e));
   KvLayout kv;
   float scale;
   int32_t chunk, max_splits;
@@ -116,9 +121,8 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   s = scratch_address(dev, &base);
   if (s != AIHOST_OK) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // sticky: kernels only set bits; aihost_attn_noalloc_sync_status reads and clears them
   int32_t* status = reinterpret_cast<int32_t*>(base);
-  e = cudaMemsetAsync(status, 0, sizeof(int32_t), st);
-  if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "cudaMemsetAsync(status): %s", cudaGetErrorString(e));
 
   DecodeArgs a;
   memset(&a, 0, sizeof(a));
@@ -151,5 +155,29 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   a.epoch = next_epoch(dev);
   e = launch_decode_any(a, st, nullptr);
   if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "decode launch: %s", cudaGetErrorString(e));
+  return AIHOST_OK;
+}
+
+extern "C" aihost_status aihost_attn_noalloc_sync_status(void* stream, int32_t* out_bits) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return api_fail(AIHOST_EUNSUPPORTED, "device index %d >= %d", dev, kMaxDevices);
+  uint8_t* base = nullptr;
+  aihost_status s = scratch_address(dev, &base);
+  if (s != AIHOST_OK) return s;
+  e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "cudaStreamSynchronize: %s", cudaGetErrorString(e));
+  // a host int and the device word: plain synchronous copies, no allocation on either side
+  int32_t bits = 0;
+  const int32_t zero = 0;
+  e = cudaMemcpy(&bits, base, sizeof(bits), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(base, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "reading the no-alloc status word: %s", cudaGetErrorString(e));
+  if (out_bits) *out_bits = bits;
+  if (bits & kStatusWaitTimeout)
+    return api_fail(AIHOST_ETIMEOUT, "a no-alloc decode kernel's bounded wait expired (status 0x%x)", bits);
+  if (bits & kStatusBadLength)
+    return api_fail(AIHOST_EINVAL, "a no-alloc decode call got a device-side sequence length past kv_capacity");
   return AIHOST_OK;
 }

@@ -177,7 +177,10 @@ class PagedKVCache:
     page allocation every `page_rows` tokens; memory follows the sequences' actual lengths.
 
     `reserve(b, rows)` takes pages from the free list until sequence b can hold `rows` rows;
-    `release(b)` returns its pages. Lengths advance as in KVCache (`advance`)."""
+    `release(b)` returns its pages. Lengths advance as in KVCache (`advance`). Both update the
+    device block table with a copy enqueued on `stream` (default: torch's current stream): pass
+    the stream the attention calls run on, so the copy is ordered after the steps that read the
+    old table and before the next one."""
 
     def __init__(self, ctx: Context, spec: LayerSpec, n_pages: int, page_rows: int = 128, batch: int = 1,
                  n_layers: int = 1, device=None):
@@ -198,7 +201,14 @@ class PagedKVCache:
         self.seq_len = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.host_len = [0] * batch
 
-    def reserve(self, b: int, rows: int) -> None:
+    def _upload_table(self, stream) -> None:
+        if self.block_table.device.type != "cuda":
+            self.block_table.copy_(self.table_host)
+            return
+        with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream(self.block_table.device)):
+            self.block_table.copy_(self.table_host)
+
+    def reserve(self, b: int, rows: int, stream=None) -> None:
         if rows > self.spec.kv_capacity:
             raise AttnError(EINVAL, f"{rows} rows exceed kv_capacity {self.spec.kv_capacity}")
         need = -(-rows // self.page_rows)
@@ -210,13 +220,13 @@ class PagedKVCache:
             pg = self.free.pop(0)
             self.table_host[b, len(self.pages[b])] = pg
             self.pages[b].append(pg)
-        self.block_table.copy_(self.table_host)
+        self._upload_table(stream)
 
-    def release(self, b: int) -> None:
+    def release(self, b: int, stream=None) -> None:
         self.free.extend(self.pages[b])
         self.pages[b] = []
         self.table_host[b] = -1
-        self.block_table.copy_(self.table_host)
+        self._upload_table(stream)
         self.host_len[b] = 0
         self.seq_len[b] = 0
 
@@ -314,7 +324,7 @@ class ComputeOps:
         B, S = q.shape[0], q.shape[1]
         spec = cache.spec
         for b in range(B):
-            cache.reserve(b, cache.host_len[b] + S)
+            cache.reserve(b, cache.host_len[b] + S, stream=self.stream)
         if out is None:
             odt = torch.float32 if spec.out_dtype == F32 else torch.float16
             out = torch.empty(B, S, spec.n_q_heads, spec.head_dim, dtype=odt, device=q.device)

@@ -252,9 +252,10 @@ class ContextShard:
 
 
 class NcclDist:
-    """aihost_attn_dist: the library's NCCL communicator for one rank (one process per GPU)."""
+    """aihost_attn_dist: the library's NCCL communicator for one rank (one process per GPU).
+    Set-up waits at most `timeout_ms` for the other ranks (AttnError ETIMEOUT otherwise)."""
 
-    def __init__(self, world: int, rank: int, nccl_id: bytes, device: int):
+    def __init__(self, world: int, rank: int, nccl_id: bytes, device: int, timeout_ms: int = 300000):
         import ctypes
 
         from . import check, lib
@@ -263,7 +264,8 @@ class NcclDist:
             raise ValueError("an NCCL unique id is 128 bytes")
         self._id = ctypes.create_string_buffer(nccl_id, 128)
         self._h = ctypes.c_void_p()
-        check(lib().aihost_attn_dist_init(world, rank, self._id, device, ctypes.byref(self._h)))
+        check(lib().aihost_attn_dist_init_bounded(world, rank, self._id, device, int(timeout_ms),
+                                                  ctypes.byref(self._h)))
         self.world, self.rank = world, rank
 
     @staticmethod
@@ -280,6 +282,14 @@ class NcclDist:
     @property
     def handle(self):
         return self._h
+
+    def sync(self, stream=None, timeout_ms: int = 60000) -> None:
+        """Wait at most timeout_ms for the stream's kernels and collectives (aborts the
+        communicator and raises AttnError ETIMEOUT / ENCCL when they do not finish)."""
+        from . import check, lib
+        from .ops import _stream
+
+        check(lib().aihost_attn_dist_sync(self._h, _stream(stream), int(timeout_ms)))
 
     def close(self) -> None:
         from . import lib

@@ -7,9 +7,13 @@ library's public C ABI (aihost_attn_forward) on one batch of seeded synthetic in
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
 Default workload: config 2 (causal prefill, Qwen2-0.5B shape, S=2048) -> TFLOP/s (causal-pair
-FLOPs), plus a `decode` object for config 3 (batched decode, Llama-3-8B shape) -> tokens/s and
-KV-read GB/s. N>1 (torchrun, one rank per GPU): every rank runs its own independent sequence(s)
-(sharding by sequence, no data-path collective), time = max over ranks, weak scaling.
+FLOPs) as the line's value, plus one object per other config of the workload list:
+`config_1` (fp32 decode, TinyLlama shape; single call, and 256 rotating layer caches),
+`config_3` (batched fp16 decode, Llama-3-8B shape), `config_4` (long prefill, S=32768) and
+`config_5` (Q8_0 batched decode, Llama-3-70B shape), each with its own value, roofline, e2e and
+CPU baseline. N>1 (torchrun, one rank per GPU): configs 1-3 run one independent sequence set per
+rank (no data-path collective, weak scaling); configs 4 and 5 split their KV heads over the ranks
+and all-gather the head outputs with NCCL (strong scaling). Time = max over ranks.
 --impl reference times the CPU restatement of the reference path (oracle/, faithful fp32 mode,
 all host threads) on bounded samples of the same workload.
 """
@@ -39,7 +43,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode object")
+    ap.add_argument("--no-decode", action="store_true", help="config 2: skip the objects of configs 1, 3, 4 and 5")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time")
     ap.add_argument("--shard", default="seq", choices=["seq", "heads", "rows", "context"],
@@ -215,10 +219,12 @@ def device_inputs(cfg, device, rank):
 
     from aihost_b200.configs import make_inputs
 
-    c = cfg.scaled(number=cfg.number + 1000 * rank) if rank else cfg
+    # Other ranks reseed the data but keep the global lengths (and so the same capacity and the
+    # same per-GPU work); a reseeded config would also redraw its lengths.
+    c = cfg.scaled(number=cfg.number + 1000 * rank, cached=None, cached_range=None,
+                   cached_list=cfg.lengths()) if rank else cfg
     inp = make_inputs(c, device=device)
-    inp["lengths"] = cfg.lengths()  # same lengths on every rank (same per-GPU work)
-    inp["seq_len"] = torch.tensor(inp["lengths"], dtype=torch.int32, device=device)
+    assert inp["lengths"] == cfg.lengths() and inp["capacity"] == cfg.capacity()
     return inp
 
 
@@ -261,8 +267,10 @@ def shard_inputs(cfg, device, rank, world):
     from aihost_b200.shard import HeadShard
 
     shard = HeadShard(cfg.spec(cfg.capacity()), rank, world)
-    local = cfg.scaled(number=cfg.number + 1000 * rank, n_q_heads=shard.q_per_rank, n_kv_heads=shard.kv_per_rank)
+    local = cfg.scaled(number=cfg.number + 1000 * rank, n_q_heads=shard.q_per_rank, n_kv_heads=shard.kv_per_rank,
+                       cached=None, cached_range=None, cached_list=cfg.lengths())
     inp = make_inputs(local, device=device)
+    assert inp["capacity"] == cfg.capacity()
     spec = shard.local_spec()
     spec.kv_capacity = inp["capacity"]
     rb = row_bytes(cfg.kv_dtype, cfg.head_dim) * shard.kv_per_rank
@@ -571,9 +579,7 @@ def summarize(cfg, r, n_gpus, dist_on, pk, pk_kind):
                 "frac": achieved / pk["hbm_gbs"], "traffic": None, "kernel": decode_kernel_name(cfg),
                 "kernel_ms": k_ms, "algorithmic_per_launch": w["kernel_bytes"], "peak_source": f"{pk_kind} copy",
                 "frac_of_8tbs_spec": achieved / 8000.0}
-    traffic = read_traffic(cfg.number)
-    if traffic is not None:
-        roof["traffic"] = traffic
+    roof["traffic"], roof["traffic_source"] = read_traffic(cfg.number)
     other = {k: {"launches": n, "mean_ms": (t / n if n else None)} for k, (n, t) in r["kern"].items()}
     out = dict(value=value, unit=unit, ms_per_step=ms_step, roofline=roof,
                e2e={"value": e2e_value, "unit": unit, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
@@ -585,28 +591,68 @@ def summarize(cfg, r, n_gpus, dist_on, pk, pk_kind):
     return out
 
 
+KERNEL_SOURCE = {1: "decode.cu", 2: "prefill_sm100.cu", 3: "decode_mma.cu", 4: "prefill_sm100.cu", 5: "decode_mma.cu"}
+
+
+def source_sha16(name: str) -> str:
+    import hashlib
+
+    return hashlib.sha256((ROOT / "aihost_b200" / "csrc" / name).read_bytes()).hexdigest()[:16]
+
+
 def read_traffic(config_number: int):
-    """DRAM bytes per launch of the dominant kernel from profiles/traffic.txt (ncu capture)."""
+    """DRAM bytes per launch of the dominant kernel of `config_number` from profiles/traffic.txt
+    (one ncu capture each). A line is `configN <bytes> <kernel source file> <sha256[:16] of that
+    file when captured>`; a figure whose source has changed since is stale and is not reported.
+    Returns (bytes or None, note)."""
     p = ROOT / "profiles" / "traffic.txt"
     if not p.exists():
-        return None
+        return None, "no capture"
     for ln in p.read_text().splitlines():
         parts = ln.split()
-        if len(parts) >= 2 and parts[0] == f"config{config_number}":
+        if len(parts) >= 4 and parts[0] == f"config{config_number}":
             try:
-                return float(parts[1])
+                nbytes = float(parts[1])
             except ValueError:
-                return None
-    return None
+                return None, "unreadable capture line"
+            if source_sha16(parts[2]) != parts[3]:
+                return None, f"stale: {parts[2]} changed since the capture ({parts[3]})"
+            return nbytes, f"ncu capture of {parts[2]} @ {parts[3]}"
+    return None, "no capture"
 
 
-def cfg_desc(cfg, lengths, flushed):
-    d = {"workload": f"config {cfg.number}: {cfg.name} ({cfg.note})", "batch": cfg.batch, "n_q_heads": cfg.n_q_heads,
-         "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim, "n_new": cfg.n_new, "rope_theta": cfg.theta,
-         "cached_rows_total": int(sum(lengths)),
-         "l2": "flushed between steps (write of a 512 MiB buffer, outside the timed events)" if flushed
-         else "inputs larger than L2"}
-    return d
+def needs_flush(cfg, shard_mode="seq", world=1) -> bool:
+    """True when one step of this rank streams less than 2x the 126 MB L2, so the bench writes a
+    512 MiB buffer between steps (outside the timed events) to start every step cold."""
+    w = work(rank_cfg(cfg, shard_mode, world), cfg.lengths())
+    return w["bytes"] < 2 * 126e6
+
+
+def rank_cfg(cfg, shard_mode, world):
+    """The share of `cfg` one rank computes: its KV heads under head sharding, else all of it."""
+    if shard_mode == "heads" and world > 1:
+        return cfg.scaled(n_q_heads=cfg.n_q_heads // world, n_kv_heads=cfg.n_kv_heads // world)
+    return cfg
+
+
+def parallelism(shard_mode, world, rank_rows=None) -> str:
+    if world <= 1:
+        return "single GPU"
+    return {"heads": f"KV heads split over {world} ranks + NCCL all-gather of head outputs",
+            "rows": f"query rows split over {world} ranks (causal-balanced 128-row blocks, rank 0 rows {rank_rows}) "
+                    f"+ NCCL all-gather of row blocks",
+            "context": f"every sequence's cached rows split into {world} chunks (context parallel) + NCCL all-gather "
+                       f"of (out, lse) + merge kernel"}.get(shard_mode, "one independent sequence set per rank")
+
+
+def cfg_desc(cfg, shard_mode="seq", world=1, rank_rows=None):
+    """The `config` object of a bench line; the reference arm prints the same one for the same run."""
+    return {"workload": f"config {cfg.number}: {cfg.name} ({cfg.note})", "batch": cfg.batch,
+            "n_q_heads": cfg.n_q_heads, "n_kv_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim, "n_new": cfg.n_new,
+            "rope_theta": cfg.theta, "cached_rows_total": int(sum(cfg.lengths())),
+            "l2": "flushed between steps (write of a 512 MiB buffer, outside the timed events)"
+            if needs_flush(cfg, shard_mode, world) else "inputs larger than L2",
+            "parallelism": parallelism(shard_mode, world, rank_rows)}
 
 
 def init_dist(args):
@@ -658,7 +704,7 @@ def run_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (reference arithmetic on fp16-converted inputs)",
             "data": "synthetic (seeded SplitMix64 + Box-Muller)",
-            "config": cfg_desc(cfg, cfg.lengths(), False),
+            "config": cfg_desc(cfg, args.shard, int(os.environ.get("WORLD_SIZE", "1"))),
             "cpu_baseline": {"value": value, "unit": meta["unit"], "cores": meta["cores"], "kind": "port",
                              "sample": meta["sample"]},
             "e2e": {"value": value, "unit": meta["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -768,6 +814,34 @@ def bench_qk_norm(args, device, pk, pk_kind):
     print(json.dumps(line), flush=True)
 
 
+def config_object(cfg, shard_mode, args, device, ctx, dist_on, ws, rank, pk, pk_kind, cpu_s, layers=0):
+    """One config's measurements as a JSON object: the device-timed value, the dominant kernel's
+    roofline, the end-to-end value through the C ABI with host buffers, and (rank 0, N = 1) the
+    CPU baseline and, for decode configs with `layers`, the rotating-cache throughput."""
+    steps = args.steps if cfg.n_new > 1 else max(args.steps, 10)
+    r = bench_ours(cfg, steps, args.warmup, device, ctx, 512 << 20, dist_on, shard_mode=shard_mode,
+                   paged=args.paged)
+    res = summarize(cfg, r, ws, dist_on, pk, pk_kind)
+    res["config"] = cfg_desc(cfg, shard_mode, ws, r.get("rank_rows"))
+    res["scaling"] = "strong" if (ws > 1 and shard_mode != "seq") else "weak"
+    res["dtype"] = "f32" if cfg.q_dtype == 0 else "f16 (fp32 accumulate)"
+    kern_ms = sum(v["mean_ms"] or 0.0 for v in res["kernels"].values() if v["launches"])
+    if ws > 1 and shard_mode != "seq":
+        # NCCL collective(s) plus launch gaps: the step time this library's kernels do not cover
+        res["collective_ms"] = max(0.0, res["ms_per_step"] - max_over_ranks(kern_ms, dist_on))
+    if layers > 0 and cfg.n_new == 1 and ws == 1:
+        l_ms, l_bytes = bench_layers(cfg, layers, max(args.steps, 10), args.warmup, device, ctx)
+        res["layers"] = {"layers": layers, "ms_per_step": l_ms, "tokens_per_s": cfg.batch * layers / (l_ms * 1e-3),
+                         "kv_read_gbs": l_bytes / (l_ms * 1e-3) * 1e-9,
+                         "frac_of_measured_hbm": l_bytes / (l_ms * 1e-3) * 1e-9 / pk["hbm_gbs"],
+                         "note": "one CUDA graph of `layers` fused calls on distinct caches (together larger than "
+                                 "L2, so the bytes come from HBM), replayed per step; bytes = algorithmic bytes of "
+                                 "every layer's call"}
+    if rank == 0 and ws == 1 and cpu_s > 0:
+        res["cpu_baseline"] = cpu_baseline(cfg, cpu_s)
+    return res
+
+
 def main():
     args = parse_args()
     if args.warmup < 3:
@@ -799,58 +873,36 @@ def main():
     ctx = Context(local)
     clocks = ClockSampler(local).start()
     cfg = CONFIGS[args.config]
-    flush_bytes = 512 << 20
-    heads = args.shard == "heads"
-    row_mode = args.shard == "rows"
-    cp_mode = args.shard == "context"
-    r = bench_ours(cfg, args.steps, args.warmup, device, ctx, flush_bytes, dist_on, shard_mode=args.shard,
-                   paged=args.paged)
-    main_res = summarize(cfg, r, ws, dist_on, pk, pk_kind)
-    dec = None
+    cpu_main = 0.0 if args.no_cpu else args.cpu_seconds
+    main_res = config_object(cfg, args.shard, args, device, ctx, dist_on, ws, rank, pk, pk_kind, cpu_main,
+                             layers=args.layers)
+    # The default run (config 2 headline) measures every other BASELINE config too: config 1
+    # (fp32 decode; with 256 rotating layer caches at N = 1), config 3 (batched fp16 decode), and
+    # configs 4 and 5 with their KV heads split over the ranks (one NCCL all-gather of the head
+    # outputs) at N > 1, as the workload names them.
+    extra = {}
     if args.config == 2 and not args.no_decode:
-        c3 = CONFIGS[3]
-        r3 = bench_ours(c3, max(args.steps, 10), args.warmup, device, ctx, flush_bytes, dist_on)
-        dec = summarize(c3, r3, ws, dist_on, pk, pk_kind)
-        dec["config"] = cfg_desc(c3, r3["lengths"], r3["flushed"])
-        main_res["gpu_launches_decode"] = dec.pop("gpu_launches")
+        cpu_other = 0.0 if args.no_cpu else min(args.cpu_seconds, 6.0)
+        plan = [(1, "seq", 256), (3, "seq", 0), (4, "heads" if ws > 1 else "seq", 0),
+                (5, "heads" if ws > 1 else "seq", 0)]
+        for number, mode, layers in plan:
+            extra[f"config_{number}"] = config_object(CONFIGS[number], mode, args, device, ctx, dist_on, ws, rank,
+                                                      pk, pk_kind, cpu_other, layers=layers if ws == 1 else 0)
     clk = clocks.stop()
-    cpu = None
-    layers_res = None
-    if args.layers > 0 and cfg.n_new == 1 and ws == 1:
-        l_ms, l_bytes = bench_layers(cfg, args.layers, max(args.steps, 10), args.warmup, device, ctx)
-        layers_res = {"layers": args.layers, "ms_per_step": l_ms, "tokens_per_s": cfg.batch / (l_ms * 1e-3),
-                      "kv_read_gbs": l_bytes / (l_ms * 1e-3) * 1e-9,
-                      "frac_of_measured_hbm": l_bytes / (l_ms * 1e-3) * 1e-9 / pk["hbm_gbs"],
-                      "note": "one CUDA graph of `layers` fused calls on distinct caches (HBM-resident), "
-                              "replayed per step; bytes = algorithmic bytes of every layer's call"}
-    if rank == 0 and ws == 1 and not args.no_cpu:
-        cpu = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
         line = {"metric": METRIC, "value": main_res["value"], "unit": main_res["unit"], "n_gpus": ws,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": main_res["ms_per_step"],
-                "higher_is_better": True, "scaling": "strong" if (heads or row_mode or cp_mode) else "weak",
-                "vs_baseline": None,
-                "dtype": "f16 (fp32 accumulate)" if cfg.q_dtype == 1 else "f32",
-                "data": "synthetic (seeded SplitMix64 + Box-Muller, no model weights)",
-                "config": {**cfg_desc(cfg, r["lengths"], r["flushed"]),
-                           "parallelism": (f"KV heads split over {ws} ranks + NCCL all-gather of head outputs"
-                                           if heads else
-                                           f"query rows split over {ws} ranks (causal-balanced 128-row blocks, "
-                                           f"rank 0 rows {r['rank_rows']}) + NCCL all-gather of row blocks"
-                                           if row_mode else
-                                           f"every sequence's cached rows split into {ws} chunks (context "
-                                           f"parallel) + NCCL all-gather of (out, lse) + merge kernel"
-                                           if cp_mode else "one independent sequence set per rank")
-                           if ws > 1 else "single GPU"},
-                "roofline": main_res["roofline"], "cpu_baseline": cpu, "e2e": main_res["e2e"],
+                "higher_is_better": True, "scaling": main_res["scaling"], "vs_baseline": None,
+                "dtype": main_res["dtype"], "data": "synthetic (seeded SplitMix64 + Box-Muller, no model weights)",
+                "config": main_res["config"], "roofline": main_res["roofline"],
+                "cpu_baseline": main_res.get("cpu_baseline"), "e2e": main_res["e2e"],
                 "kv_layout": (f"paged: {args.paged}-row pages of a shared pool, shuffled order, block table"
                               if args.paged else "contiguous per sequence"),
-                "gpu_launches": main_res["gpu_launches"], "clocks": clk, "kernels": main_res["kernels"],
-                "wall_s_timed_region": r["wall"]}
-        if dec is not None:
-            line["decode"] = dec
-        if layers_res is not None:
-            line["layers"] = layers_res
+                "gpu_launches": main_res["gpu_launches"], "clocks": clk, "kernels": main_res["kernels"]}
+        for key in ("layers", "collective_ms", "kv_read_gbs", "kv_read_frac_of_8tbs"):
+            if key in main_res:
+                line[key] = main_res[key]
+        line.update(extra)
         print(json.dumps(line), flush=True)
     ctx.close()
     if dist_on:

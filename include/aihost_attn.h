@@ -10,8 +10,7 @@
  * (AIHost/AIHost/Compute/ComputeOps.cs:1279-1304, Formats/CombinedQKVFormat.cs:52-67,
  *  Formats/QwenHybridFormat.cs:141-145). The reference dispatches these as GLSL compute shaders
  * through Vulkan; its CUDA backend (ICompute/CUDA/CudaComputeCommandQueue.cs:56-61) cannot
- * dispatch at all. A C# host binds the functions below with [DllImport("aihost_attn")]; the
- * binding is listed in INTEGRATION.md.
+ * dispatch at all. A C# host binds the functions below with [DllImport("aihost_attn")].
  *
  * Conventions (mirroring ICompute/CUDA/CudaApi.cs:11-92, where every native call returns an
  * error enum that the caller checks):
@@ -189,11 +188,20 @@ aihost_status aihost_attn_profiler_reset(aihost_attn_ctx* ctx);
  * split scratch, batch * n_q_heads * splits * (head_dim + 2) * 4 bytes, exceeds 8 MiB return
  * AIHOST_ENOMEM. Runs on the current CUDA device. The first call on each device looks up the
  * array's device address: make it before any stream capture. All calls share the array, so
- * calls that overlap on the GPU race; serialise them. Results equal aihost_attn_forward's. */
+ * calls that overlap on the GPU race; serialise them. Results equal aihost_attn_forward's.
+ * Errors the kernels find on the device (a seq_len past kv_capacity, a bounded wait that ran
+ * out) are collected in a status word of the array; read them with the call below. */
 aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc, int32_t batch, const void* q,
                                          const void* k_new, const void* v_new, void* k_cache, void* v_cache,
                                          const int32_t* seq_len, const int32_t* h_seq_len, void* out,
                                          void* stream);
+/* No counterpart in the reference. The status read of aihost_attn_decode_noalloc, which has no
+ * context and so no aihost_attn_sync_status: waits for `stream` (the stream of the decode calls),
+ * then reads and clears the current device's no-alloc status word, which holds the error bits of
+ * every no-alloc call since the last read. Returns AIHOST_EINVAL for a device-side length past
+ * kv_capacity, AIHOST_ETIMEOUT for an expired wait, else AIHOST_OK; *out_bits (may be NULL)
+ * receives the raw bits. Allocates nothing. */
+aihost_status aihost_attn_noalloc_sync_status(void* stream, int32_t* out_bits);
 
 /* ---- KV-head sharding across GPUs (one process per GPU, NCCL over NVLink). Replaces the
  * reference's layer split with host staging (Inference/MultiGPUTransformer.cs:48-183).
@@ -202,14 +210,29 @@ aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc, int32_t b
 typedef struct aihost_attn_dist aihost_attn_dist;
 /* One rank creates the 128-byte NCCL id and the host hands it to every rank. */
 aihost_status aihost_attn_dist_unique_id(void* out_id);
-/* Collective over all ranks (blocks until every rank has called it). */
+/* Collective over all ranks: returns once every rank has called it, or after timeout_ms with
+ * AIHOST_ETIMEOUT (a rank that never joins; the half-built communicator is aborted and nothing is
+ * returned). The communicator is nonblocking: every NCCL wait of this library is a bounded host
+ * poll, never an unbounded block. No counterpart in the reference, whose waits are unbounded
+ * (ICompute/Vulkan/VulkanComputeCommandQueue.cs:287). */
+aihost_status aihost_attn_dist_init_bounded(int32_t world, int32_t rank, const void* nccl_id, int32_t device,
+                                            int32_t timeout_ms, aihost_attn_dist** out);
+/* aihost_attn_dist_init_bounded with the limit AIHOST_NCCL_TIMEOUT_MS from the environment
+ * (default 300000 ms). */
 aihost_status aihost_attn_dist_init(int32_t world, int32_t rank, const void* nccl_id, int32_t device,
                                     aihost_attn_dist** out);
 aihost_status aihost_attn_dist_destroy(aihost_attn_dist* dist);
+/* Waits at most timeout_ms for everything enqueued on `stream` (this rank's kernels and
+ * collectives) to finish. AIHOST_ETIMEOUT when it does not (a peer that stopped taking part) and
+ * AIHOST_ENCCL on an asynchronous NCCL error; in both cases the communicator is aborted, which
+ * ends its in-flight collectives, and later sharded calls on it return AIHOST_ENCCL. The host's
+ * replacement for a Flush() fence wait (ComputeOps.cs:115-140) on the sharded path. */
+aihost_status aihost_attn_dist_sync(aihost_attn_dist* dist, void* stream, int32_t timeout_ms);
 /* aihost_attn_forward of this rank's heads (`local`: n_q_heads = Hq/N, n_kv_heads = Hkv/N and the
  * local cache layout), written into this rank's slot of out_gathered, then one in-place
  * all-gather on `stream`: out_gathered is [N][batch][n_new][Hq/N][head_dim] (rank-major) on every
- * rank. Every rank must make the same calls in the same order. */
+ * rank. Every rank must make the same calls in the same order. ctx and dist must be on the same
+ * device (AIHOST_EINVAL otherwise). */
 aihost_status aihost_attn_forward_sharded(aihost_attn_dist* dist, aihost_attn_ctx* ctx,
                                           const aihost_attn_desc* local, int32_t batch, int32_t n_new,
                                           const void* q, const void* k_new, const void* v_new,

@@ -309,11 +309,13 @@ static void store_row(uint8_t* dst, int32_t dtype, const float* x, int32_t head_
   else oracle_q8_0_quantize(x, head_dim, dst);
 }
 
-int32_t oracle_attn_forward_part(const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
+int32_t oracle_attn_forward_rows(const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
                                  const void* q, const void* k_new, const void* v_new,
                                  void* k_cache, void* v_cache, const int32_t* seq_len, void* out,
-                                 int32_t mode, int32_t b0, int32_t b1, int32_t h0, int32_t h1) {
+                                 int32_t mode, int32_t b0, int32_t b1, int32_t h0, int32_t h1,
+                                 int32_t r0, int32_t r1) {
   if (!desc || !q || !k_new || !v_new || !k_cache || !v_cache || !seq_len || !out) return 1;
+  if (r0 < 0 || r1 > n_new || r0 >= r1) return 1;
   const int32_t Hq = desc->n_q_heads, Hkv = desc->n_kv_heads, D = desc->head_dim;
   if (batch < 1 || n_new < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv || D < 2 || D % 2 || D > 256) return 1;
   if (desc->kv_dtype == AIHOST_Q8_0 && D % 32) return 1;
@@ -370,7 +372,7 @@ int32_t oracle_attn_forward_part(const aihost_attn_desc* desc, int32_t batch, in
 #pragma omp for collapse(3) schedule(dynamic, 1)
       for (int32_t b = b0; b < b1; ++b)
         for (int32_t h = h0; h < h1; ++h)
-          for (int32_t i = 0; i < n_new; ++i) {
+          for (int32_t i = r0; i < r1; ++i) {
             const int32_t P = seq_len[b];
             const kv_view kk = {(const uint8_t*)k_cache + (int64_t)b * seq_stride, desc->kv_dtype, tok_stride, head_stride};
             const kv_view vv = {(const uint8_t*)v_cache + (int64_t)b * seq_stride, desc->kv_dtype, tok_stride, head_stride};
@@ -389,6 +391,14 @@ int32_t oracle_attn_forward_part(const aihost_attn_desc* desc, int32_t batch, in
   (void)out_es;
   free(qf);
   return err;
+}
+
+int32_t oracle_attn_forward_part(const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
+                                 const void* q, const void* k_new, const void* v_new,
+                                 void* k_cache, void* v_cache, const int32_t* seq_len, void* out,
+                                 int32_t mode, int32_t b0, int32_t b1, int32_t h0, int32_t h1) {
+  return oracle_attn_forward_rows(desc, batch, n_new, q, k_new, v_new, k_cache, v_cache, seq_len, out, mode, b0, b1,
+                                  h0, h1, 0, n_new);
 }
 
 int32_t oracle_attn_forward(const aihost_attn_desc* desc, int32_t batch, int32_t n_new,

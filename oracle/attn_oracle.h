@@ -84,6 +84,13 @@ int32_t oracle_attn_forward_part(const aihost_attn_desc* desc, int32_t batch, in
                                  const void* q, const void* k_new, const void* v_new,
                                  void* k_cache, void* v_cache, const int32_t* seq_len, void* out,
                                  int32_t mode, int32_t b0, int32_t b1, int32_t h0, int32_t h1);
+/* As oracle_attn_forward_part, attending only query rows [r0, r1) of every selected sequence and
+ * head (the append still covers all n_new rows): samples of long prefills. */
+int32_t oracle_attn_forward_rows(const aihost_attn_desc* desc, int32_t batch, int32_t n_new,
+                                 const void* q, const void* k_new, const void* v_new,
+                                 void* k_cache, void* v_cache, const int32_t* seq_len, void* out,
+                                 int32_t mode, int32_t b0, int32_t b1, int32_t h0, int32_t h1,
+                                 int32_t r0, int32_t r1);
 
 #ifdef __cplusplus
 }

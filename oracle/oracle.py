@@ -48,6 +48,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_attn_forward.restype = i32
         L.oracle_attn_forward_part.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32]
         L.oracle_attn_forward_part.restype = i32
+        L.oracle_attn_forward_rows.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32,
+                                               i32]
+        L.oracle_attn_forward_rows.restype = i32
         _LIB = L
     return _LIB
 
@@ -124,11 +127,12 @@ def mha(q: np.ndarray, k: np.ndarray, v: np.ndarray, n_q_heads: int, start_pos: 
 
 
 def attn_forward(desc, q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, k_cache: np.ndarray,
-                 v_cache: np.ndarray, seq_len: np.ndarray, mode: int = EXACT, part=None) -> np.ndarray:
+                 v_cache: np.ndarray, seq_len: np.ndarray, mode: int = EXACT, part=None, rows=None) -> np.ndarray:
     """The fused forward on host arrays; k_cache / v_cache (uint8 bytes) are appended in place.
 
     desc is an aihost_b200.AttnDesc (the same struct the C ABI takes). part = (b0, b1, h0, h1)
-    restricts the sequences and query heads computed (bounded CPU-baseline samples)."""
+    restricts the sequences and query heads computed (bounded CPU-baseline samples); rows =
+    (r0, r1) further restricts the attended query rows (the other rows of `out` stay zero)."""
     B, S = q.shape[0], q.shape[1]
     out_dt = np.float32 if desc.out_dtype == 0 else np.float16
     out = np.zeros((B, S, desc.n_q_heads, desc.head_dim), dtype=out_dt)
@@ -136,7 +140,11 @@ def attn_forward(desc, q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, k_ca
     for c in (k_cache, v_cache):
         assert c.flags["C_CONTIGUOUS"] and c.dtype == np.uint8
     sl = np.ascontiguousarray(seq_len, dtype=np.int32)
-    if part is None:
+    if rows is not None:
+        p = part if part is not None else (0, B, 0, desc.n_q_heads)
+        rc = lib().oracle_attn_forward_rows(ctypes.addressof(desc), B, S, *(_p(a) for a in arrs), _p(k_cache),
+                                            _p(v_cache), _p(sl), _p(out), mode, *p, *rows)
+    elif part is None:
         rc = lib().oracle_attn_forward(ctypes.addressof(desc), B, S, *(_p(a) for a in arrs), _p(k_cache),
                                        _p(v_cache), _p(sl), _p(out), mode)
     else:

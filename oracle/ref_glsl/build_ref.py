@@ -11,6 +11,8 @@ glsl_runtime.cpp. Nothing from the reference is copied into the repository: the 
 translation unit and the library live only in oracle/_ref/ (git-ignored).
 
 Usage: python oracle/ref_glsl/build_ref.py [--reference PATH_TO_REFERENCE_CHECKOUT]
+The checkout defaults to $AIHOST_REFERENCE_DIR, else a directory named `reference` beside this
+repository's root.
 """
 from __future__ import annotations
 
@@ -22,6 +24,14 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE.parent / "_ref"
+
+
+def default_reference() -> Path:
+    """$AIHOST_REFERENCE_DIR, else `reference` beside the repository root."""
+    import os
+
+    env = os.environ.get("AIHOST_REFERENCE_DIR")
+    return Path(env) if env else HERE.parent.parent.parent / "reference"
 
 # ComputeShaders field name -> (shader name used by TryLoadOrInline, inline constant)
 SHADERS = {
@@ -117,7 +127,7 @@ def translate(name: str, src: str) -> str:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=str(default_reference()))
     args = ap.parse_args()
     ref = Path(args.reference)
     if not (ref / "AIHost/AIHost/Compute/ComputeShaders.cs").exists():

@@ -25,8 +25,9 @@ def gpu_forward(ctx, cfg: AttnConfig, inp: dict, pass_host_len: bool = True):
     return out.cpu(), cache.k[0].cpu(), cache.v[0].cpu()
 
 
-def oracle_forward(cfg: AttnConfig, inp: dict, mode=None, part=None):
-    """The same call on the CPU oracle. Returns (out, k_cache, v_cache) as numpy arrays."""
+def oracle_forward(cfg: AttnConfig, inp: dict, mode=None, part=None, rows=None):
+    """The same call on the CPU oracle (part = (b0, b1, h0, h1) sequences and query heads, rows =
+    (r0, r1) query rows; None = all). Returns (out, k_cache, v_cache) as numpy arrays."""
     from oracle import oracle as orc
 
     mode = orc.EXACT if mode is None else mode
@@ -34,7 +35,7 @@ def oracle_forward(cfg: AttnConfig, inp: dict, mode=None, part=None):
     kc = inp["k_cache"].numpy().copy()
     vc = inp["v_cache"].numpy().copy()
     q, kn, vn = (inp[n].numpy() for n in ("q", "k_new", "v_new"))
-    out = orc.attn_forward(desc, q, kn, vn, kc, vc, inp["seq_len"].numpy(), mode=mode, part=part)
+    out = orc.attn_forward(desc, q, kn, vn, kc, vc, inp["seq_len"].numpy(), mode=mode, part=part, rows=rows)
     return out, kc, vc
 
 

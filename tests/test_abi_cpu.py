@@ -77,6 +77,24 @@ def test_null_context_and_pointers_rejected():
     assert L.aihost_attn_sync_status(None, None) == A.EINVAL
 
 
+def test_dist_calls_validate_arguments_before_nccl():
+    """The bounded NCCL set-up and wait reject bad arguments without loading NCCL or a device."""
+    L = A.lib()
+    nid = ctypes.create_string_buffer(128)
+    h = ctypes.c_void_p()
+    assert L.aihost_attn_dist_init_bounded(2, 0, nid, 0, 1000, None) == A.EINVAL
+    assert L.aihost_attn_dist_init_bounded(2, 0, None, 0, 1000, ctypes.byref(h)) == A.EINVAL
+    assert L.aihost_attn_dist_init_bounded(2, 2, nid, 0, 1000, ctypes.byref(h)) == A.EINVAL
+    assert L.aihost_attn_dist_init_bounded(2, 0, nid, 0, 0, ctypes.byref(h)) == A.EINVAL
+    assert b"timeout_ms" in L.aihost_attn_last_error()
+    assert not h
+    assert L.aihost_attn_dist_sync(None, None, 1000) == A.EINVAL
+    d = LayerSpec(8, 2, 64, kv_capacity=64).desc()
+    assert L.aihost_attn_forward_sharded(None, None, ctypes.byref(d), 1, 1, None, None, None, None, None, None, None,
+                                         None, None) == A.EINVAL
+    assert L.aihost_attn_noalloc_sync_status is not None
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
 def test_create_without_device_fails_cleanly():
     h = ctypes.c_void_p()

@@ -47,6 +47,7 @@ def _run_rank(rank, world, nccl_id, cfg, capacity, device):
         dev = torch.device("cuda", device)
         out = shard.forward(dist, ComputeOps(ctx), shard.slice_q(inp["q"]).to(dev), shard.slice_kv(inp["k_new"]).to(dev),
                             shard.slice_kv(inp["v_new"]).to(dev), cache)
+        dist.sync(timeout_ms=60000)  # bounded wait for the kernels and the all-gather
         torch.cuda.synchronize()
         ctx.sync_status()
         return HeadShard.to_reference_layout(out.cpu()).float().numpy(), inp

@@ -128,6 +128,29 @@ def test_prefill_cfg2_full(ctx):
     check_call(ctx, CONFIGS[2], part=(0, 1, 0, 14))
 
 
+def test_prefill_cfg4_full_sample(ctx):
+    """Config 4 at its real size: S = 32768, Hq 32 / Hkv 8, d 128 (up to 256 cache tiles per query
+    tile, thousands of online-softmax steps, the pair schedule at full occupancy). The whole call
+    runs on the GPU; the oracle checks query heads 0 and 31 (the first and the last KV head) on
+    the first query tile, a middle block and the last 256 rows, which attend every cache tile;
+    the appended V rows of those KV heads must equal the oracle's bit for bit."""
+    cfg = CONFIGS[4]
+    inp = make_inputs(cfg)
+    out, _, vc = gpu_forward(ctx, cfg, inp)
+    out = out.float().numpy()
+    assert np.isfinite(out).all()
+    S, cap, D = cfg.n_new, inp["capacity"], cfg.head_dim
+    gv = vc.numpy().view(np.float16).reshape(cap, cfg.n_kv_heads, D)
+    for h in (0, cfg.n_q_heads - 1):
+        kvh = h // (cfg.n_q_heads // cfg.n_kv_heads)
+        for r0, r1 in ((0, 128), (S // 2 - 64, S // 2 + 64), (S - 256, S)):
+            ref, _, rvc = oracle_forward(cfg, inp, part=(0, 1, h, h + 1), rows=(r0, r1))
+            err = max_abs(out[:, r0:r1, h], ref[:, r0:r1, h])
+            assert err <= TOL[F16], f"head {h} rows [{r0}, {r1}): max |gpu - oracle| = {err:.3g}"
+        rv = rvc.view(np.float16).reshape(cap, cfg.n_kv_heads, D)
+        assert np.array_equal(gv[:S, kvh], rv[:S, kvh]), f"appended V rows of KV head {kvh} differ"
+
+
 @pytest.mark.parametrize("s", [2, 37, 128, 129, 300])
 @pytest.mark.parametrize("d", [64, 128])
 def test_prefill_ragged(ctx, s, d):

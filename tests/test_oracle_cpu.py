@@ -184,3 +184,16 @@ def test_faithful_forward_close_to_exact():
 
 def test_num_threads_positive():
     assert orc.num_threads() >= 1
+
+
+def test_oracle_row_range_equals_full_rows():
+    """oracle_attn_forward_rows (samples of long prefills) computes exactly the full call's rows."""
+    from helpers import oracle_forward
+
+    cfg = CONFIGS[2].scaled(n_new=300, n_q_heads=4, n_kv_heads=2, cached=None, cached_list=[37])
+    inp = make_inputs(cfg)
+    full, fk, fv = oracle_forward(cfg, inp)
+    sub, sk, sv = oracle_forward(cfg, inp, part=(0, 1, 1, 3), rows=(100, 250))
+    assert np.array_equal(full[:, 100:250, 1:3], sub[:, 100:250, 1:3])
+    assert not sub[:, :100].any() and not sub[:, 250:].any()
+    assert np.array_equal(fv, sv)  # query heads 1-2 use both KV heads: every new row is appended

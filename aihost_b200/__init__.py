@@ -16,6 +16,7 @@ OK, EINVAL, ENOMEM, ECUDA, ETIMEOUT, EUNSUPPORTED, ENCCL = range(7)
 STATUS_NAMES = {0: "OK", 1: "EINVAL", 2: "ENOMEM", 3: "ECUDA", 4: "ETIMEOUT", 5: "EUNSUPPORTED", 6: "ENCCL"}
 # aihost_dtype (AIHost DataType ordinals)
 F32, F16, Q8_0 = 0, 1, 6
+Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 8, 9, 10, 11, 12
 # aihost_rope_mode
 ROPE_INTERLEAVED, ROPE_NEOX, ROPE_NONE = 0, 1, 2
 
@@ -28,9 +29,10 @@ EXPORTS = (
     "aihost_attn_dist_unique_id", "aihost_attn_dist_init", "aihost_attn_dist_destroy", "aihost_attn_forward_sharded",
     "aihost_attn_decode_partial", "aihost_attn_merge_partials", "aihost_qk_norm_rope", "aihost_attn_forward_paged",
     "aihost_attn_noalloc_sync_status", "aihost_attn_dist_init_bounded", "aihost_attn_dist_sync",
+    "aihost_matmul_workspace_size", "aihost_matmul_weights", "aihost_dequantize",
 )
 # aihost_kernel ids of the device-time profiler
-KERNEL_APPEND, KERNEL_DECODE, KERNEL_COMBINE, KERNEL_PREFILL, KERNEL_CONVERT = range(5)
+KERNEL_APPEND, KERNEL_DECODE, KERNEL_COMBINE, KERNEL_PREFILL, KERNEL_CONVERT, KERNEL_MATMUL = range(6)
 
 
 class AttnDesc(ctypes.Structure):
@@ -85,6 +87,9 @@ def lib() -> ctypes.CDLL:
     L.aihost_attn_dist_init_bounded.argtypes = [i32, i32, vp, i32, i32, ctypes.POINTER(vp)]
     L.aihost_attn_dist_destroy.argtypes = [vp]
     L.aihost_attn_dist_sync.argtypes = [vp, vp, i32]
+    L.aihost_matmul_workspace_size.argtypes = [vp, ctypes.POINTER(sz)]
+    L.aihost_matmul_weights.argtypes = [vp, vp, vp, vp, vp, vp]
+    L.aihost_dequantize.argtypes = [vp, i32, ctypes.c_int64, vp, i32, vp]
     L.aihost_attn_forward_sharded.argtypes = [vp, vp, dp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.aihost_attn_decode_partial.argtypes = [vp, dp, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     L.aihost_attn_merge_partials.argtypes = [vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]
@@ -105,5 +110,5 @@ def check(status: int) -> None:
         raise AttnError(status, msg.decode() if msg else "")
 
 
-__all__ = ["lib", "check", "AttnDesc", "AttnError", "F32", "F16", "Q8_0", "ROPE_INTERLEAVED", "ROPE_NEOX",
+__all__ = ["lib", "check", "AttnDesc", "AttnError", "F32", "F16", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "ROPE_INTERLEAVED", "ROPE_NEOX",
            "ROPE_NONE", "EXPORTS", "LIB_PATH"]

@@ -15,7 +15,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libaihost_attn.so"
-SOURCES = ["api.cu", "rope_append.cu", "decode.cu", "prefill_sm100.cu", "noalloc.cu", "decode_mma.cu", "dist.cu"]
+SOURCES = ["api.cu", "rope_append.cu", "decode.cu", "prefill_sm100.cu", "noalloc.cu", "decode_mma.cu", "dist.cu",
+           "matmul_sm100.cu"]
 HEADERS = ["common.cuh", "kernels.h", "rows.cuh"]
 
 

@@ -9,6 +9,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -874,6 +875,181 @@ aihost_status aihost_attn_profiler_reset(aihost_attn_ctx* ctx) {
     ctx->prof[k].launches = 0;
     ctx->prof[k].total_ms = 0.0;
   }
+  return AIHOST_OK;
+}
+
+// ------------------------------------------------------------------ weight products
+}  // extern "C"
+
+namespace {
+
+bool is_kquant(int32_t t) { return t >= AIHOST_Q2_K && t <= AIHOST_Q6_K; }
+
+aihost_status check_matmul(const aihost_matmul_desc* d) {
+  if (!d) return fail(AIHOST_EINVAL, "desc is NULL");
+  if (d->rows < 1 || d->k < 1 || d->n_out < 1 || d->n_parts < 1)
+    return fail(AIHOST_EINVAL, "rows (%d), k (%d), n_out (%d) and n_parts (%d) must be >= 1", d->rows, d->k,
+                d->n_out, d->n_parts);
+  if (d->k % 64 || d->k % d->n_parts || (d->k / d->n_parts) % 64)
+    return fail(AIHOST_EINVAL, "k (%d) and k / n_parts must be multiples of 64", d->k);
+  if (d->n_out % 8) return fail(AIHOST_EINVAL, "n_out (%d) must be a multiple of 8", d->n_out);
+  if (d->a_dtype != AIHOST_F16 && d->a_dtype != AIHOST_F32) return fail(AIHOST_EINVAL, "a_dtype must be F16 or F32");
+  if (d->out_dtype != AIHOST_F16 && d->out_dtype != AIHOST_F32)
+    return fail(AIHOST_EINVAL, "out_dtype must be F16 or F32");
+  if (d->w_dtype != AIHOST_F16 && d->w_dtype != AIHOST_F32 && !is_kquant(d->w_dtype))
+    return fail(AIHOST_EINVAL, "w_dtype %d must be F16, F32 or a K-quant (Q2_K..Q6_K)", d->w_dtype);
+  if (is_kquant(d->w_dtype) && d->k % 256)
+    return fail(AIHOST_EINVAL, "k (%d) must be a multiple of 256 for K-quant weights", d->k);
+  return AIHOST_OK;
+}
+
+struct GemmPlan {
+  int32_t block_n, k_splits, kt_per_split;
+  size_t a_stage, w_stage, partials;  // scratch bytes (each rounded to 256)
+};
+
+GemmPlan plan_gemm(const aihost_matmul_desc* d, int32_t num_sms) {
+  GemmPlan p;
+  p.block_n = gemm_block_n(d->rows, d->n_out, num_sms);
+  const int64_t tiles = static_cast<int64_t>((d->rows + 127) / 128) * ((d->n_out + p.block_n - 1) / p.block_n);
+  const int32_t kt_total = d->k / 64;
+  int64_t splits = 1;
+  if (p.block_n == 64 && tiles < 2LL * num_sms && tiles <= kMaxSplitCounters)
+    splits = std::min<int64_t>(kt_total, (2LL * num_sms + tiles - 1) / tiles);
+  p.kt_per_split = static_cast<int32_t>((kt_total + splits - 1) / splits);
+  p.k_splits = (kt_total + p.kt_per_split - 1) / p.kt_per_split;
+  p.a_stage = d->a_dtype == AIHOST_F16 ? 0 : round256(static_cast<size_t>(d->rows) * d->k * 2);
+  p.w_stage = d->w_dtype == AIHOST_F16 ? 0 : round256(static_cast<size_t>(d->n_out) * d->k * 2);
+  p.partials = p.k_splits > 1 ? round256(static_cast<size_t>(p.k_splits) * d->rows * d->n_out * 4) : 0;
+  return p;
+}
+
+int32_t current_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
+aihost_status encode_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t stride_bytes,
+                            uint32_t box_inner, uint32_t box_outer, const char* what) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned(base, 16) || stride_bytes % 16) return fail(AIHOST_EINVAL, "%s must be 16-byte aligned", what);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what, static_cast<int>(r));
+  return AIHOST_OK;
+}
+
+aihost_status encode_3d_f16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                            uint64_t s2, uint32_t b0, uint32_t b1, const char* what) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned(base, 16) || s1 % 16 || s2 % 16) return fail(AIHOST_EINVAL, "%s must be 16-byte aligned", what);
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what, static_cast<int>(r));
+  return AIHOST_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+aihost_status aihost_matmul_workspace_size(const aihost_matmul_desc* desc, size_t* out_bytes) {
+  if (!out_bytes) return fail(AIHOST_EINVAL, "out_bytes is NULL");
+  aihost_status s = check_matmul(desc);
+  if (s != AIHOST_OK) return s;
+  const GemmPlan p = plan_gemm(desc, current_sms());
+  *out_bytes = p.a_stage + p.w_stage + p.partials;
+  return AIHOST_OK;
+}
+
+aihost_status aihost_matmul_weights(aihost_attn_ctx* ctx, const aihost_matmul_desc* desc, const void* a,
+                                    const void* w, void* out, void* stream) {
+  aihost_status s = check_ctx(ctx);
+  if (s != AIHOST_OK) return s;
+  s = check_matmul(desc);
+  if (s != AIHOST_OK) return s;
+  if (!a || !w || !out) return fail(AIHOST_EINVAL, "a, w and out must be non-NULL");
+  if (!aligned(a, 16) || !aligned(w, 16) || !aligned(out, 16))
+    return fail(AIHOST_EINVAL, "a, w and out must be 16-byte aligned");
+  DeviceGuard g(ctx->device);
+  if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
+  const GemmPlan p = plan_gemm(desc, ctx->num_sms);
+  const size_t need = p.a_stage + p.w_stage + p.partials;
+  if (need > ctx->scratch_bytes)
+    return fail(AIHOST_ENOMEM, "this product needs %zu bytes of scratch, context has %zu (aihost_matmul_workspace_size)",
+                need, ctx->scratch_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* sp = static_cast<uint8_t*>(ctx->scratch);
+  const int64_t M = desc->rows, K = desc->k, N = desc->n_out, parts = desc->n_parts;
+  const void* a16 = a;
+  const void* w16 = w;
+  if (desc->a_dtype == AIHOST_F32) {
+    __half* dst = reinterpret_cast<__half*>(sp);
+    sp += p.a_stage;
+    cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_CONVERT, st, [&] {
+      return launch_f32_to_f16(static_cast<const float*>(a), dst, M * K, ctx->num_sms, st);
+    });
+    if (e != cudaSuccess) return cuda_fail(e, "A conversion launch");
+    a16 = dst;
+  }
+  if (desc->w_dtype != AIHOST_F16) {
+    __half* dst = reinterpret_cast<__half*>(sp);
+    sp += p.w_stage;
+    cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_CONVERT, st, [&] {
+      return desc->w_dtype == AIHOST_F32 ? launch_f32_to_f16(static_cast<const float*>(w), dst, N * K, ctx->num_sms, st)
+                                         : launch_dequant(w, desc->w_dtype, N * K, dst, AIHOST_F16, st);
+    });
+    if (e != cudaSuccess) return cuda_fail(e, "weight dequantisation launch");
+    w16 = dst;
+  }
+  GemmArgs ga;
+  memset(&ga, 0, sizeof(ga));
+  const int64_t part_cols = K / parts;
+  s = encode_3d_f16(&ga.a_map, a16, part_cols, M, parts, part_cols * 2, M * part_cols * 2, 64, 128, "a");
+  if (s != AIHOST_OK) return s;
+  s = encode_2d_f16(&ga.b_map, w16, K, N, K * 2, 64, p.block_n, "w");
+  if (s != AIHOST_OK) return s;
+  ga.M = desc->rows;
+  ga.N = desc->n_out;
+  ga.K = desc->k;
+  ga.part_cols = static_cast<int32_t>(part_cols);
+  ga.k_splits = p.k_splits;
+  ga.kt_per_split = p.kt_per_split;
+  ga.out = out;
+  ga.out_dtype = desc->out_dtype;
+  ga.ldc = N;
+  ga.partials = p.k_splits > 1 ? reinterpret_cast<float*>(sp) : nullptr;
+  ga.counters = ctx->counters;
+  ga.epoch = ctx->epoch++;
+  ga.status = ctx->d_status;
+  cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_MATMUL, st, [&] { return launch_gemm(ga, p.block_n, ctx->num_sms, st); });
+  if (e != cudaSuccess) return cuda_fail(e, "matmul launch");
+  return AIHOST_OK;
+}
+
+aihost_status aihost_dequantize(const void* w, int32_t w_dtype, int64_t n_elems, void* out, int32_t out_dtype,
+                                void* stream) {
+  if (!w || !out) return fail(AIHOST_EINVAL, "w and out must be non-NULL");
+  if (!is_kquant(w_dtype)) return fail(AIHOST_EINVAL, "w_dtype %d is not a K-quant type (Q2_K..Q6_K)", w_dtype);
+  if (out_dtype != AIHOST_F16 && out_dtype != AIHOST_F32) return fail(AIHOST_EINVAL, "out_dtype must be F16 or F32");
+  if (n_elems < 0 || n_elems % 256) return fail(AIHOST_EINVAL, "n_elems (%lld) must be a multiple of 256",
+                                                static_cast<long long>(n_elems));
+  if (!aligned(out, 16)) return fail(AIHOST_EINVAL, "out must be 16-byte aligned");
+  cudaError_t e = launch_dequant(w, w_dtype, n_elems, out, out_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dequantisation launch");
   return AIHOST_OK;
 }
 

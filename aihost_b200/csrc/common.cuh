@@ -86,6 +86,35 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 2-D and 3-D tiled loads (same rules: no multicast).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0, int32_t c1,
+                                            int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// AND of `v` over the 128 threads that use named barrier 1 (a barrier plus a vote: every one of
+// those threads gets the same answer, so they can leave a loop together).
+__device__ __forceinline__ bool bar1_and_128(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred p, 1, 128, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -241,6 +270,23 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Counts this split's arrival on an epoch-tagged counter (high 32 bits: the call's epoch, low:
+// arrivals); true for the last of n_splits arrivals of this call, which then resets the counter
+// to zero. A counter still holding another epoch (left by a call that did not finish) restarts
+// at 1. Never waits on another CTA; the CAS retries only on contention.
+__device__ __forceinline__ bool split_arrive(unsigned long long* c, uint32_t epoch, int n_splits, int32_t* status) {
+  unsigned long long cur = atomicAdd(c, 0ull);
+  for (uint32_t it = 0; it < kMaxWaitIters; ++it) {
+    const bool same = static_cast<uint32_t>(cur >> 32) == epoch;
+    const unsigned long long want = same ? cur + 1 : ((static_cast<unsigned long long>(epoch) << 32) | 1ull);
+    const unsigned long long seen = atomicCAS(c, cur, want);
+    if (seen == cur) return static_cast<uint32_t>(want) == static_cast<uint32_t>(n_splits);
+    cur = seen;
+  }
+  atomicOr(status, kStatusWaitTimeout);
+  return false;
+}
 
 // ------------------------------------------------------------------------------- numeric helpers
 __device__ __forceinline__ float ld_as_float(const float* p) { return *p; }

@@ -107,22 +107,6 @@ __device__ __forceinline__ void append_new_row(const DecodeArgs& p, int b, int k
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Counts this split's arrival on an epoch-tagged counter (high 32 bits: the call's epoch, low:
-// arrivals); true for the last of n_splits arrivals of this call, which then resets the counter
-// to zero. A counter still holding another epoch (left by a call that did not finish) restarts
-// at 1. Never waits on another CTA; the CAS retries only on contention.
-__device__ __forceinline__ bool split_arrive(unsigned long long* c, uint32_t epoch, int n_splits, int32_t* status) {
-  unsigned long long cur = atomicAdd(c, 0ull);
-  for (uint32_t it = 0; it < kMaxWaitIters; ++it) {
-    const bool same = static_cast<uint32_t>(cur >> 32) == epoch;
-    const unsigned long long want = same ? cur + 1 : ((static_cast<unsigned long long>(epoch) << 32) | 1ull);
-    const unsigned long long seen = atomicCAS(c, cur, want);
-    if (seen == cur) return static_cast<uint32_t>(want) == static_cast<uint32_t>(n_splits);
-    cur = seen;
-  }
-  atomicOr(status, kStatusWaitTimeout);
-  return false;
-}
 
 // Output of one split (compute warps, after each warp has put its per-head (max, sum) at
 // merge[(warp * 16 + head) * 2] and its unnormalised O row at o_s[(warp * 16 + head) * (D + 8)]):

@@ -183,4 +183,28 @@ bool prefill_supported(int32_t head_dim);
 bool prefill_split_kv(int32_t batch, int32_t n_new, int32_t n_q_heads, int32_t num_sms);
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st);
 
+// ---------------------------------------------------------------- matmul_sm100.cu
+// C[M, N] = A[M, K] . W[N, K]^T on the tensor cores (fp16 operands, fp32 accumulation).
+struct GemmArgs {
+  CUtensorMap a_map;   // fp16 A: dims {part_cols, M, n_parts}, box {64, 128, 1}, 128-byte swizzle
+  CUtensorMap b_map;   // fp16 W: dims {K, N}, box {64, BN}, 128-byte swizzle
+  int32_t M, N, K, part_cols;
+  int32_t k_splits, kt_per_split;  // K range split over CTAs (64-wide K tiles per split)
+  void* out;           // [M][ldc] in out_dtype
+  int32_t out_dtype;
+  int64_t ldc;
+  float* partials;     // [k_splits][M][N] fp32 scratch (k_splits > 1)
+  unsigned long long* counters;  // per output tile, epoch-tagged (k_splits > 1)
+  uint32_t epoch;
+  int32_t* status;
+};
+// Bytes of one 256-element GGUF block of a K-quant type (0 for other types).
+int32_t weight_block_bytes(int32_t wt);
+// GGUF K-quant blocks -> n_elems values (a multiple of 256) in out_dtype (F16 or F32).
+cudaError_t launch_dequant(const void* w, int32_t wt, int64_t n_elems, void* out, int32_t out_dtype, cudaStream_t st);
+cudaError_t launch_f32_to_f16(const float* x, __half* y, int64_t n, int32_t num_sms, cudaStream_t st);
+// Output-tile width the GEMM uses for this shape (256 when the tiles fill the SMs, else 64).
+int32_t gemm_block_n(int32_t M, int32_t N, int32_t num_sms);
+cudaError_t launch_gemm(const GemmArgs& a, int32_t block_n, int32_t num_sms, cudaStream_t st);
+
 }  // namespace aihost

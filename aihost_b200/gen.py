@@ -88,4 +88,22 @@ def q8_0_blocks(n_blocks: int, seed: int, stream: str, scale_lo: float = 0.001, 
     return out.reshape(-1)
 
 
-__all__ = ["uniform", "normal", "randint", "q8_0_blocks", "stream_key"]
+# GGUF K-quant block sizes (bytes per 256 values) and where each block keeps its fp16 super-scales
+KQUANT_BLOCK_BYTES = {8: 84, 9: 110, 10: 144, 11: 176, 12: 210}
+_KQUANT_F16 = {8: (80, 82), 9: (108,), 10: (0, 2), 11: (0, 2), 12: (208,)}
+
+
+def kquant_blocks(kind: int, n_blocks: int, seed: int, stream: str, scale_lo: float = 0.001, scale_hi: float = 0.01,
+                  device="cpu") -> torch.Tensor:
+    """GGUF K-quant weight blocks (kind = AIHost DataType ordinal, Q2_K 8 .. Q6_K 12) as uint8
+    [n_blocks * bytes]: every quant and sub-block scale byte uniform in [0, 255], the fp16
+    super-scales (d, and dmin where the format has one) uniform in [scale_lo, scale_hi]."""
+    nb = KQUANT_BLOCK_BYTES[kind]
+    out = randint((n_blocks, nb), 0, 255, seed, stream + ".bytes", device).to(torch.uint8)
+    for i, off in enumerate(_KQUANT_F16[kind]):
+        d = (scale_lo + uniform(n_blocks, seed, f"{stream}.d{i}", device) * (scale_hi - scale_lo)).to(torch.float16)
+        out[:, off:off + 2] = d.view(torch.uint8).reshape(n_blocks, 2)
+    return out.reshape(-1)
+
+
+__all__ = ["uniform", "normal", "randint", "q8_0_blocks", "kquant_blocks", "KQUANT_BLOCK_BYTES", "stream_key"]

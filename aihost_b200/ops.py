@@ -361,6 +361,52 @@ class ComputeOps:
         return out
 
 
+class MatMulDesc(ctypes.Structure):
+    """aihost_matmul_desc."""
+
+    _fields_ = [("rows", ctypes.c_int32), ("k", ctypes.c_int32), ("n_out", ctypes.c_int32), ("n_parts", ctypes.c_int32),
+                ("a_dtype", ctypes.c_int32), ("w_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32)]
+
+
+class WeightOps:
+    """The weight products beside the attention op, executed by libaihost_attn:
+
+      ComputeOps.MatMulWeights(a, w) (ComputeOps.cs:275-313)   -> mat_mul_weights
+      ComputeOps.Dequantize / DequantizeInto (ComputeOps.cs:733-861) -> dequantize
+
+    Weights are GGUF tensors as stored (column-major: n_out rows of k values; K-quant blocks
+    as raw bytes in a uint8 tensor)."""
+
+    def __init__(self, ctx: Context, stream=None):
+        self.ctx, self.stream = ctx, stream
+
+    def mat_mul_weights(self, a: torch.Tensor, w: torch.Tensor, w_dtype: int, n_out: int, n_parts: int = 1,
+                        out_dtype: torch.dtype = torch.float16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """C [rows, n_out] = A . W. `a` is [rows, k] (n_parts = 1) or n_parts column blocks
+        stored one after another, [n_parts, rows, k / n_parts] (e.g. the rank-major output of
+        a KV-head-sharded attention call viewed as [N, B*S, Hq/N*d])."""
+        if n_parts == 1:
+            rows, k = a.shape[-2], a.shape[-1]
+        else:
+            rows, k = a.shape[1], a.shape[0] * a.shape[2]
+        d = MatMulDesc(rows, k, n_out, n_parts, dtype_code(a), w_dtype, _TORCH_CODES[out_dtype])
+        need = ctypes.c_size_t()
+        check(lib().aihost_matmul_workspace_size(ctypes.byref(d), ctypes.byref(need)))
+        if need.value:
+            check(lib().aihost_attn_reserve(self.ctx.handle, need.value))
+        if out is None:
+            out = torch.empty(rows, n_out, dtype=out_dtype, device=a.device)
+        check(lib().aihost_matmul_weights(self.ctx.handle, ctypes.byref(d), _ptr(a), _ptr(w), _ptr(out),
+                                          _stream(self.stream)))
+        return out
+
+    def dequantize(self, w: torch.Tensor, w_dtype: int, n: int, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """K-quant blocks -> n values (DequantizeInto writes fp32; fp16 is that value rounded once)."""
+        out = torch.empty(n, dtype=out_dtype, device=w.device)
+        check(lib().aihost_dequantize(_ptr(w), w_dtype, n, _ptr(out), _TORCH_CODES[out_dtype], _stream(self.stream)))
+        return out
+
+
 def default_scale(head_dim: int) -> float:
     """1.0f / MathF.Sqrt(headDim) in fp32 (ComputeOps.cs:1065)."""
     import numpy as np
@@ -368,4 +414,5 @@ def default_scale(head_dim: int) -> float:
     return float(np.float32(1.0) / np.sqrt(np.float32(head_dim)))
 
 
-__all__ = ["Context", "LayerSpec", "KVCache", "ComputeOps", "dtype_code", "row_bytes", "default_scale", "math"]
+__all__ = ["Context", "LayerSpec", "KVCache", "ComputeOps", "WeightOps", "MatMulDesc", "dtype_code", "row_bytes",
+           "default_scale", "math"]

@@ -63,6 +63,9 @@ def parse_args():
                     help="qk-norm-rope: time the Qwen TypeB Q/K prologue kernel alone (one GPU; GB/s of HBM)")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N untimed fused calls of --config and exit (the command profiled with ncu)")
+    ap.add_argument("--profile-new", type=int, default=0,
+                    help="with --profile-steps: override the config's new rows per sequence (a smaller prefill "
+                         "of the same shape, for captures that must stay small)")
     return ap.parse_args()
 
 
@@ -163,8 +166,9 @@ def cpu_sample_run(cfg, target_s: float):
     from oracle import oracle as orc
 
     S = cfg.n_new
-    if S > 1:  # prefill: whole sequence, a subset of query heads
-        sub = cfg.scaled(batch=1)
+    if S > 1:  # prefill: whole sequence, a subset of the query heads of one KV head
+        G = cfg.n_q_heads // cfg.n_kv_heads
+        sub = cfg.scaled(batch=1, n_q_heads=G, n_kv_heads=1)
         inp = make_inputs(sub)
         lengths = inp["lengths"]
         w = work(sub, lengths)
@@ -176,13 +180,13 @@ def cpu_sample_run(cfg, target_s: float):
                              inp["seq_len"].numpy(), mode=orc.FAITHFUL, part=(0, 1, 0, nh))
             return time.perf_counter() - t
         t1 = run(1)
-        nh = int(max(1, min(cfg.n_q_heads, round(target_s / max(t1, 1e-3)))))
+        nh = int(max(1, min(G, round(target_s / max(t1, 1e-3)))))
         t = run(nh) if nh > 1 else t1
         t, reps = _repeat_to(lambda: run(nh), t, target_s)
-        units = w["flops"] * nh / cfg.n_q_heads * reps
-        return dict(units=units, seconds=t, reps=reps, unit="TFLOP/s", scale=1e-12, cores=orc.num_threads(),
-                    sample=f"1 sequence x {nh}/{cfg.n_q_heads} query heads, S={S}, {reps} run(s) "
-                           f"(faithful fp32 oracle)")
+        units = w["flops"] * nh / G * reps
+        return dict(units=units, seconds=t, reps=reps, unit="TFLOP/s", scale=1e-12, cores=orc.num_threads(), nh=nh,
+                    sample=f"1 sequence x {nh} query head(s) of one KV head (of {cfg.n_q_heads}), S={S}, {reps} "
+                           f"run(s) (faithful fp32 oracle)")
     # decode: a subset of sequences, all heads
     lengths_all = cfg.lengths()
     nb = 1
@@ -200,7 +204,7 @@ def cpu_sample_run(cfg, target_s: float):
     if nb > 1:
         t1, sub = run(nb)
     t1, reps = _repeat_to(lambda: run(nb)[0], t1, target_s)
-    return dict(units=float(nb * reps), seconds=t1, reps=reps, unit="tokens/s", scale=1.0, cores=orc.num_threads(),
+    return dict(units=float(nb * reps), seconds=t1, reps=reps, unit="tokens/s", scale=1.0, cores=orc.num_threads(), nb=nb,
                 sample=f"{nb}/{cfg.batch} sequences, all {cfg.n_q_heads} query heads, {reps} run(s) "
                        f"(faithful fp32 oracle)")
 
@@ -724,12 +728,12 @@ def _rerun(cfg, meta):
     key = cfg.number
     if key not in _RERUN_CACHE:
         if cfg.n_new > 1:
-            nh = int(meta["sample"].split(" x ")[1].split("/")[0])
-            sub = cfg.scaled(batch=1)
+            nh = meta["nh"]
+            sub = cfg.scaled(batch=1, n_q_heads=cfg.n_q_heads // cfg.n_kv_heads, n_kv_heads=1)
             inp = make_inputs(sub)
             _RERUN_CACHE[key] = (sub, inp, (0, 1, 0, nh))
         else:
-            nb = int(meta["sample"].split("/")[0])
+            nb = meta["nb"]
             ls = cfg.lengths()[:nb]
             sub = cfg.scaled(batch=nb, cached_range=None, cached=None, cached_list=ls)
             inp = make_inputs(sub, capacity=max(ls) + 1)
@@ -818,6 +822,7 @@ def config_object(cfg, shard_mode, args, device, ctx, dist_on, ws, rank, pk, pk_
     """One config's measurements as a JSON object: the device-timed value, the dominant kernel's
     roofline, the end-to-end value through the C ABI with host buffers, and (rank 0, N = 1) the
     CPU baseline and, for decode configs with `layers`, the rotating-cache throughput."""
+    t_start = time.perf_counter()
     steps = args.steps if cfg.n_new > 1 else max(args.steps, 10)
     r = bench_ours(cfg, steps, args.warmup, device, ctx, 512 << 20, dist_on, shard_mode=shard_mode,
                    paged=args.paged)
@@ -837,8 +842,12 @@ def config_object(cfg, shard_mode, args, device, ctx, dist_on, ws, rank, pk, pk_
                          "note": "one CUDA graph of `layers` fused calls on distinct caches (together larger than "
                                  "L2, so the bytes come from HBM), replayed per step; bytes = algorithmic bytes of "
                                  "every layer's call"}
+    t_gpu = time.perf_counter()
     if rank == 0 and ws == 1 and cpu_s > 0:
         res["cpu_baseline"] = cpu_baseline(cfg, cpu_s)
+    if rank == 0:
+        print(f"[bench] config {cfg.number} ({shard_mode}): gpu legs {t_gpu - t_start:.1f} s, cpu baseline "
+              f"{time.perf_counter() - t_gpu:.1f} s", file=sys.stderr, flush=True)
     return res
 
 
@@ -863,7 +872,10 @@ def main():
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if args.profile_steps:
-        profile_steps(CONFIGS[args.config], args.profile_steps, device)
+        pcfg = CONFIGS[args.config]
+        if args.profile_new:
+            pcfg = pcfg.scaled(n_new=args.profile_new)
+        profile_steps(pcfg, args.profile_steps, device)
         return
     pk, pk_kind = peaks()
     if args.op == "qk-norm-rope":

@@ -56,8 +56,13 @@ typedef enum {
 } aihost_status;
 
 /* Element types; the numeric values are AIHost's DataType ordinals
- * (ICompute/IComputeBuffer.cs:57-76: F32=0, F16=1, Q8_0=6). */
-typedef enum { AIHOST_F32 = 0, AIHOST_F16 = 1, AIHOST_Q8_0 = 6 } aihost_dtype;
+ * (ICompute/IComputeBuffer.cs:57-76: F32=0, F16=1, Q8_0=6, Q2_K=8 ... Q6_K=12). The K-quant
+ * types are GGUF weight blocks of 256 values (QuantizationFormats.cs header: Q2_K 84 bytes,
+ * Q3_K 110, Q4_K 144, Q5_K 176, Q6_K 210) and are accepted as weights only. */
+typedef enum {
+  AIHOST_F32 = 0, AIHOST_F16 = 1, AIHOST_Q8_0 = 6,
+  AIHOST_Q2_K = 8, AIHOST_Q3_K = 9, AIHOST_Q4_K = 10, AIHOST_Q5_K = 11, AIHOST_Q6_K = 12
+} aihost_dtype;
 
 /* RoPE pairing. INTERLEAVED is the reference's (x[2i], x[2i+1]) pairing used by every
  * architecture in AIHost (Compute/ComputeShaders.cs:517-543). NEOX pairs (x[i], x[i+d/2]).
@@ -172,8 +177,9 @@ typedef enum {
   AIHOST_KERNEL_DECODE = 1,   /* split-K decode */
   AIHOST_KERNEL_COMBINE = 2,  /* split merge */
   AIHOST_KERNEL_PREFILL = 3,  /* tcgen05 prefill */
-  AIHOST_KERNEL_CONVERT = 4,  /* fp16 staging of fp32 / Q8_0 prefill operands */
-  AIHOST_KERNEL_COUNT = 5
+  AIHOST_KERNEL_CONVERT = 4,  /* fp16 staging of fp32 / Q8_0 prefill operands, weight dequantisation */
+  AIHOST_KERNEL_MATMUL = 5,   /* tcgen05 weight product (aihost_matmul_weights) */
+  AIHOST_KERNEL_COUNT = 6
 } aihost_kernel;
 aihost_status aihost_attn_profiler_enable(aihost_attn_ctx* ctx, int32_t enable);
 aihost_status aihost_attn_profiler_read(aihost_attn_ctx* ctx, int32_t kernel, int64_t* launches, double* total_ms);
@@ -265,6 +271,36 @@ aihost_status aihost_attn_decode_partial(aihost_attn_ctx* ctx, const aihost_attn
 aihost_status aihost_attn_merge_partials(aihost_attn_ctx* ctx, int32_t n_parts, int32_t rows, int32_t head_dim,
                                          int32_t dtype, const void* o_parts, const float* lse_parts, void* out,
                                          float* lse_out, void* stream);
+
+/* ---- The weight products around the op: C[rows, n_out] = A[rows, k] . W, with W a GGUF weight
+ * ("column-major" in GGUF terms: element (k, n) at n * k_total + k, i.e. n_out rows of k values,
+ * K-quant blocks running along k). Replaces ComputeOps.MatMulWeights (ComputeOps.cs:275-313) at
+ * its calls beside attention: the Q/K/V projections that feed the op (ComputeOps.cs:1274-1276,
+ * weights dequantised per call by TransformerBase.TempF32 / ComputeOps.DequantizeInto,
+ * ComputeOps.cs:761-861) and the output projection right after it (ComputeOps.cs:1317).
+ * A is given as n_parts column blocks stored one after another, [n_parts][rows][k / n_parts]
+ * (n_parts = 1: plain row-major [rows][k]); with n_parts = N this is the rank-major
+ * [N][batch][n_new][Hq/N][head_dim] buffer aihost_attn_forward_sharded gathers, read in place.
+ * fp16 operands on the tensor cores (fp32 A is rounded to fp16 first; K-quant weights are
+ * dequantised with the reference shaders' formulas, then rounded once to fp16), fp32
+ * accumulation. Needs aihost_matmul_workspace_size bytes of the context's scratch. */
+typedef struct {
+  int32_t rows;       /* M: rows of A and of the output */
+  int32_t k;          /* K: a multiple of 64 (of 256 for K-quant weights); k / n_parts a multiple of 64 */
+  int32_t n_out;      /* N: output columns, a multiple of 8 */
+  int32_t n_parts;    /* column blocks of A (>= 1) */
+  int32_t a_dtype;    /* F16 or F32 */
+  int32_t w_dtype;    /* F16, F32, Q2_K, Q3_K, Q4_K, Q5_K or Q6_K */
+  int32_t out_dtype;  /* F16 or F32 */
+} aihost_matmul_desc;
+aihost_status aihost_matmul_workspace_size(const aihost_matmul_desc* desc, size_t* out_bytes);
+aihost_status aihost_matmul_weights(aihost_attn_ctx* ctx, const aihost_matmul_desc* desc, const void* a,
+                                    const void* w, void* out, void* stream);
+/* ComputeOps.DequantizeInto (ComputeOps.cs:761-861) with the reference's own formulas
+ * (QuantizationFormats.cs): n_elems (a multiple of 256) values of a K-quant tensor into out, F32
+ * (the reference's target type; equal to its shader's result) or F16 (that value rounded once). */
+aihost_status aihost_dequantize(const void* w, int32_t w_dtype, int64_t n_elems, void* out, int32_t out_dtype,
+                                void* stream);
 
 /* Synchronise the context's device and read-and-clear the device status word that kernels
  * set when a bounded wait expired (AIHOST_ETIMEOUT) or a device-side length exceeded

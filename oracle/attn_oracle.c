@@ -169,6 +169,18 @@ void oracle_rope_full(float* x, int32_t seq, int32_t n_heads, int32_t head_dim, 
       rope_row(x + ((int64_t)s * n_heads + h) * head_dim, head_dim, start_pos + s, theta, rope_mode);
 }
 
+/* RoPE of rows [s0, s1) and heads [h0, h1) of x [seq, n_heads * head_dim] (rows rotated at
+ * start_pos + s): the same per-element operations as oracle_rope_full, restricted to the part a
+ * sampled call attends or appends. */
+static void rope_part(float* x, int32_t n_heads, int32_t head_dim, int32_t start_pos, float theta, int32_t rope_mode,
+                      int32_t s0, int32_t s1, int32_t h0, int32_t h1) {
+  if (rope_mode == AIHOST_ROPE_NONE) return;
+#pragma omp parallel for schedule(static)
+  for (int32_t s = s0; s < s1; ++s)
+    for (int32_t h = h0; h < h1; ++h)
+      rope_row(x + ((int64_t)s * n_heads + h) * head_dim, head_dim, start_pos + s, theta, rope_mode);
+}
+
 /* ---------------------------------------------------------------- attention row */
 
 /* K/V row access: fp32 rows, fp16 rows or Q8_0 rows, dequantised into dst[head_dim]. */
@@ -344,8 +356,9 @@ int32_t oracle_attn_forward_rows(const aihost_attn_desc* desc, int32_t batch, in
     to_f32((const uint8_t*)q + (int64_t)b * qe * in_es, desc->q_dtype, qe, qb);
     to_f32((const uint8_t*)k_new + (int64_t)b * ke * in_es, desc->q_dtype, ke, kf);
     to_f32((const uint8_t*)v_new + (int64_t)b * ke * in_es, desc->q_dtype, ke, vf);
-    oracle_rope_full(qb, n_new, Hq, D, P, desc->rope_theta, desc->rope_mode);
-    oracle_rope_full(kf, n_new, Hkv, D, P, desc->rope_theta, desc->rope_mode);
+    /* only the query rows and heads this call attends, and the KV heads it appends */
+    rope_part(qb, Hq, D, P, desc->rope_theta, desc->rope_mode, r0, r1, h0, h1);
+    rope_part(kf, Hkv, D, P, desc->rope_theta, desc->rope_mode, 0, n_new, kvh0, kvh1);
     for (int32_t s = 0; s < n_new; ++s)
       for (int32_t h = kvh0; h < kvh1; ++h) {
         const int64_t off = (int64_t)b * seq_stride + (int64_t)(P + s) * tok_stride + (int64_t)h * head_stride;
@@ -407,4 +420,125 @@ int32_t oracle_attn_forward(const aihost_attn_desc* desc, int32_t batch, int32_t
   if (!desc) return 1;
   return oracle_attn_forward_part(desc, batch, n_new, q, k_new, v_new, k_cache, v_cache, seq_len, out,
                                   mode, 0, batch, 0, desc->n_q_heads);
+}
+
+/* ------------------------------------------------------------------ weights beside the op
+ * GGUF K-quant dequantisation, restated from the reference's shaders (the inline sources the
+ * reference runs: QuantizationFormats.cs DequantizeQ2K_Correct .. DequantizeQ6K_Correct, chosen
+ * by ComputeShaders.cs:12-16 since no dequant .glsl is deployed). Each value is evaluated in the
+ * shader's order, one fp32 rounding per operation (this file is built without contraction). */
+static float kq_f16(const uint8_t* p) { return oracle_f16_to_f32((uint16_t)(p[0] | (p[1] << 8))); }
+
+static void kq_scale_min_k4(int j, const uint8_t* q, float* sc, float* mn) { /* get_scale_min_k4 */
+  if (j < 4) {
+    *sc = (float)(q[j] & 63);
+    *mn = (float)(q[j + 4] & 63);
+  } else {
+    *sc = (float)((q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4));
+    *mn = (float)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+  }
+}
+
+static float kq_value(int32_t kind, const uint8_t* b, int e) {
+  switch (kind) {
+    case 8: { /* Q2_K: scales[16] | qs[64] | d | dmin — QuantizationFormats.cs:20-56 */
+      const uint8_t sc = b[e / 16];
+      const int chunk = e / 128, local = e % 128;
+      const int qv = (b[16 + chunk * 32 + local % 32] >> ((local / 32) * 2)) & 3;
+      const float d = kq_f16(b + 80), dmin = kq_f16(b + 82);
+      const float t = d * (float)(sc & 0xF);
+      return t * (float)qv - dmin * (float)((sc >> 4) & 0xF);
+    }
+    case 9: { /* Q3_K: hmask[32] | qs[64] | scales[12] | d — QuantizationFormats.cs:65-128 */
+      const int chunk = e / 128, local = e % 128;
+      const int low2 = (b[32 + chunk * 32 + local % 32] >> ((local / 32) * 2)) & 3;
+      const int high1 = (b[local % 32] >> (chunk * 4 + local / 32)) & 1;
+      const int qval = (low2 | (high1 << 2)) - 4;
+      const int is = e / 16, k = is % 4, ag = is / 4;
+      const uint8_t* sc = b + 96;
+      const int tmp = sc[8 + k];
+      int sb;
+      if (ag == 0) sb = (sc[k] & 0xF) | (((tmp >> 0) & 3) << 4);
+      else if (ag == 1) sb = (sc[k + 4] & 0xF) | (((tmp >> 2) & 3) << 4);
+      else if (ag == 2) sb = ((sc[k] >> 4) & 0xF) | (((tmp >> 4) & 3) << 4);
+      else sb = ((sc[k + 4] >> 4) & 0xF) | (((tmp >> 6) & 3) << 4);
+      const float dl = kq_f16(b + 108) * (float)(sb - 32);
+      return dl * (float)qval;
+    }
+    case 10: { /* Q4_K: d | dmin | scales[12] | qs[128] — QuantizationFormats.cs:140-197 */
+      const int group = e / 64, within = e % 64, upper = within >= 32;
+      float sc, mn;
+      kq_scale_min_k4(group * 2 + upper, b + 4, &sc, &mn);
+      const int q = (b[16 + group * 32 + within % 32] >> (upper * 4)) & 0xF;
+      const float t = kq_f16(b) * sc;
+      return t * (float)q - kq_f16(b + 2) * mn;
+    }
+    case 11: { /* Q5_K: d | dmin | scales[12] | qh[32] | qs[128] — QuantizationFormats.cs:204-257 */
+      float sc, mn;
+      kq_scale_min_k4(e / 32, b + 4, &sc, &mn);
+      const int j = e / 64, local = e % 64, upper = local >= 32, l = local % 32;
+      const int ql = (b[48 + j * 32 + l] >> (upper * 4)) & 0xF;
+      const int qh = (b[16 + j * 32 + l] >> (j * 2 + upper)) & 1;
+      const float t = kq_f16(b) * sc;
+      return t * (float)(ql | (qh << 4)) - kq_f16(b + 2) * mn;
+    }
+    case 12: { /* Q6_K: ql[128] | qh[64] | scales[16] | d — QuantizationFormats.cs:264-315 */
+      const int half = e / 128, w = e % 128, quarter = w / 32, wq = w % 32;
+      const int ql_extra = (quarter == 1 || quarter == 3) ? 32 : 0;
+      const int upper = quarter >= 2;
+      const int lower4 = (b[half * 64 + ql_extra + wq] >> (upper * 4)) & 0xF;
+      const int upper2 = (b[128 + half * 32 + wq] >> (quarter * 2)) & 3;
+      const int q = lower4 | (upper2 << 4);
+      const float sc = (float)(int8_t)b[192 + e / 16];
+      const float t = kq_f16(b + 208) * sc;
+      return t * ((float)q - 32.0f);
+    }
+    default:
+      return 0.0f;
+  }
+}
+
+int32_t oracle_kquant_block_bytes(int32_t kind) {
+  switch (kind) {
+    case 8: return 84;
+    case 9: return 110;
+    case 10: return 144;
+    case 11: return 176;
+    case 12: return 210;
+    default: return 0;
+  }
+}
+
+int32_t oracle_dequantize(int32_t kind, const uint8_t* blocks, int64_t n, float* out) {
+  const int32_t bb = oracle_kquant_block_bytes(kind);
+  if (!bb || !blocks || !out || n < 0 || n % 256) return 1;
+  f16_lut_init();
+#pragma omp parallel for schedule(static)
+  for (int64_t blk = 0; blk < n / 256; ++blk)
+    for (int e = 0; e < 256; ++e) out[blk * 256 + e] = kq_value(kind, blocks + blk * bb, e);
+  return 0;
+}
+
+/* ComputeOps.MatMulWeights (ComputeOps.cs:275-313; shader _inlineMatMulWeights in
+ * ComputeShaders.cs): C [M, N] = A [M, K] . B, B GGUF column-major, element (k, n) at
+ * w[n * K + k]. FAITHFUL: one fp32 accumulator per output, k ascending, as the shader's 16-wide
+ * tiles visit them; EXACT: double accumulation. */
+int32_t oracle_matmul_weights(const float* a, int32_t M, int32_t K, const float* w, int32_t N, float* c, int32_t mode) {
+  if (!a || !w || !c || M < 1 || K < 1 || N < 1) return 1;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int32_t m = 0; m < M; ++m)
+    for (int32_t n = 0; n < N; ++n) {
+      const float* ar = a + (int64_t)m * K;
+      const float* wr = w + (int64_t)n * K;
+      if (mode == ORACLE_EXACT) {
+        double acc = 0.0;
+        for (int32_t k = 0; k < K; ++k) acc += (double)ar[k] * (double)wr[k];
+        c[(int64_t)m * N + n] = (float)acc;
+      } else {
+        float acc = 0.0f;
+        for (int32_t k = 0; k < K; ++k) acc += ar[k] * wr[k];
+        c[(int64_t)m * N + n] = acc;
+      }
+    }
+  return 0;
 }

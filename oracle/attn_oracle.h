@@ -92,6 +92,15 @@ int32_t oracle_attn_forward_rows(const aihost_attn_desc* desc, int32_t batch, in
                                  int32_t mode, int32_t b0, int32_t b1, int32_t h0, int32_t h1,
                                  int32_t r0, int32_t r1);
 
+/* GGUF K-quant weights (kind = AIHost DataType ordinal: Q2_K 8, Q3_K 9, Q4_K 10, Q5_K 11, Q6_K 12):
+ * bytes per 256-value block, and n values (a multiple of 256) dequantised to fp32 with the
+ * reference shaders' formulas (QuantizationFormats.cs). */
+int32_t oracle_kquant_block_bytes(int32_t kind);
+int32_t oracle_dequantize(int32_t kind, const uint8_t* blocks, int64_t n, float* out);
+/* ComputeOps.MatMulWeights: C [M, N] = A [M, K] . W with W given as w[n * K + k] (GGUF
+ * column-major); mode ORACLE_FAITHFUL (fp32, k ascending) or ORACLE_EXACT (double). */
+int32_t oracle_matmul_weights(const float* a, int32_t M, int32_t K, const float* w, int32_t N, float* c, int32_t mode);
+
 #ifdef __cplusplus
 }
 #endif

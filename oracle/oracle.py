@@ -51,6 +51,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_attn_forward_rows.argtypes = [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32,
                                                i32]
         L.oracle_attn_forward_rows.restype = i32
+        L.oracle_kquant_block_bytes.argtypes, L.oracle_kquant_block_bytes.restype = [i32], i32
+        L.oracle_dequantize.argtypes, L.oracle_dequantize.restype = [i32, vp, i64, vp], i32
+        L.oracle_matmul_weights.argtypes, L.oracle_matmul_weights.restype = [vp, i32, i32, vp, i32, vp, i32], i32
         _LIB = L
     return _LIB
 
@@ -153,3 +156,22 @@ def attn_forward(desc, q: np.ndarray, k_new: np.ndarray, v_new: np.ndarray, k_ca
     if rc:
         raise RuntimeError(f"oracle_attn_forward failed ({rc})")
     return out
+
+
+def dequantize(kind: int, blocks: np.ndarray, n: int) -> np.ndarray:
+    """n values of GGUF K-quant blocks (bytes) -> fp32, the reference shaders' formulas."""
+    blk = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty(n, dtype=np.float32)
+    if lib().oracle_dequantize(kind, _p(blk), n, _p(out)):
+        raise ValueError(f"oracle_dequantize: bad kind {kind} or n {n}")
+    return out
+
+
+def matmul_weights(a: np.ndarray, w_nk: np.ndarray, mode: int = EXACT) -> np.ndarray:
+    """ComputeOps.MatMulWeights: a [M, K] times the GGUF column-major weight given as w_nk [N, K]."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    w = np.ascontiguousarray(w_nk, dtype=np.float32)
+    c = np.empty((a.shape[0], w.shape[0]), dtype=np.float32)
+    if lib().oracle_matmul_weights(_p(a), a.shape[0], a.shape[1], _p(w), w.shape[0], _p(c), mode):
+        raise ValueError("oracle_matmul_weights: bad shape")
+    return c

@@ -33,7 +33,7 @@ def default_reference() -> Path:
     env = os.environ.get("AIHOST_REFERENCE_DIR")
     return Path(env) if env else HERE.parent.parent.parent / "reference"
 
-# ComputeShaders field name -> (shader name used by TryLoadOrInline, inline constant)
+# shader name used by TryLoadOrInline -> inline constant in ComputeShaders.cs (private const)
 SHADERS = {
     "rope_full": "_inlineRoPEFull",
     "concat_axis0": "_inlineConcatAxis0",
@@ -46,7 +46,20 @@ SHADERS = {
     "slice_cols": "_inlineSliceCols",
     "scatter_cols": "_inlineScatterCols",
     "layernorm": "_inlineLayerNorm",
+    "matmul_weights": "_inlineMatMulWeights",
 }
+# the K-quant dequantisation shaders: inline constants in QuantizationFormats.cs (public const),
+# ComputeShaders.cs:12-16
+QUANT_SHADERS = {f"dequant_q{k}k": f"DequantizeQ{k}K_Correct" for k in (2, 3, 4, 5, 6)}
+
+
+def deployed_shaders(ref: Path) -> set[str]:
+    """Vulkan shader files the reference copies next to its assembly (csproj Content items);
+    ShaderLoader.Load (ShaderLoader.cs:11-48) finds only these, everything else falls back to
+    the inline source (ComputeShaders.TryLoadOrInline, ComputeShaders.cs:73-85)."""
+    proj = (ref / "AIHost/AIHost.csproj").read_text()
+    return set(re.findall(r'Content Include="Shaders\\Vulkan\\(\w+)\.glsl"', proj))
+
 
 BLOCK_RE = re.compile(
     r"layout\s*\(([^)]*)\)\s*((?:(?:readonly|writeonly|coherent|restrict|volatile)\s+)*)buffer\s+(\w+)\s*"
@@ -57,16 +70,18 @@ LOCAL_RE = re.compile(r"layout\s*\(\s*local_size_x\s*=\s*(\d+)(?:\s*,\s*local_si
 
 def load_sources(ref: Path) -> dict[str, str]:
     cs = (ref / "AIHost/AIHost/Compute/ComputeShaders.cs").read_text()
+    qf = (ref / "AIHost/AIHost/Compute/QuantizationFormats.cs").read_text()
+    deployed = deployed_shaders(ref)
     out = {}
-    for name, const in SHADERS.items():
-        deployed = ref / "AIHost/Shaders/Vulkan" / f"{name}.glsl"
-        if deployed.exists():
-            out[name] = deployed.read_text()
-            continue
-        m = re.search(r"private const string " + re.escape(const) + r'\s*=\s*@"(.*?)";', cs, re.S)
-        if not m:
-            raise SystemExit(f"shader constant {const} not found in ComputeShaders.cs")
-        out[name] = m.group(1).replace('""', '"')
+    for table, text, kind in ((SHADERS, cs, "private"), (QUANT_SHADERS, qf, "public")):
+        for name, const in table.items():
+            if name in deployed:
+                out[name] = (ref / "AIHost/AIHost/Shaders/Vulkan" / f"{name}.glsl").read_text()
+                continue
+            m = re.search(kind + r" const string " + re.escape(const) + r'\s*=\s*@"(.*?)";', text, re.S)
+            if not m:
+                raise SystemExit(f"shader constant {const} not found")
+            out[name] = m.group(1).replace('""', '"')
     return out
 
 
@@ -114,6 +129,11 @@ def translate(name: str, src: str) -> str:
 
     body = BLOCK_RE.sub(block, body)
     body = re.sub(r"\bshared\s+", "static ", body)
+    # GLSL `out` parameters become references
+    body = re.sub(r"\bout\s+(float|uint|int)\s+(\w+)", r"\1& \2", body)
+    if name.startswith("dequant_"):
+        # GLSL float literals are single precision (here: 0.0, 32.0)
+        body = re.sub(r"(?<![\w.])(\d+\.\d*(?:[eE][-+]?\d+)?)(?![\w.])", r"\1f", body)
     body = re.sub(r"\bvoid\s+main\s*\(\s*\)", "void main_()", body)
     uses_barrier = "barrier()" in body
     return (

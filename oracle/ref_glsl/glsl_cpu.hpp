@@ -1,5 +1,6 @@
 // glsl_cpu.hpp — just enough GLSL (450, compute) semantics to compile AIHost's attention
-// shaders as C++ and run them on the CPU. TEST INFRASTRUCTURE ONLY (oracle pinning).
+// shaders (and the weight dequantisation / MatMulWeights shaders beside them) as C++ and run
+// them on the CPU. TEST INFRASTRUCTURE ONLY (oracle pinning).
 //
 // Each shader becomes its own namespace. Invocations of one workgroup run as threads when the
 // shader calls barrier(), or one after another when it does not; workgroups run one at a
@@ -38,6 +39,12 @@ inline float pow(float x, float y) { return powf(x, y); }
 inline float cos(float x) { return cosf(x); }
 inline float sin(float x) { return sinf(x); }
 inline float sqrt(float x) { return sqrtf(x); }
+// bit reinterpretation (used by the dequantisation shaders' f16tof32)
+inline float uintBitsToFloat(uint u) {
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
 
 // Runs `main_fn` for every invocation of a gx*gy*gz dispatch of workgroups of size `local`.
 void dispatch(void (*main_fn)(), uvec3 local, uvec3 groups, bool uses_barrier);

@@ -28,6 +28,12 @@ AIHOST_SHADER(rowwise_softmax)
 AIHOST_SHADER(slice_cols)
 AIHOST_SHADER(scatter_cols)
 AIHOST_SHADER(layernorm)
+AIHOST_SHADER(matmul_weights)
+AIHOST_SHADER(dequant_q2k)
+AIHOST_SHADER(dequant_q3k)
+AIHOST_SHADER(dequant_q4k)
+AIHOST_SHADER(dequant_q5k)
+AIHOST_SHADER(dequant_q6k)
 #undef AIHOST_SHADER
 
 namespace {
@@ -231,6 +237,42 @@ int ref_layer_attention(const float* q, const float* k_new, const float* v_new, 
   std::memcpy(out, o.data(), o.size() * 4);
   std::memcpy(k_all, Kc.data(), Kc.size() * 4);
   std::memcpy(v_all, Vc.data(), Vc.size() * 4);
+  return 0;
+}
+
+// ComputeOps.Dequantize (ComputeOps.cs:733-745 -> DequantizeQ2K..DequantizeQ6K): one dispatch of
+// ceil(n / 256) workgroups, element offset 0 (DequantizeInto's chunked dispatches differ only in
+// that offset, and every invocation is independent). kind = AIHost DataType ordinal (Q2_K = 8 ..
+// Q6_K = 12); blocks hold n / 256 GGUF blocks.
+int ref_dequantize(int kind, const void* blocks, int n, float* out) {
+  uint32_t zero = 0;
+  void (*bind)(int, void*) = nullptr;
+  void (*run)(glsl::uint, glsl::uint, glsl::uint) = nullptr;
+  switch (kind) {
+    case 8: bind = sh_dequant_q2k::bind; run = sh_dequant_q2k::run; break;
+    case 9: bind = sh_dequant_q3k::bind; run = sh_dequant_q3k::run; break;
+    case 10: bind = sh_dequant_q4k::bind; run = sh_dequant_q4k::run; break;
+    case 11: bind = sh_dequant_q5k::bind; run = sh_dequant_q5k::run; break;
+    case 12: bind = sh_dequant_q6k::bind; run = sh_dequant_q6k::run; break;
+    default: return 1;
+  }
+  bind(0, const_cast<void*>(blocks));
+  bind(1, out);
+  bind(2, &zero);
+  run((uint32_t(n) + 255u) / 256u, 1, 1);
+  return 0;
+}
+
+// ComputeOps.MatMulWeights (ComputeOps.cs:275-313): C [M, N] = A [M, K] . B with B a GGUF
+// column-major weight (element (k, n) at n * K + k); params {M, K, N}; workgroups of 16 x 16
+// over {ceil(N / 16), ceil(M / 16)}.
+int ref_matmul_weights(const float* a, int M, int K, const float* b, int N, float* c) {
+  uint32_t p[3] = {uint32_t(M), uint32_t(K), uint32_t(N)};
+  sh_matmul_weights::bind(0, const_cast<float*>(a));
+  sh_matmul_weights::bind(1, const_cast<float*>(b));
+  sh_matmul_weights::bind(2, c);
+  sh_matmul_weights::bind(3, p);
+  sh_matmul_weights::run((uint32_t(N) + 15u) / 16u, (uint32_t(M) + 15u) / 16u, 1);
   return 0;
 }
 

@@ -28,6 +28,8 @@ def lib():
         L.ref_qk_norm_rope.argtypes = [vp, i32, i32, i32, vp, f32, i32, f32]
         L.ref_mha.argtypes = [vp, i32, vp, vp, i32, i32, i32, i32, i32, vp]
         L.ref_layer_attention.argtypes = [vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, f32, vp, vp, vp]
+        L.ref_dequantize.argtypes = [i32, vp, i32, vp]
+        L.ref_matmul_weights.argtypes = [vp, i32, i32, vp, i32, vp]
         _LIB = L
     return _LIB
 
@@ -72,3 +74,24 @@ def layer_attention(q, k_new, v_new, k_cached, v_cached, pos, n_q_heads, n_kv_he
                               pos, n_q_heads, n_kv_heads, head_dim, theta, out.ctypes.data, k_all.ctypes.data,
                               v_all.ctypes.data)
     return out, k_all, v_all
+
+
+def dequantize(kind: int, blocks: np.ndarray, n: int) -> np.ndarray:
+    """ComputeOps.Dequantize of n values (GGUF K-quant blocks as bytes) -> fp32."""
+    blk = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty(n, dtype=np.float32)
+    if lib().ref_dequantize(kind, blk.ctypes.data, n, out.ctypes.data):
+        raise ValueError(f"unsupported kind {kind}")
+    return out
+
+
+def matmul_weights(a: np.ndarray, w_nk: np.ndarray) -> np.ndarray:
+    """ComputeOps.MatMulWeights: a [M, K] fp32 times a GGUF column-major weight given as
+    w_nk [N, K] (element (k, n) at n * K + k) -> [M, N] fp32."""
+    a = _f(a)
+    w = _f(w_nk)
+    M, K = a.shape
+    N = w.shape[0]
+    c = np.empty((M, N), dtype=np.float32)
+    lib().ref_matmul_weights(a.ctypes.data, M, K, w.ctypes.data, N, c.ctypes.data)
+    return c

@@ -452,15 +452,19 @@ cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ct
   if (!mma) memcpy(g_err, saved, sizeof(g_err));  // strides TMA cannot describe: CUDA-core kernel instead
   // One CTA per <= 16 query heads: with a single head group per KV head, the CTA of the last
   // split appends the new rows itself and the last split to finish merges the partials.
+  // The CUDA-core kernel (fp32 caches, strides TMA cannot describe) fuses the append for fp32
+  // caches (its shared copy of the new row is then exactly the stored row) and the merge for
+  // any layout, with up to batch * n_q_heads counters (one per head group).
   const int32_t G = a.n_q_heads / a.n_kv_heads;
   const bool one_group = G <= 16;
-  const int64_t n_counters = static_cast<int64_t>(a.batch) * a.n_kv_heads;
-  a.fuse_append = mma && one_group && a.k_new ? 1 : 0;
+  const int64_t n_counters = mma ? static_cast<int64_t>(a.batch) * a.n_kv_heads
+                                 : static_cast<int64_t>(a.batch) * a.n_q_heads;
+  a.fuse_append = a.k_new && ((mma && one_group) || (!mma && a.kv.dtype == AIHOST_F32)) ? 1 : 0;
   if (ctx) {
     a.counters = ctx->counters;
     a.epoch = ctx->epoch++;
   }
-  if (!(mma && one_group && n_counters <= kMaxSplitCounters)) a.counters = nullptr;
+  if (!((mma ? one_group : true) && n_counters <= kMaxSplitCounters)) a.counters = nullptr;
   cudaError_t e = cudaSuccess;
   if (a.k_new && !a.fuse_append) {
     e = run(AIHOST_KERNEL_APPEND, [&] {

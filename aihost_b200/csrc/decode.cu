@@ -9,12 +9,19 @@
 //   - lanes own head_dim slices, so each K/V row is one coalesced warp-wide load;
 //   - the G dot products of a row are reduced with a multi-value butterfly (G/2 + ... + 1
 //     shuffles per row instead of 5*G);
-//   - partial (max, sum, unnormalised P.V) per split are merged by decode_combine_kernel
-//     (the exp-rescaled sum of the standard split softmax), so any length fits.
+//   - partial (max, sum, unnormalised P.V) per split are merged (the exp-rescaled sum of the
+//     standard split softmax), so any length fits: by the split of a (sequence, head group)
+//     that arrives last (epoch-tagged counter, no CTA waits on another), or, without counters,
+//     by decode_combine_kernel;
+//   - with fuse_append (fp32 caches), the CTAs of a sequence's last split rotate the new token's
+//     K and load its V themselves; the head group's first CTA also stores both rows into the
+//     cache (the append kernel's code, identical bytes), and the new row's scores and P.V use
+//     the shared-memory copy, so the whole decode step is one launch.
 // Q is rotated inside the kernel (RoPE at the sequence's position). Softmax runs in the
 // exp2 domain: s2 = (q.k) * scale * log2(e).
 #include "common.cuh"
 #include "kernels.h"
+#include "rows.cuh"
 
 namespace aihost {
 namespace {
@@ -133,6 +140,33 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
   const int32_t n = min(a.chunk, Lk - t0);
   const int n_splits = (Lk + a.chunk - 1) / a.chunk;
 
+  // ---- the new token's rows (fused append, fp32 caches): rotated K / V of this KV head in
+  // shared memory for this split's last row; the group's first CTA also writes them to the cache
+  __shared__ __align__(16) float new_s[2][D];
+  const bool has_new = a.fuse_append && t0 + a.chunk >= Lk;
+  if (has_new && warp < 2) {
+    const bool is_k = warp == 0;
+    const int64_t row = static_cast<int64_t>(b) * a.n_kv_heads + kvh;
+    const int esz = a.new_dtype == AIHOST_F32 ? 4 : 2;
+    const uint8_t* src = static_cast<const uint8_t*>(is_k ? a.k_new : a.v_new) + row * D * esz;
+    float x[E];
+    load_row_warp<E>(src, a.new_dtype, lane, x);
+    const int32_t t = Lk - 1;
+    if (is_k && a.rope_mode != AIHOST_ROPE_NONE)
+      rope_row_warp<E>(x, lane, static_cast<float>(a.q_pos ? a.q_pos[b] : t), a.rope_mode, a.freqs);
+#pragma unroll
+    for (int e = 0; e < E; ++e) new_s[warp][lane * E + e] = x[e];
+    if (sub == 0) {
+      if (!kv_row_ok(a.kv, b, t)) {
+        if (lane == 0) atomicOr(a.status, kStatusBadLength);
+      } else {
+        uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(is_k ? a.k_cache : a.v_cache)) + kv_row_offset(a.kv, b, t) +
+                       static_cast<int64_t>(kvh) * a.kv.head_stride;
+        store_row_warp<E>(x, lane, dst, a.kv.dtype);
+      }
+    }
+  }
+
   // ---- q rows of this group, rotated at the new token's position, kept as floats
   const float pos = static_cast<float>(a.q_pos ? a.q_pos[b] : start + a.rope_pos_offset);
   for (int idx = threadIdx.x; idx < GT * (D / 2); idx += kDecodeThreads) {
@@ -179,7 +213,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * kDecodeWarps;
-      if (j < n) RowLoader<KV, E>::load(kbase + kv_row_offset(a.kv, b, t0 + j), lane * E, kx[u]);
+      if (has_new && j == n - 1) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) kx[u][e] = new_s[0][lane * E + e];
+      } else if (j < n) RowLoader<KV, E>::load(kbase + kv_row_offset(a.kv, b, t0 + j), lane * E, kx[u]);
       else {
 #pragma unroll
         for (int e = 0; e < E; ++e) kx[u][e] = 0.0f;
@@ -233,7 +270,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int j = j0 + u * kDecodeWarps;
-      if (j < n) RowLoader<KV, E>::load(vbase + kv_row_offset(a.kv, b, t0 + j), lane * E, vx[u]);
+      if (has_new && j == n - 1) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) vx[u][e] = new_s[1][lane * E + e];
+      } else if (j < n) RowLoader<KV, E>::load(vbase + kv_row_offset(a.kv, b, t0 + j), lane * E, vx[u]);
       else {
 #pragma unroll
         for (int e = 0; e < E; ++e) vx[u][e] = 0.0f;
@@ -278,6 +318,38 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
         a.part_ml[pidx * 2 + 1] = l_s[g];
       }
     }
+  }
+  if (n_splits == 1 || !a.counters) return;
+  // ---- fused merge: the last split of this (sequence, head group) to arrive combines them all
+  __shared__ uint32_t s_last;
+  __threadfence();
+  __syncthreads();
+  unsigned long long* counter = &a.counters[static_cast<int64_t>(b) * gridDim.y + blockIdx.y];
+  if (threadIdx.x == 0) {
+    const bool last = split_arrive(counter, a.epoch, n_splits, a.status);
+    if (last) atomicExch(counter, 0ull);  // a replay of the same launch starts from zero
+    s_last = last ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < g_count * D; idx += kDecodeThreads) {
+    const int g = idx / D, d = idx % D;
+    const int h = h0 + g;
+    const int64_t base = (static_cast<int64_t>(b) * a.n_q_heads + h) * a.max_splits;
+    float m = -INFINITY;
+    for (int sp = 0; sp < n_splits; ++sp) m = fmaxf(m, __ldcg(&a.part_ml[(base + sp) * 2]));
+    float l = 0.0f, o = 0.0f;
+    for (int sp = 0; sp < n_splits; ++sp) {
+      const float w = exp2f(__ldcg(&a.part_ml[(base + sp) * 2]) - m);
+      l = fmaf(__ldcg(&a.part_ml[(base + sp) * 2 + 1]), w, l);
+      o = fmaf(__ldcg(&a.part_o[(base + sp) * D + d]), w, o);
+    }
+    const float v = o / l;
+    const int64_t oidx = (static_cast<int64_t>(b) * a.n_q_heads + h) * D + d;
+    if (a.out_dtype == AIHOST_F32) static_cast<float*>(a.out)[oidx] = v;
+    else static_cast<__half*>(a.out)[oidx] = __float2half_rn(v);
+    if (a.lse && d == 0) a.lse[static_cast<int64_t>(b) * a.n_q_heads + h] = (m + log2f(l)) * kLn2;
   }
 }
 

@@ -744,6 +744,163 @@ def _rerun(cfg, meta):
                      inp["v_cache"].numpy(), inp["seq_len"].numpy(), mode=orc.FAITHFUL, part=part)
 
 
+# ------------------------------------------------------------------ weight products
+# (name, rows M, k K, n_out N, weight dtype, n_parts of A, description)
+WEIGHT_CASES = [
+    ("wo_prefill_cfg4", 32768, 4096, 4096, "F16", 1,
+     "output projection after config 4's attention: [32768 x 4096] head outputs . Wo [4096 x 4096] fp16"),
+    ("wo_decode_cfg3", 64, 4096, 4096, "F16", 1,
+     "output projection after config 3's decode step: [64 x 4096] . Wo [4096 x 4096] fp16"),
+    ("qkv_q4k_decode_cfg3", 64, 4096, 6144, "Q4_K", 1,
+     "Q, K, V projections feeding config 3's decode (Wq|Wk|Wv stacked, 6144 x 4096) as GGUF Q4_K"),
+    ("qkv_q6k_prefill_4096", 4096, 4096, 6144, "Q6_K", 1,
+     "Q, K, V projections of a 4096-token Llama-3-8B prefill chunk (Wq|Wk|Wv stacked, 6144 x 4096) as GGUF Q6_K"),
+]
+
+
+def weight_bytes(kind: str, n: int, k: int) -> float:
+    from aihost_b200.gen import KQUANT_BLOCK_BYTES
+    import aihost_b200 as A
+
+    if kind == "F16":
+        return 2.0 * n * k
+    return n * k / 256 * KQUANT_BLOCK_BYTES[getattr(A, kind)]
+
+
+def bench_weights(args, device, ctx, pk, pk_kind, cpu_s):
+    """aihost_matmul_weights on the projections around the op, fp16 A, fp16 output: the device
+    time of a step (weight dequantisation included for K-quant weights: the reference
+    dequantises its weights on every call), the dominant kernel's roofline (tensor-bound when
+    2MNK / bytes exceeds the peaks' ratio, else HBM-bound over the algorithmic bytes: weight as
+    stored + A + output), end to end with A copied in and C copied out, and the oracle's
+    MatMulWeights (+ dequantisation) on a bounded sample of rows on the host cores."""
+    import torch
+
+    import aihost_b200 as A
+    from aihost_b200 import gen
+    from aihost_b200.ops import WeightOps
+
+    ops = WeightOps(ctx)
+    out = {}
+    for name, M, K, N, kind, parts, desc in WEIGHT_CASES:
+        t_start = time.perf_counter()
+        wt = getattr(A, kind)
+        a = gen.normal((M, K), 99, name + ".a", dtype=torch.float16, device=device)
+        if kind == "F16":
+            w = gen.normal((N, K), 99, name + ".w", std=0.02, dtype=torch.float16, device=device)
+        else:
+            w = gen.kquant_blocks(wt, N * K // 256, 99, name + ".w", device=device)
+        c = ops.mat_mul_weights(a, w, wt, N)
+        flops = 2.0 * M * N * K
+        nbytes = weight_bytes(kind, N, K) + 2.0 * M * K + 2.0 * M * N
+        flush = torch.empty(512 << 20, dtype=torch.uint8, device=device) if nbytes < 2 * 126e6 else None
+        for _ in range(args.warmup):
+            if flush is not None:
+                flush.zero_()
+            ops.mat_mul_weights(a, w, wt, N, out=c)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for e0, e1 in ev:
+            if flush is not None:
+                flush.zero_()
+            e0.record()
+            ops.mat_mul_weights(a, w, wt, N, out=c)
+            e1.record()
+        torch.cuda.synchronize()
+        ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+        ctx.profiler_reset()
+        ctx.profiler(True)
+        for _ in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+            ops.mat_mul_weights(a, w, wt, N, out=c)
+        torch.cuda.synchronize()
+        ctx.profiler(False)
+        n_mm, t_mm = ctx.profiler_read(A.KERNEL_MATMUL)
+        n_cv, t_cv = ctx.profiler_read(A.KERNEL_CONVERT)
+        ctx.sync_status()
+        k_ms = t_mm / max(n_mm, 1)
+        tensor_bound = flops / nbytes > pk["bf16_tflops"] * 1e12 / (pk["hbm_gbs"] * 1e9)
+        if tensor_bound:
+            ach = flops / (k_ms * 1e-3) * 1e-12
+            roof = {"bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": ach / pk["bf16_tflops"], "kernel": "gemm_kernel<256>", "kernel_ms": k_ms,
+                    "algorithmic_per_launch": flops, "peak_source": f"{pk_kind} bf16 burst", "traffic": None}
+        else:
+            w16 = 2.0 * N * K  # the GEMM reads the fp16 weight (dequantised copy for K-quants)
+            gbytes = w16 + 2.0 * M * K + 2.0 * M * N
+            ach = gbytes / (k_ms * 1e-3) * 1e-9
+            roof = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+                    "kernel": "gemm_kernel<64>", "kernel_ms": k_ms, "algorithmic_per_launch": gbytes,
+                    "peak_source": f"{pk_kind} copy", "traffic": None,
+                    "note": "bytes of the GEMM launch: fp16 weight + A + C"}
+        # end to end: A from pinned host memory, C back, per step
+        ha = a.cpu().pin_memory()
+        hc = torch.empty(c.shape, dtype=c.dtype, pin_memory=True)
+        e_ms = []
+        for i in range(args.steps + args.warmup):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            a.copy_(ha, non_blocking=True)
+            ops.mat_mul_weights(a, w, wt, N, out=c)
+            hc.copy_(c, non_blocking=True)
+            e1.record()
+            e1.synchronize()
+            if i >= args.warmup:
+                e_ms.append(e0.elapsed_time(e1))
+        res = {"workload": desc, "rows": M, "k": K, "n_out": N, "weight": kind,
+               "value": flops / (ms * 1e-3) * 1e-12, "unit": "TFLOP/s", "ms_per_step": ms,
+               "weight_bytes_as_stored": weight_bytes(kind, N, K),
+               "weight_stream_gbs": weight_bytes(kind, N, K) / (ms * 1e-3) * 1e-9,
+               "roofline": roof, "kernels": {"matmul": {"launches": n_mm, "mean_ms": k_ms},
+                                             "dequant": {"launches": n_cv, "mean_ms": (t_cv / n_cv if n_cv else None)}},
+               "gpu_launches": args.steps * (2 if kind != "F16" else 1),
+               "e2e": {"value": flops / (statistics.mean(e_ms) * 1e-3) * 1e-12, "unit": "TFLOP/s",
+                       "h2d_bytes_per_step": ha.numel() * 2, "d2h_bytes_per_step": hc.numel() * 2,
+                       "ms_per_step": statistics.mean(e_ms)},
+               "l2": "flushed between steps" if flush is not None else "inputs larger than L2"}
+        t_gpu = time.perf_counter()
+        if cpu_s > 0:
+            res["cpu_baseline"] = cpu_weights_baseline(name, M, K, N, kind, a, w, cpu_s)
+        print(f"[bench] weights {name}: gpu {t_gpu - t_start:.1f} s, cpu {time.perf_counter() - t_gpu:.1f} s",
+              file=sys.stderr, flush=True)
+        out[name] = res
+        del a, w, c, flush
+    return out
+
+
+def cpu_weights_baseline(name, M, K, N, kind, a, w, target_s):
+    """The reference's per-call work on the host cores (oracle, faithful fp32): dequantise the
+    whole weight (K-quants; ComputeOps.DequantizeInto runs on every call) and MatMulWeights over
+    a bounded sample of rows, repeated to about target_s; scaled to the whole product."""
+    import numpy as np
+
+    import aihost_b200 as A
+    from oracle import oracle as orc
+
+    a_np = a[: min(M, 64)].float().cpu().numpy()
+    w_np = w.cpu().numpy()
+
+    def run(rows):
+        t = time.perf_counter()
+        wf = (w_np.astype(np.float32) if kind == "F16"
+              else orc.dequantize(getattr(A, kind), w_np, N * K)).reshape(N, K)
+        t_dq = time.perf_counter() - t
+        t = time.perf_counter()
+        orc.matmul_weights(a_np[:rows], wf, mode=orc.FAITHFUL)
+        return t_dq, time.perf_counter() - t
+
+    rows = 1
+    t_dq, t_mm = run(rows)
+    rows = int(max(1, min(a_np.shape[0], round(target_s / 2 / max(t_mm, 1e-4)))))
+    t_dq, t_mm = run(rows)
+    per_call = (t_dq if kind != "F16" else 0.0) + t_mm * M / rows
+    return {"value": 2.0 * M * N * K / per_call * 1e-12, "unit": "TFLOP/s", "cores": orc.num_threads(), "kind": "port",
+            "sample": f"{rows}/{M} rows of MatMulWeights (faithful fp32 oracle) scaled to all rows"
+                      + (", plus one full dequantisation of the weight" if kind != "F16" else ""),
+            "seconds": round(t_dq + t_mm, 3)}
+
+
 def bench_qk_norm(args, device, pk, pk_kind):
     """aihost_qk_norm_rope on a Qwen TypeB-shaped Q block larger than L2: 32768 token rows of
     16 heads x 256, fp16, in place. Algorithmic bytes per launch: the block read and written once."""
@@ -900,6 +1057,8 @@ def main():
         for number, mode, layers in plan:
             extra[f"config_{number}"] = config_object(CONFIGS[number], mode, args, device, ctx, dist_on, ws, rank,
                                                       pk, pk_kind, cpu_other, layers=layers if ws == 1 else 0)
+        if ws == 1:  # the weight products around the op (one GPU; they do not shard here)
+            extra["weights"] = bench_weights(args, device, ctx, pk, pk_kind, 0.0 if args.no_cpu else 3.0)
     clk = clocks.stop()
     if rank == 0:
         line = {"metric": METRIC, "value": main_res["value"], "unit": main_res["unit"], "n_gpus": ws,

@@ -171,6 +171,25 @@ DecodePlan plan_decode(const aihost_attn_desc* d, int32_t batch, int32_t num_sms
   return p;
 }
 
+// The stream-K schedule of the Q8_0 decode (see decode_q8s_kernel) applies to head groups of
+// up to 8 query heads and at most kQ8StreamKMaxUnits sequences.
+bool q8_stream_k_eligible(const aihost_attn_desc* d, int32_t batch) {
+  return d->kv_dtype == AIHOST_Q8_0 && d->n_q_heads / d->n_kv_heads <= 8 && batch <= kQ8StreamKMaxUnits &&
+         d->n_kv_heads <= 64 && batch * static_cast<int64_t>(d->n_kv_heads) <= kMaxSplitCounters;
+}
+
+// Decode scratch of the split plan, and of the stream-K schedule where it applies (the larger
+// of the two); *use_sk tells whether `have` bytes allow the stream-K schedule.
+size_t decode_need_bytes(const aihost_attn_desc* d, int32_t batch, int32_t num_sms, size_t have = SIZE_MAX,
+                         bool* use_sk = nullptr) {
+  const DecodePlan p = plan_decode(d, batch, num_sms);
+  const size_t split = decode_scratch_bytes(batch, d->n_q_heads, d->head_dim, p.max_splits);
+  const size_t sk = q8_stream_k_eligible(d, batch) ? std::max(split, q8_stream_k_bytes(d->head_dim, num_sms)) : 0;
+  const bool sk_ok = sk != 0 && sk <= have;
+  if (use_sk) *use_sk = sk_ok;
+  return sk_ok || have == SIZE_MAX ? std::max(split, sk) : split;
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -275,7 +294,8 @@ aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const 
                          const void* k_new = nullptr, const void* v_new = nullptr, const int32_t* q_pos = nullptr,
                          float* lse = nullptr) {
   DecodePlan plan = plan_decode(d, batch, ctx->num_sms);
-  const size_t need = decode_scratch_bytes(batch, d->n_q_heads, d->head_dim, plan.max_splits);
+  bool use_sk = false;
+  const size_t need = decode_need_bytes(d, batch, ctx->num_sms, ctx->scratch_bytes, &use_sk);
   if (need > ctx->scratch_bytes)
     return fail(AIHOST_ENOMEM, "decode needs %zu bytes of scratch, context has %zu (call aihost_attn_reserve)", need,
                 ctx->scratch_bytes);
@@ -310,6 +330,8 @@ aihost_status run_decode(aihost_attn_ctx* ctx, const aihost_attn_desc* d, const 
   a.new_dtype = d->q_dtype;
   a.q_pos = q_pos;
   a.lse = lse;
+  a.stream_k = use_sk ? 1 : 0;
+  a.num_sms = ctx->num_sms;
   cudaError_t e = launch_decode_any(a, st, ctx);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return AIHOST_OK;
@@ -465,6 +487,7 @@ cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ct
     a.epoch = ctx->epoch++;
   }
   if (!((mma ? one_group : true) && n_counters <= kMaxSplitCounters)) a.counters = nullptr;
+  if (!mma || !a.counters) a.stream_k = 0;  // the stream-K schedule needs the tensor maps and counters
   cudaError_t e = cudaSuccess;
   if (a.k_new && !a.fuse_append) {
     e = run(AIHOST_KERNEL_APPEND, [&] {
@@ -485,6 +508,10 @@ cudaError_t launch_decode_any(DecodeArgs a, cudaStream_t st, aihost_attn_ctx* ct
 }
 
 int32_t ctx_device(const aihost_attn_ctx* ctx) { return ctx ? ctx->device : -1; }
+
+size_t noalloc_need_bytes(const aihost_attn_desc* desc, int32_t batch, int32_t num_sms, size_t have, bool* use_sk) {
+  return decode_need_bytes(desc, batch, num_sms, have, use_sk);
+}
 
 // Validation, split plan and RoPE table of a one-token decode, for aihost_attn_decode_noalloc.
 aihost_status noalloc_prepare(const aihost_attn_desc* desc, int32_t batch, KvLayout* kv, float* scale,
@@ -570,8 +597,7 @@ aihost_status aihost_attn_workspace_size(const aihost_attn_desc* desc, int32_t b
     int sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    DecodePlan p = plan_decode(desc, batch, sms);
-    *out_bytes = decode_scratch_bytes(batch, desc->n_q_heads, desc->head_dim, p.max_splits);
+    *out_bytes = decode_need_bytes(desc, batch, sms);
   }
   return AIHOST_OK;
 }
@@ -915,11 +941,12 @@ struct GemmPlan {
 GemmPlan plan_gemm(const aihost_matmul_desc* d, int32_t num_sms) {
   GemmPlan p;
   p.block_n = gemm_block_n(d->rows, d->n_out, num_sms);
-  const int64_t tiles = static_cast<int64_t>((d->rows + 127) / 128) * ((d->n_out + p.block_n - 1) / p.block_n);
+  const int64_t tiles = gemm_tiles(d->rows, d->n_out, p.block_n);
   const int32_t kt_total = d->k / 64;
+  const int64_t slots = (p.block_n == 64 || p.block_n == -64 ? 2LL : 1LL) * num_sms;
   int64_t splits = 1;
-  if (p.block_n == 64 && tiles < 2LL * num_sms && tiles <= kMaxSplitCounters)
-    splits = std::min<int64_t>(kt_total, (2LL * num_sms + tiles - 1) / tiles);
+  if (p.block_n != 256 && tiles < slots && tiles <= kMaxSplitCounters)
+    splits = std::min<int64_t>(kt_total, (slots + tiles - 1) / tiles);
   p.kt_per_split = static_cast<int32_t>((kt_total + splits - 1) / splits);
   p.k_splits = (kt_total + p.kt_per_split - 1) / p.kt_per_split;
   p.a_stage = d->a_dtype == AIHOST_F16 ? 0 : round256(static_cast<size_t>(d->rows) * d->k * 2);
@@ -1022,9 +1049,11 @@ aihost_status aihost_matmul_weights(aihost_attn_ctx* ctx, const aihost_matmul_de
   GemmArgs ga;
   memset(&ga, 0, sizeof(ga));
   const int64_t part_cols = K / parts;
-  s = encode_3d_f16(&ga.a_map, a16, part_cols, M, parts, part_cols * 2, M * part_cols * 2, 64, 128, "a");
+  const bool swap = p.block_n < 0;
+  const uint32_t a_rows = swap ? static_cast<uint32_t>(-p.block_n) : 128u, w_rows = swap ? 128u : p.block_n;
+  s = encode_3d_f16(&ga.a_map, a16, part_cols, M, parts, part_cols * 2, M * part_cols * 2, 64, a_rows, "a");
   if (s != AIHOST_OK) return s;
-  s = encode_2d_f16(&ga.b_map, w16, K, N, K * 2, 64, p.block_n, "w");
+  s = encode_2d_f16(&ga.b_map, w16, K, N, K * 2, 64, w_rows, "w");
   if (s != AIHOST_OK) return s;
   ga.M = desc->rows;
   ga.N = desc->n_out;

@@ -509,12 +509,12 @@ __device__ __forceinline__ void decode_compute_t(const DecodeArgs& p, uint8_t* s
 
 // Q rows of the group, rotated at the new token's position, as fp16 rows of QROW elements
 // (rows >= g_count zero). All `nthreads` threads of the CTA take part.
-template <int D>
+template <int D, int ROWS = 16>
 __device__ __forceinline__ void load_q_rows(const DecodeArgs& p, __half* q_s, int b, int h0, int g_count,
                                             int32_t start, int nthreads) {
   constexpr int QROW = D + 8;
   const float pos = static_cast<float>(p.q_pos ? p.q_pos[b] : start + p.rope_pos_offset);
-  for (int idx = threadIdx.x; idx < 16 * (D / 2); idx += nthreads) {
+  for (int idx = threadIdx.x; idx < ROWS * (D / 2); idx += nthreads) {
     const int g = idx / (D / 2), pair = idx % (D / 2);
     const int i1 = p.rope_mode == AIHOST_ROPE_NEOX ? pair : 2 * pair;
     const int i2 = p.rope_mode == AIHOST_ROPE_NEOX ? pair + D / 2 : 2 * pair + 1;
@@ -1083,6 +1083,429 @@ __global__ void __launch_bounds__(kQ8kThreads, 2) decode_q8k_kernel(const __grid
   decode_emit<D>(p, merge, h0, g_count, b, split, n_splits);
 }
 
+// ------------------------------------------------------------------ Q8_0 decode, stream-K schedule
+// The same per-tile work as decode_q8k_kernel (K straight from the raw tiles, V through two
+// converter warps), scheduled as one wave: the sequences' 64-row cache tiles are laid end to end,
+// and for every KV head the k-th of C CTAs takes tiles [k*T/C, (k+1)*T/C) of the T in total
+// (CTA k * Hkv + kvh: the heads of a token block are streamed together). A (sequence, KV head)
+// unit is a sequence's tiles for one head. A CTA's range
+// covers one or more units, whole or in part; the producer streams straight across unit
+// boundaries (the ring never drains between units), the compute warps restart their softmax
+// state at each unit. A unit that lies inside one range is written directly; a unit split
+// between CTAs leaves one partial (max, sum, unnormalised O) per part in its CTA's slot (first
+// or last segment of the range: two slots per CTA) and the part that arrives last merges them
+// (epoch-tagged counter per unit, nobody waits). Every CTA streams about the same number of
+// tiles, so there is no partial last wave and each CTA pays its fixed costs once. The four
+// compute warps' partials go to per-CTA slots in scratch (read back from L2), which keeps the
+// shared memory for a 4-deep raw ring at two CTAs per SM.
+constexpr int kSkMaxUnits = kQ8StreamKMaxUnits;  // sequences this schedule handles
+constexpr int kSkMinTiles = 8;     // fewest tiles a range gets (small problems use fewer CTAs)
+
+template <int D>
+struct Q8sCfg {
+  using B = Q8Cfg<D>;
+  static constexpr int NSR = 4;                                 // raw K+V ring depth
+  static constexpr int NSF = 2;                                 // fp16 V ring depth
+  static constexpr int RAW_OFF = 0;
+  static constexpr int F_OFF = (2 * NSR * B::RAW_TILE + 1023) / 1024 * 1024;
+  static constexpr int Q_OFF = F_OFF + NSF * B::F_TILE;
+  static constexpr int Q_BYTES = 8 * (D + 8) * 2;               // the head group's 8 rows of Q
+  static constexpr int TS_OFF = Q_OFF + Q_BYTES;                // tile prefix sums [units + 1]
+  static constexpr int BAR_OFF = TS_OFF + ((kSkMaxUnits + 1) * 4 + 15) / 16 * 16;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;
+  static_assert(SMEM <= 115712, "two stream-K Q8_0 CTAs must fit one SM");
+};
+// Per-warp partial slots of a CTA in scratch: [3 slots][4 warps][8 heads] x (D + 2) floats; slot
+// 0 = the range's first segment, 1 = its last, 2 = a unit that lies wholly inside the range.
+constexpr int kSkSlots = 3;
+
+// Owner CTA of flattened tile t when CTA c covers [c*T/C, (c+1)*T/C).
+__device__ __forceinline__ int sk_owner(int64_t t, int64_t T, int64_t C) {
+  return static_cast<int>(((t + 1) * C - 1) / T);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kQ8kThreads, 2) decode_q8s_kernel(const __grid_constant__ DecodeMmaArgs a) {
+  using C = Q8sCfg<D>;
+  using B = Q8Cfg<D>;
+  constexpr int ROW = B::ROW_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Q8Bars& bar = *reinterpret_cast<Q8Bars*>(smem + C::BAR_OFF);
+  __half* q_s = reinterpret_cast<__half*>(smem + C::Q_OFF);
+  int32_t* ts = reinterpret_cast<int32_t*>(smem + C::TS_OFF);
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const DecodeArgs& p = a.base;
+  const int G = p.n_q_heads / p.n_kv_heads;  // <= 8: one head group per KV head
+  const int NB = p.batch;
+  // CTA c = k * Hkv + kvh: every KV head has the same ranges, taken by adjacent CTAs, so the
+  // heads of a token block are streamed side by side (one DRAM page serves all of a row's heads)
+  const int kvh = static_cast<int>(blockIdx.x) % p.n_kv_heads;
+  const int k_cta = static_cast<int>(blockIdx.x) / p.n_kv_heads;
+  const int64_t Ch = gridDim.x / p.n_kv_heads;
+
+  // ---- tiles per sequence and their prefix sums over the batch, by warp 0
+  if (warp == 0) {
+    const int per = (NB + 31) / 32;
+    const int b0 = lane * per, b1 = min(NB, b0 + per);
+    auto tiles_of = [&](int b) -> int {
+      const int32_t Lk = (p.seq_len ? p.seq_len[b] : p.start_scalar) + p.len_offset;
+      if (Lk > p.kv.capacity || Lk < 1) {
+        if (blockIdx.x == 0) atomicOr(p.status, kStatusBadLength);
+        return 0;
+      }
+      return (Lk + kTileRows - 1) / kTileRows;
+    };
+    int sum = 0;
+    for (int b = b0; b < b1; ++b) sum += tiles_of(b);
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    int run = incl - sum;
+    for (int b = b0; b < b1; ++b) {
+      ts[b] = run;
+      run += tiles_of(b);
+    }
+    if (lane == 31) ts[NB] = incl;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NSR; ++i) {
+      mbar_init(&bar.raw_full[i], 1);
+      mbar_init(&bar.raw_empty[i], kQ8kConvWarps * 32 + kComputeWarps);
+    }
+    for (int i = 0; i < C::NSF; ++i) {
+      mbar_init(&bar.f_full[i], kQ8kConvWarps * 32);
+      mbar_init(&bar.f_empty[i], kComputeWarps);
+    }
+    mbar_init(&bar.appended, 64);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int64_t T = ts[NB];  // tiles of one KV head over the whole batch
+  const int64_t min_ctas = (T + kSkMinTiles - 1) / kSkMinTiles;
+  const int64_t Cn = Ch < min_ctas ? Ch : (min_ctas > 0 ? min_ctas : 1);
+  const int c = blockIdx.x;
+  if (T == 0 || k_cta >= Cn) return;
+  const int64_t lo = k_cta * T / Cn, hi = (k_cta + 1) * T / Cn;
+  if (lo >= hi) return;
+  // first sequence of the range: the last b with ts[b] <= lo (empty sequences have ts[b] == ts[b + 1])
+  int b_first = 0;
+  {
+    int l = 0, r = NB - 1;
+    while (l < r) {
+      const int m = (l + r + 1) >> 1;
+      if (ts[m] <= lo) l = m; else r = m - 1;
+    }
+    b_first = l;
+    while (b_first < NB - 1 && ts[b_first + 1] <= lo) ++b_first;
+  }
+  // Walks this range's segments: f(u, b, kvh, seg_lo, seg_hi, Lk) with tile indices local to the
+  // sequence; u = b * Hkv + kvh is the (sequence, KV head) unit.
+  auto for_segments = [&](auto&& f) {
+    int64_t t = lo;
+    for (int b = b_first; b < NB && t < hi; ++b) {
+      if (ts[b + 1] <= t) continue;
+      const int32_t Lk = (p.seq_len ? p.seq_len[b] : p.start_scalar) + p.len_offset;
+      const int s_lo = static_cast<int>(t - ts[b]);
+      const int64_t seg_end = hi < ts[b + 1] ? hi : static_cast<int64_t>(ts[b + 1]);
+      const int s_hi = static_cast<int>(seg_end - ts[b]);
+      if (!f(b * p.n_kv_heads + kvh, b, kvh, s_lo, s_hi, Lk)) return;
+      t = ts[b] + s_hi;
+    }
+  };
+  const int head_off_words = static_cast<int>(p.kv.head_stride / 4);
+
+  // ---- the new token's rows of every unit whose last tile is in this range (warps 0 and 1),
+  // before the producer loads those tiles
+  const bool appends = p.fuse_append != 0;
+  if (appends && warp < 2) {
+    for_segments([&](int u, int b, int kvh, int s_lo, int s_hi, int32_t Lk) {
+      if (ts[b] + s_hi == ts[b + 1]) append_new_row<D>(p, b, kvh, Lk - 1, warp, lane);
+      return true;
+    });
+    mbar_arrive(&bar.appended);
+  }
+
+  if (warp == kComputeWarps + kQ8kConvWarps) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&a.k_map);
+      tma_prefetch_desc(&a.v_map);
+      int g = 0;
+      bool ok = true;
+      for_segments([&](int u, int b, int kvh, int s_lo, int s_hi, int32_t Lk) {
+        const int head_word = kvh * head_off_words, box_x = head_word & ~3;
+        for (int i = s_lo; i < s_hi; ++i, ++g) {
+          const int s = g % C::NSR;
+          if (appends && i == (Lk - 1) / kTileRows && !mbar_wait(&bar.appended, 0, p.status)) { ok = false; break; }
+          if (!mbar_wait(&bar.raw_empty[s], ((g / C::NSR) & 1) ^ 1, p.status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar.raw_full[s], 2 * B::RAW_TILE);
+          const int r = kv_phys_row(p.kv, b, i * kTileRows), bc = p.kv.block_table ? 0 : b;
+          tma_load_4d(smem + C::RAW_OFF + s * B::RAW_TILE, &a.k_map, &bar.raw_full[s], box_x, r, bc, 0);
+          tma_load_4d(smem + C::RAW_OFF + (C::NSR + s) * B::RAW_TILE, &a.v_map, &bar.raw_full[s], box_x, r, bc, 0);
+        }
+        return ok;
+      });
+    }
+    return;
+  }
+  if (warp >= kComputeWarps) {
+    // ------------------------------------------------------------------ V converters
+    const int row = threadIdx.x - kComputeWarps * 32;  // 0..63
+    int g = 0;
+    bool ok = true;
+    for_segments([&](int u, int b, int kvh, int s_lo, int s_hi, int32_t Lk) {
+      const int off_words = (kvh * head_off_words) & 3;
+      for (int i = s_lo; i < s_hi; ++i, ++g) {
+        const int sr = g % C::NSR, sf = g % C::NSF;
+        if (!mbar_wait(&bar.raw_full[sr], (g / C::NSR) & 1, p.status)) { ok = false; break; }
+        uint32_t w[B::BOX_WORDS];
+        const uint4* src = reinterpret_cast<const uint4*>(smem + C::RAW_OFF + (C::NSR + sr) * B::RAW_TILE + row * ROW);
+#pragma unroll
+        for (int cc = 0; cc < B::BOX_WORDS / 4; ++cc) {
+          const uint4 v = src[cc];
+          w[4 * cc] = v.x;
+          w[4 * cc + 1] = v.y;
+          w[4 * cc + 2] = v.z;
+          w[4 * cc + 3] = v.w;
+        }
+        mbar_arrive(&bar.raw_empty[sr]);
+        if (!mbar_wait(&bar.f_empty[sf], ((g / C::NSF) & 1) ^ 1, p.status)) { ok = false; break; }
+        uint8_t* tile = smem + C::F_OFF + sf * B::F_TILE;
+        if (i * kTileRows + row < Lk) {
+          if constexpr (D == 128) {
+            if (off_words == 0) q8_row_to_f16<D, 0>(w, tile, row);
+            else q8_row_to_f16<D, 2>(w, tile, row);
+          } else {
+            switch (off_words) {
+              case 0: q8_row_to_f16<D, 0>(w, tile, row); break;
+              case 1: q8_row_to_f16<D, 1>(w, tile, row); break;
+              case 2: q8_row_to_f16<D, 2>(w, tile, row); break;
+              default: q8_row_to_f16<D, 3>(w, tile, row); break;
+            }
+          }
+        } else {  // rows past the unit's end: zeros (their stale bytes could decode to NaN)
+#pragma unroll
+          for (int cc = 0; cc < D / 8; ++cc)
+            *reinterpret_cast<uint4*>(tile + (cc >> 3) * (kTileRows * 128) + row * 128 + (((cc & 7) ^ (row & 7)) << 4)) =
+                make_uint4(0, 0, 0, 0);
+        }
+        mbar_arrive(&bar.f_full[sf]);
+      }
+      return ok;
+    });
+    return;
+  }
+
+  // ------------------------------------------------------------------ compute warps
+  const int grp = lane >> 2, tig = lane & 3;
+  const int mi = lane >> 3, r8 = lane & 7;
+  const __half2 k1152 = __floats2half2_rn(1152.0f, 1152.0f);
+  auto i8pair = [&](const uint8_t* p2) -> uint32_t {  // two int8 (2-byte aligned) -> exact fp16 pair
+    const uint32_t x = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(p2)) ^ 0x8080u;
+    const uint32_t e = __byte_perm(x, 0x64646464u, 0x4140);
+    const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&e), k1152);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  };
+  const float sl2 = p.scale * kLog2e;
+  const uint32_t v_base = smem_u32(smem + C::F_OFF);
+  // scratch: part_o [C][slot][warp][8][D], then part_ml [C][slot][warp][8][2]
+  float* part_o = p.part_o;
+  float* part_ml = p.part_o + static_cast<int64_t>(gridDim.x) * kSkSlots * kComputeWarps * 8 * D;
+  int g = 0;
+  bool ok = true;
+  bool first_seg = true;
+  for_segments([&](int u, int b, int kvh, int s_lo, int s_hi, int32_t Lk) {
+    const int h0 = kvh * G;
+    const int32_t start = Lk - p.len_offset;
+    load_q_rows<D, 8>(p, q_s, b, h0, G, start, kComputeWarps * 32);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    uint32_t qb[D / 16][2];
+    {
+      const uint32_t qbase = smem_u32(q_s);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; kk += 2)
+        ldsm_x4(qbase + (r8 * (D + 8) + kk * 16 + 8 * mi) * 2, qb[kk][0], qb[kk][1], qb[kk + 1][0], qb[kk + 1][1]);
+    }
+    float m_run[2] = {-1e30f, -1e30f}, l_run[2] = {0.0f, 0.0f};
+    float o[D / 16][4];
+#pragma unroll
+    for (int m2 = 0; m2 < D / 16; ++m2) o[m2][0] = o[m2][1] = o[m2][2] = o[m2][3] = 0.0f;
+    const int off = ((kvh * head_off_words) & 3) * 4;
+    for (int i = s_lo; i < s_hi && ok; ++i, ++g) {
+      const int sr = g % C::NSR, sf = g % C::NSF;
+      if (!mbar_wait(&bar.raw_full[sr], (g / C::NSR) & 1, p.status)) { ok = false; break; }
+      const int r0 = warp * 16;
+      const uint8_t* k_lo = smem + C::RAW_OFF + sr * B::RAW_TILE + (r0 + grp) * ROW + off;
+      const uint8_t* k_hi = k_lo + 8 * ROW;
+      float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int blk = 0; blk < D / 32; ++blk) {
+        float sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int cb = blk * 34 + 2 + h * 16 + 2 * tig;
+          mma16816(sb, i8pair(k_lo + cb), i8pair(k_hi + cb), i8pair(k_lo + cb + 8), i8pair(k_hi + cb + 8),
+                   qb[2 * blk + h][0], qb[2 * blk + h][1]);
+        }
+        const float d_lo = __half2float(*reinterpret_cast<const __half*>(k_lo + blk * 34));
+        const float d_hi = __half2float(*reinterpret_cast<const __half*>(k_hi + blk * 34));
+        sacc[0] = fmaf(d_lo, sb[0], sacc[0]);
+        sacc[1] = fmaf(d_lo, sb[1], sacc[1]);
+        sacc[2] = fmaf(d_hi, sb[2], sacc[2]);
+        sacc[3] = fmaf(d_hi, sb[3], sacc[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.raw_empty[sr]);
+      const int base_row = i * kTileRows + r0;
+      const bool lo_ok = base_row + grp < Lk, hi_ok = base_row + grp + 8 < Lk;
+      const float s0 = lo_ok ? sacc[0] * sl2 : -INFINITY, s1 = lo_ok ? sacc[1] * sl2 : -INFINITY;
+      const float s2 = hi_ok ? sacc[2] * sl2 : -INFINITY, s3 = hi_ok ? sacc[3] * sl2 : -INFINITY;
+      float mt[2] = {fmaxf(s0, s2), fmaxf(s1, s3)};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 4));
+        mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 8));
+        mt[h] = fmaxf(mt[h], __shfl_xor_sync(0xffffffffu, mt[h], 16));
+      }
+      float f[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float m_new = fmaxf(m_run[h], mt[h]);
+        f[h] = ex2_approx(m_run[h] - m_new);
+        m_run[h] = m_new;
+        l_run[h] *= f[h];
+      }
+#pragma unroll
+      for (int m2 = 0; m2 < D / 16; ++m2) {
+        o[m2][0] *= f[0];
+        o[m2][1] *= f[1];
+        o[m2][2] *= f[0];
+        o[m2][3] *= f[1];
+      }
+      const float p0 = ex2_approx(s0 - m_run[0]), p1 = ex2_approx(s1 - m_run[1]);
+      const float p2 = ex2_approx(s2 - m_run[0]), p3 = ex2_approx(s3 - m_run[1]);
+      l_run[0] += p0 + p2;
+      l_run[1] += p1 + p3;
+      const uint32_t pb0 = movmatrix_trans(pack_h2(p0, p1)), pb1 = movmatrix_trans(pack_h2(p2, p3));
+      if (!mbar_wait(&bar.f_full[sf], (g / C::NSF) & 1, p.status)) { ok = false; break; }
+      const uint32_t vt = v_base + sf * B::F_TILE;
+#pragma unroll
+      for (int m2 = 0; m2 < D / 16; ++m2) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(sw_addr(vt, r0 + r8 + 8 * (mi >> 1), m2 * 16 + 8 * (mi & 1)), a0, a1, a2, a3);
+        mma16816(o[m2], a0, a1, a2, a3, pb0, pb1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.f_empty[sf]);
+    }
+    // every compute thread takes the same path out, so the named barriers below always meet
+    if (!bar1_and_128(ok)) return false;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 4);
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 8);
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 16);
+    }
+    // ---- this warp's (max, sum, unnormalised O) per head into its slot (heads in N: 2 * tig + h)
+    const int n_parts = sk_owner(ts[b + 1] - 1, T, Cn) - sk_owner(ts[b], T, Cn) + 1;
+    const int slot = n_parts == 1 ? 2 : first_seg ? 0 : 1;
+    first_seg = false;
+    const int64_t wbase = ((static_cast<int64_t>(c) * kSkSlots + slot) * kComputeWarps + warp) * 8;
+    if (grp == 0) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        part_ml[(wbase + 2 * tig + h) * 2] = m_run[h];
+        part_ml[(wbase + 2 * tig + h) * 2 + 1] = l_run[h];
+      }
+    }
+#pragma unroll
+    for (int m2 = 0; m2 < D / 16; ++m2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        part_o[(wbase + 2 * tig + (e & 1)) * D + m2 * 16 + grp + 8 * (e >> 1)] = o[m2][e];
+    __threadfence();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // the warps' partials to merge: this slot alone (a whole unit), or every part's slot, once the
+    // part that arrives last has seen all of them
+    int c0 = 0, n_merge = 1;
+    bool c0_first = slot == 0;
+    bool merge = true;
+    if (n_parts > 1) {
+      unsigned long long* counter = &p.counters[u];
+      if (threadIdx.x == 0) {
+        const bool last = split_arrive(counter, p.epoch, n_parts, p.status);
+        if (last) atomicExch(counter, 0ull);
+        s_last = last ? 1 : 0;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      merge = s_last != 0;
+      c0 = sk_owner(ts[b], T, Cn);       // this KV head's range index of the unit's first part
+      c0_first = c0 * T / Cn >= ts[b];  // the unit is that range's first segment
+      n_merge = n_parts;
+      if (merge) __threadfence();
+    }
+    if (merge) {
+      for (int idx = threadIdx.x; idx < G * (D / 4); idx += kComputeWarps * 32) {
+        const int gg = idx / (D / 4), d = (idx % (D / 4)) * 4;
+        auto slot_base = [&](int k, int w) -> int64_t {
+          const int sl = n_parts == 1 ? 2 : (k > 0 || c0_first) ? 0 : 1;
+          const int64_t cc = n_parts == 1 ? c : static_cast<int64_t>(c0 + k) * p.n_kv_heads + kvh;  // CTA of part k
+          return ((cc * kSkSlots + sl) * kComputeWarps + w) * 8 + gg;
+        };
+        float m = -INFINITY;
+        for (int k = 0; k < n_merge; ++k)
+#pragma unroll
+          for (int w = 0; w < kComputeWarps; ++w) m = fmaxf(m, __ldcg(&part_ml[slot_base(k, w) * 2]));
+        float l = 0.0f;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int k = 0; k < n_merge; ++k)
+#pragma unroll
+          for (int w = 0; w < kComputeWarps; ++w) {
+            const int64_t pb = slot_base(k, w);
+            const float wt = exp2f(__ldcg(&part_ml[pb * 2]) - m);
+            l = fmaf(__ldcg(&part_ml[pb * 2 + 1]), wt, l);
+            const float4 o4 = __ldcg(reinterpret_cast<const float4*>(&part_o[pb * D + d]));
+            acc.x = fmaf(o4.x, wt, acc.x);
+            acc.y = fmaf(o4.y, wt, acc.y);
+            acc.z = fmaf(o4.z, wt, acc.z);
+            acc.w = fmaf(o4.w, wt, acc.w);
+          }
+        const float inv = 1.0f / l;
+        const int h = h0 + gg;
+        const int64_t oidx = (static_cast<int64_t>(b) * p.n_q_heads + h) * D + d;
+        if (p.out_dtype == AIHOST_F32) {
+          *reinterpret_cast<float4*>(static_cast<float*>(p.out) + oidx) =
+              make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        } else {
+          *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + oidx) =
+              make_uint2(pack_h2(acc.x * inv, acc.y * inv), pack_h2(acc.z * inv, acc.w * inv));
+        }
+        if (p.lse && d == 0) p.lse[static_cast<int64_t>(b) * p.n_q_heads + h] = (m + log2f(l)) * kLn2;
+      }
+    }
+    // slot 2 and q_s are reused by the next segment
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    return true;
+  });
+}
+
+template <int D>
+cudaError_t launch_q8s(const DecodeMmaArgs& a, int32_t num_sms, cudaStream_t st) {
+  using C = Q8sCfg<D>;
+  auto kern = decode_q8s_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int hkv = a.base.n_kv_heads;
+  kern<<<(2 * num_sms) / hkv * hkv, kQ8kThreads, C::SMEM, st>>>(a);
+  return cudaGetLastError();
+}
+
 template <int D>
 cudaError_t launch_q8k(const DecodeMmaArgs& a, cudaStream_t st) {
   using C = Q8kCfg<D>;
@@ -1123,7 +1546,13 @@ cudaError_t launch_d(const DecodeMmaArgs& a, cudaStream_t st) {
 
 }  // namespace
 
+size_t q8_stream_k_bytes(int32_t head_dim, int32_t num_sms) {
+  return sizeof(float) * static_cast<size_t>(2 * num_sms) * kSkSlots * kComputeWarps * 8 * (head_dim + 2);
+}
+
 cudaError_t launch_decode_mma(const DecodeMmaArgs& a, cudaStream_t st) {
+  if (a.base.kv.dtype == AIHOST_Q8_0 && a.base.stream_k)
+    return a.base.head_dim == 64 ? launch_q8s<64>(a, a.base.num_sms, st) : launch_q8s<128>(a, a.base.num_sms, st);
   if (a.base.kv.dtype == AIHOST_Q8_0) return a.base.head_dim == 64 ? launch_q8<64>(a, st) : launch_q8<128>(a, st);
   return a.base.head_dim == 64 ? launch_d<64>(a, st) : launch_d<128>(a, st);
 }

@@ -125,12 +125,16 @@ aihost_status wait_comm(aihost_attn_dist* d, int32_t timeout_ms, const char* wha
       abort_comm(d);
       return nccl_fail(st, what);
     }
-    if (elapsed_ms(t0) > timeout_ms) {
+    const double ms = elapsed_ms(t0);
+    if (ms > timeout_ms) {
       abort_comm(d);
       return api_fail(AIHOST_ETIMEOUT, "%s did not finish within %d ms (a rank missing?); communicator aborted", what,
                       timeout_ms);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    // a collective's enqueue normally finishes within microseconds: spin (yielding) for the first
+    // 2 ms so the stream gets its work at once, then poll every 100 us (set-up, a slow peer)
+    if (ms < 2.0) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(100));
   }
 }
 
@@ -224,13 +228,15 @@ aihost_status aihost_attn_dist_sync(aihost_attn_dist* d, void* stream, int32_t t
         break;
       }
     }
-    if (elapsed_ms(t0) > timeout_ms) {
+    const double ms = elapsed_ms(t0);
+    if (ms > timeout_ms) {
       if (d->world > 1) abort_comm(d);
       s = api_fail(AIHOST_ETIMEOUT, "the stream's work did not finish within %d ms%s", timeout_ms,
                    d->world > 1 ? "; communicator aborted" : "");
       break;
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(100));
+    if (ms < 2.0) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(100));
   }
   cudaSetDevice(prev);
   return s;

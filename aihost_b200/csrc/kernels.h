@@ -115,6 +115,11 @@ struct DecodeArgs {
   // lse[b][h] = ln sum_j exp(scale * q.k_j) over the attended rows, written with the output.
   const int32_t* q_pos;
   float* lse;
+  // Q8_0 caches, head groups of <= 8, batch <= 512: the stream-K schedule (one wave
+  // of 2 CTAs per SM over the flattened cache tiles); part_o then holds q8_stream_k_bytes of
+  // per-CTA partial slots. Set by the host (launch_decode_any keeps it only for TMA-able caches).
+  int32_t stream_k;
+  int32_t num_sms;
 };
 constexpr float kLn2 = 0.6931471805599453f;
 // Arrival counters a fused combine may use (per (sequence, KV head, head group)).
@@ -139,6 +144,10 @@ struct DecodeMmaArgs {
   CUtensorMap v_map;
 };
 cudaError_t launch_decode_mma(const DecodeMmaArgs& a, cudaStream_t st);
+// Scratch of the stream-K Q8_0 decode: three per-warp partial slots of 8 heads per CTA (2 CTAs
+// per SM).
+size_t q8_stream_k_bytes(int32_t head_dim, int32_t num_sms);
+constexpr int32_t kQ8StreamKMaxUnits = 512;
 // Width in 32-bit words of the TMA box that holds one (token, head) slice of a Q8_0 cache whose
 // heads are head_stride bytes apart (the narrowest 16-byte multiple every head offset fits).
 uint32_t q8_box_words(int32_t head_dim, int64_t head_stride);
@@ -186,8 +195,8 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t st);
 // ---------------------------------------------------------------- matmul_sm100.cu
 // C[M, N] = A[M, K] . W[N, K]^T on the tensor cores (fp16 operands, fp32 accumulation).
 struct GemmArgs {
-  CUtensorMap a_map;   // fp16 A: dims {part_cols, M, n_parts}, box {64, 128, 1}, 128-byte swizzle
-  CUtensorMap b_map;   // fp16 W: dims {K, N}, box {64, BN}, 128-byte swizzle
+  CUtensorMap a_map;   // fp16 A: dims {part_cols, M, n_parts}, box {64, 128 (BN when swapped), 1}, 128-byte swizzle
+  CUtensorMap b_map;   // fp16 W: dims {K, N}, box {64, BN (128 when swapped)}, 128-byte swizzle
   int32_t M, N, K, part_cols;
   int32_t k_splits, kt_per_split;  // K range split over CTAs (64-wide K tiles per split)
   void* out;           // [M][ldc] in out_dtype
@@ -203,8 +212,11 @@ int32_t weight_block_bytes(int32_t wt);
 // GGUF K-quant blocks -> n_elems values (a multiple of 256) in out_dtype (F16 or F32).
 cudaError_t launch_dequant(const void* w, int32_t wt, int64_t n_elems, void* out, int32_t out_dtype, cudaStream_t st);
 cudaError_t launch_f32_to_f16(const float* x, __half* y, int64_t n, int32_t num_sms, cudaStream_t st);
-// Output-tile width the GEMM uses for this shape (256 when the tiles fill the SMs, else 64).
+// Output-tile width the GEMM uses for this shape: 256 when the tiles fill the SMs, else 64; for
+// at most 128 rows of A, -64 / -128: the swapped form (weight rows in the MMA's M, BN rows of A).
 int32_t gemm_block_n(int32_t M, int32_t N, int32_t num_sms);
+// Output tiles of that shape and width.
+int64_t gemm_tiles(int32_t M, int32_t N, int32_t block_n);
 cudaError_t launch_gemm(const GemmArgs& a, int32_t block_n, int32_t num_sms, cudaStream_t st);
 
 }  // namespace aihost

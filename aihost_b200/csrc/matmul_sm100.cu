@@ -14,7 +14,7 @@
 // part k / (K / n_parts). With n_parts = N ranks this is the rank-major buffer the KV-head
 // sharded all-gather leaves ([N][B][S][Hq/N][d]), consumed in place, with no permute.
 //
-// Kernel: persistent, one CTA per SM (BN = 256) or two (BN = 64), 256 threads:
+// Kernel: persistent, one CTA per SM (BN = 256, 128) or two (BN = 64), 256 threads:
 //   warp 0      TMA producer: A [128 x 64] and W [BN x 64] tiles into an NS-stage ring
 //   warp 1      TMEM owner (2 x BN fp32 columns: two accumulators) and the tcgen05.mma issuer
 //               (M = 128, N = BN, K = 16, both operands K-major, 128-byte swizzle)
@@ -70,7 +70,11 @@ __device__ __forceinline__ void store8(void* out, int32_t out_dtype, int64_t idx
   }
 }
 
-template <int BN>
+// SWAP (few rows of A, i.e. decode): the MMA's M = 128 rows are weight rows (output columns) and
+// its N = BN columns are rows of A, so the weight, not zero padding, fills the 128-row operand;
+// the accumulator then holds C^T and the epilogue stores it transposed (one row of C per TMEM
+// column: 32 lanes write 32 consecutive outputs).
+template <int BN, bool SWAP>
 __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -78,7 +82,9 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
   GemmBars& bar = *reinterpret_cast<GemmBars*>(smem + C::BAR_OFF);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int m_tiles = (a.M + kGBM - 1) / kGBM, n_tiles = (a.N + BN - 1) / BN;
+  // tile rows (TMEM lanes) and tile columns: C's rows and columns, or its columns and rows (SWAP)
+  const int R = SWAP ? a.N : a.M, NC = SWAP ? a.M : a.N;
+  const int m_tiles = (R + kGBM - 1) / kGBM, n_tiles = (NC + BN - 1) / BN;
   const int kt_total = a.K / kGBK;
   const int units = m_tiles * n_tiles * a.k_splits;
   int32_t* status = a.status;
@@ -125,8 +131,13 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
           uint8_t* st = smem + s * C::STAGE;
           mbar_arrive_expect_tx(&bar.full[s], C::STAGE);
           const int k = kt * kGBK;
-          tma_load_3d(st, &a.a_map, &bar.full[s], k % a.part_cols, mt * kGBM, k / a.part_cols);
-          tma_load_2d(st + C::A_BYTES, &a.b_map, &bar.full[s], k, nt * BN);
+          if constexpr (SWAP) {  // A operand: weight rows; B operand: rows of A
+            tma_load_2d(st, &a.b_map, &bar.full[s], k, mt * kGBM);
+            tma_load_3d(st + C::A_BYTES, &a.a_map, &bar.full[s], k % a.part_cols, nt * BN, k / a.part_cols);
+          } else {
+            tma_load_3d(st, &a.a_map, &bar.full[s], k % a.part_cols, mt * kGBM, k / a.part_cols);
+            tma_load_2d(st + C::A_BYTES, &a.b_map, &bar.full[s], k, nt * BN);
+          }
         }
       }
     }
@@ -172,31 +183,53 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
       // the four epilogue warps leave together (they meet at named barrier 1 below)
       if (!bar1_and_128(mbar_wait(&bar.acc_full[buf], (j >> 1) & 1, status))) break;
       tc_fence_after();
-      const int m = mt * kGBM + r, n0 = nt * BN;
-      const bool row_ok = m < a.M;
       const int ks = u % a.k_splits;
       // fp32 partial of this split (split-K), or the output itself
       float* part = a.k_splits > 1 ? a.partials + static_cast<int64_t>(ks) * a.M * a.N : nullptr;
+      if constexpr (SWAP) {
+        // lane r = output column n, TMEM column j = output row m: for each j the warp's 32 lanes
+        // write 32 consecutive outputs of row m
+        const int n = mt * kGBM + r, m0 = nt * BN;
+        const bool col_ok = n < a.N;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + static_cast<uint32_t>(buf * BN + c * 32), v);
-        tmem_wait_ld();
-        if (!row_ok) continue;
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_base + static_cast<uint32_t>(buf * BN + c * 32), v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int g8 = 0; g8 < 4; ++g8) {
-          const int n = n0 + c * 32 + g8 * 8;
-          if (n >= a.N) break;
-          float f[8];
+          for (int jj = 0; jj < 32; ++jj) {
+            const int m = m0 + c * 32 + jj;
+            if (!col_ok || m >= a.M) continue;
+            const float f = __uint_as_float(v[jj]);
+            if (part) part[static_cast<int64_t>(m) * a.N + n] = f;
+            else if (a.out_dtype == AIHOST_F16) static_cast<__half*>(a.out)[static_cast<int64_t>(m) * a.ldc + n] = __float2half_rn(f);
+            else static_cast<float*>(a.out)[static_cast<int64_t>(m) * a.ldc + n] = f;
+          }
+        }
+      } else {
+        const int m = mt * kGBM + r, n0 = nt * BN;
+        const bool row_ok = m < a.M;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_base + static_cast<uint32_t>(buf * BN + c * 32), v);
+          tmem_wait_ld();
+          if (!row_ok) continue;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[g8 * 8 + i]);
-          const int64_t idx = static_cast<int64_t>(m) * a.N + n;
-          if (part) {
-            float4* d = reinterpret_cast<float4*>(part + idx);
-            d[0] = make_float4(f[0], f[1], f[2], f[3]);
-            d[1] = make_float4(f[4], f[5], f[6], f[7]);
-          } else {
-            store8(a.out, a.out_dtype, static_cast<int64_t>(m) * a.ldc + n, f);
+          for (int g8 = 0; g8 < 4; ++g8) {
+            const int n = n0 + c * 32 + g8 * 8;
+            if (n >= a.N) break;
+            float f[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[g8 * 8 + i]);
+            const int64_t idx = static_cast<int64_t>(m) * a.N + n;
+            if (part) {
+              float4* d = reinterpret_cast<float4*>(part + idx);
+              d[0] = make_float4(f[0], f[1], f[2], f[3]);
+              d[1] = make_float4(f[4], f[5], f[6], f[7]);
+            } else {
+              store8(a.out, a.out_dtype, static_cast<int64_t>(m) * a.ldc + n, f);
+            }
           }
         }
       }
@@ -218,11 +251,13 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (!bar.last) continue;
       __threadfence();
-      const int rows = min(kGBM, a.M - mt * kGBM), cols = min(BN, a.N - n0);
+      // the output tile: rows [m_lo, m_lo + rows) and columns [n_lo, n_lo + cols) of C
+      const int m_lo = SWAP ? nt * BN : mt * kGBM, n_lo = SWAP ? mt * kGBM : nt * BN;
+      const int rows = min(SWAP ? BN : kGBM, a.M - m_lo), cols = min(SWAP ? kGBM : BN, a.N - n_lo);
       const int groups = cols / 4;  // N % 8 == 0
       for (int idx = et; idx < rows * groups; idx += 128) {
         const int rr = idx / groups, cg = idx % groups;
-        const int64_t e = static_cast<int64_t>(mt * kGBM + rr) * a.N + n0 + cg * 4;
+        const int64_t e = static_cast<int64_t>(m_lo + rr) * a.N + n_lo + cg * 4;
         float4 acc = __ldcg(reinterpret_cast<const float4*>(a.partials + e));
         for (int sp = 1; sp < a.k_splits; ++sp) {
           const float4 x = __ldcg(reinterpret_cast<const float4*>(a.partials + static_cast<int64_t>(sp) * a.M * a.N + e));
@@ -231,7 +266,7 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
           acc.z += x.z;
           acc.w += x.w;
         }
-        const int64_t o = static_cast<int64_t>(mt * kGBM + rr) * a.ldc + n0 + cg * 4;
+        const int64_t o = static_cast<int64_t>(m_lo + rr) * a.ldc + n_lo + cg * 4;
         if (a.out_dtype == AIHOST_F16) {
           *reinterpret_cast<uint2*>(static_cast<__half*>(a.out) + o) = make_uint2(pack2h(acc.x, acc.y), pack2h(acc.z, acc.w));
         } else {
@@ -329,6 +364,70 @@ __device__ float dequant_one(int32_t wt, const uint8_t* blk, int e) {
   }
 }
 
+// Lane l's eight values [8l, 8l + 8) of a 256-value block with vector loads: the same fp32
+// operations as dequant_one (and the reference shaders), one load per field.
+__device__ __forceinline__ void dequant8_q4k(const uint8_t* blk, int l, float (&v)[8]) {
+  const uint32_t dw = *reinterpret_cast<const uint32_t*>(blk);  // 144-byte blocks are 16-byte aligned
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dw & 0xffffu)));
+  const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(dw >> 16)));
+  uint8_t sc8[12];
+  *reinterpret_cast<uint32_t*>(sc8) = *reinterpret_cast<const uint32_t*>(blk + 4);
+  *reinterpret_cast<uint32_t*>(sc8 + 4) = *reinterpret_cast<const uint32_t*>(blk + 8);
+  *reinterpret_cast<uint32_t*>(sc8 + 8) = *reinterpret_cast<const uint32_t*>(blk + 12);
+  float sc, mn;
+  scale_min_k4(l >> 2, sc8, &sc, &mn);  // sub-block (l / 8) * 2 + upper == l / 4
+  const uint2 q = *reinterpret_cast<const uint2*>(blk + 16 + (l >> 3) * 32 + (l & 3) * 8);
+  const int shift = ((l & 7) >> 2) * 4;
+  const float t = __fmul_rn(d, sc), dm = __fmul_rn(dmin, mn);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t byte = ((i < 4 ? q.x : q.y) >> ((i & 3) * 8)) & 0xffu;
+    v[i] = __fsub_rn(__fmul_rn(t, static_cast<float>((byte >> shift) & 0xFu)), dm);
+  }
+}
+
+__device__ __forceinline__ void dequant8_q5k(const uint8_t* blk, int l, float (&v)[8]) {
+  const uint32_t dw = *reinterpret_cast<const uint32_t*>(blk);  // 176-byte blocks are 16-byte aligned
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dw & 0xffffu)));
+  const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(dw >> 16)));
+  uint8_t sc8[12];
+  *reinterpret_cast<uint32_t*>(sc8) = *reinterpret_cast<const uint32_t*>(blk + 4);
+  *reinterpret_cast<uint32_t*>(sc8 + 4) = *reinterpret_cast<const uint32_t*>(blk + 8);
+  *reinterpret_cast<uint32_t*>(sc8 + 8) = *reinterpret_cast<const uint32_t*>(blk + 12);
+  float sc, mn;
+  scale_min_k4(l >> 2, sc8, &sc, &mn);
+  const int j = l >> 3, upper = (l & 7) >> 2, off = j * 32 + (l & 3) * 8;
+  const uint2 ql = *reinterpret_cast<const uint2*>(blk + 48 + off);
+  const uint2 qh = *reinterpret_cast<const uint2*>(blk + 16 + off);  // the reference reads byte 16 + j*32 + l
+  const int hb = j * 2 + upper;
+  const float t = __fmul_rn(d, sc), dm = __fmul_rn(dmin, mn);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t lo = (((i < 4 ? ql.x : ql.y) >> ((i & 3) * 8)) >> (upper * 4)) & 0xFu;
+    const uint32_t hi = (((i < 4 ? qh.x : qh.y) >> ((i & 3) * 8)) >> hb) & 1u;
+    v[i] = __fsub_rn(__fmul_rn(t, static_cast<float>(lo | (hi << 4))), dm);
+  }
+}
+
+__device__ __forceinline__ void dequant8_q6k(const uint8_t* blk, int l, float (&v)[8]) {
+  // 210-byte blocks: 2-byte alignment only, so 16-bit loads
+  const int half = l >> 4, quarter = (l & 15) >> 2, wq = (l & 3) * 8;
+  const uint16_t* ql = reinterpret_cast<const uint16_t*>(blk + half * 64 + ((quarter & 1) ? 32 : 0) + wq);
+  const uint16_t* qh = reinterpret_cast<const uint16_t*>(blk + 128 + half * 32 + wq);
+  const int upper = quarter >> 1;
+  const float t = __fmul_rn(h2f(blk + 208), static_cast<float>(static_cast<int8_t>(blk[192 + (l >> 1)])));
+#pragma unroll
+  for (int i2 = 0; i2 < 4; ++i2) {
+    const uint32_t lw = ql[i2], hw = qh[i2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint32_t lo = ((lw >> (k * 8)) >> (upper * 4)) & 0xFu;
+      const uint32_t hi = ((hw >> (k * 8)) >> (quarter * 2)) & 3u;
+      v[2 * i2 + k] = __fmul_rn(t, __fsub_rn(static_cast<float>(lo | (hi << 4)), 32.0f));
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ w, int32_t wt, int64_t n_blocks,
                                                       int32_t block_bytes, T* __restrict__ out) {
@@ -337,8 +436,13 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
   const int lane = threadIdx.x & 31;
   const uint8_t* src = w + blk * block_bytes;
   float v[8];
+  if (wt == AIHOST_Q4_K) dequant8_q4k(src, lane, v);
+  else if (wt == AIHOST_Q5_K) dequant8_q5k(src, lane, v);
+  else if (wt == AIHOST_Q6_K) dequant8_q6k(src, lane, v);
+  else {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = dequant_one(wt, src, lane * 8 + i);
+    for (int i = 0; i < 8; ++i) v[i] = dequant_one(wt, src, lane * 8 + i);
+  }
   if constexpr (std::is_same<T, __half>::value) {
     *reinterpret_cast<uint4*>(out + blk * 256 + lane * 8) =
         make_uint4(pack2h(v[0], v[1]), pack2h(v[2], v[3]), pack2h(v[4], v[5]), pack2h(v[6], v[7]));
@@ -358,10 +462,10 @@ __global__ void __launch_bounds__(256) f32_to_f16_kernel(const float* __restrict
   }
 }
 
-template <int BN>
+template <int BN, bool SWAP>
 cudaError_t launch_gemm_bn(const GemmArgs& a, int grid, cudaStream_t st) {
   using C = GemmCfg<BN>;
-  auto kern = gemm_kernel<BN>;
+  auto kern = gemm_kernel<BN, SWAP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   kern<<<grid, kGemmThreads, C::SMEM, st>>>(a);
@@ -403,15 +507,28 @@ cudaError_t launch_f32_to_f16(const float* x, __half* y, int64_t n, int32_t num_
 }
 
 int32_t gemm_block_n(int32_t M, int32_t N, int32_t num_sms) {
+  if (M <= 128) return M <= 64 ? -64 : -128;  // few rows: swapped operands, BN = rows of A
   const int64_t tiles256 = static_cast<int64_t>((M + kGBM - 1) / kGBM) * ((N + 255) / 256);
   return tiles256 >= num_sms ? 256 : 64;
 }
 
+int64_t gemm_tiles(int32_t M, int32_t N, int32_t block_n) {
+  const bool swap = block_n < 0;
+  const int bn = swap ? -block_n : block_n;
+  const int R = swap ? N : M, NC = swap ? M : N;
+  return static_cast<int64_t>((R + kGBM - 1) / kGBM) * ((NC + bn - 1) / bn);
+}
+
 cudaError_t launch_gemm(const GemmArgs& a, int32_t block_n, int32_t num_sms, cudaStream_t st) {
-  const int64_t units = static_cast<int64_t>((a.M + kGBM - 1) / kGBM) * ((a.N + block_n - 1) / block_n) * a.k_splits;
-  const int64_t per_sm = block_n == 256 ? 1 : 2;
+  const int64_t units = gemm_tiles(a.M, a.N, block_n) * a.k_splits;
+  const int64_t per_sm = (block_n == 64 || block_n == -64) ? 2 : 1;
   const int grid = static_cast<int>(units < per_sm * num_sms ? units : per_sm * num_sms);
-  return block_n == 256 ? launch_gemm_bn<256>(a, grid, st) : launch_gemm_bn<64>(a, grid, st);
+  switch (block_n) {
+    case 256: return launch_gemm_bn<256, false>(a, grid, st);
+    case -64: return launch_gemm_bn<64, true>(a, grid, st);
+    case -128: return launch_gemm_bn<128, true>(a, grid, st);
+    default: return launch_gemm_bn<64, false>(a, grid, st);
+  }
 }
 
 }  // namespace aihost

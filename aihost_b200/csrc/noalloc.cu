@@ -40,6 +40,7 @@ namespace aihost {
 aihost_status api_fail(aihost_status st, const char* fmt, ...);
 aihost_status noalloc_prepare(const aihost_attn_desc* desc, int32_t batch, KvLayout* kv, float* scale,
                               int32_t* chunk, int32_t* max_splits, RopeFreqs* freqs, int32_t num_sms);
+size_t noalloc_need_bytes(const aihost_attn_desc* desc, int32_t batch, int32_t num_sms, size_t have, bool* use_sk);
 
 namespace {
 
@@ -100,7 +101,8 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   aihost_status s = noalloc_prepare(desc, batch, &kv, &scale, &chunk, &max_splits, &freqs, sms);
   if (s != AIHOST_OK) return s;
   // the size check depends on the description alone and comes before the pointer checks
-  const size_t need = decode_scratch_bytes(batch, desc->n_q_heads, desc->head_dim, max_splits);
+  bool use_sk = false;
+  const size_t need = noalloc_need_bytes(desc, batch, sms, kNoAllocScratchBytes, &use_sk);
   if (need > kNoAllocScratchBytes)
     return api_fail(AIHOST_ENOMEM,
                  "aihost_attn_decode_noalloc: this call needs %zu bytes of split scratch; the static array holds "
@@ -153,6 +155,8 @@ extern "C" aihost_status aihost_attn_decode_noalloc(const aihost_attn_desc* desc
   a.new_dtype = desc->q_dtype;
   a.counters = reinterpret_cast<unsigned long long*>(base + kStatusBytes);
   a.epoch = next_epoch(dev);
+  a.stream_k = use_sk ? 1 : 0;
+  a.num_sms = sms;
   e = launch_decode_any(a, st, nullptr);
   if (e != cudaSuccess) return api_fail(AIHOST_ECUDA, "decode launch: %s", cudaGetErrorString(e));
   return AIHOST_OK;

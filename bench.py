@@ -63,6 +63,9 @@ def parse_args():
                     help="qk-norm-rope: time the Qwen TypeB Q/K prologue kernel alone (one GPU; GB/s of HBM)")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N untimed fused calls of --config and exit (the command profiled with ncu)")
+    ap.add_argument("--profile-weights", default="",
+                    help="with --profile-steps: run that many untimed calls of this weight-product case "
+                         "(a name of WEIGHT_CASES) instead of an attention config")
     ap.add_argument("--profile-new", type=int, default=0,
                     help="with --profile-steps: override the config's new rows per sequence (a smaller prefill "
                          "of the same shape, for captures that must stay small)")
@@ -542,7 +545,10 @@ def decode_kernel_name(cfg) -> str:
     from aihost_b200 import F16, Q8_0
 
     if cfg.kv_dtype == Q8_0:  # head groups of up to 8 read K straight from the raw tiles
-        return "decode_q8k_kernel" if cfg.n_q_heads // cfg.n_kv_heads <= 8 else "decode_q8_kernel"
+        if cfg.n_q_heads // cfg.n_kv_heads > 8:
+            return "decode_q8_kernel"
+        # the stream-K schedule for up to 512 sequences
+        return "decode_q8s_kernel" if cfg.batch <= 512 else "decode_q8k_kernel"
     return {F16: "decode_mma_kernel"}.get(cfg.kv_dtype, "decode_splitk_kernel")
 
 
@@ -869,6 +875,28 @@ def bench_weights(args, device, ctx, pk, pk_kind, cpu_s):
     return out
 
 
+def profile_weights(name, n, device):
+    """n untimed calls of one weight-product case: the target of ncu captures."""
+    import torch
+
+    import aihost_b200 as A
+    from aihost_b200 import gen
+    from aihost_b200.ops import Context, WeightOps
+
+    case = {c[0]: c for c in WEIGHT_CASES}[name]
+    _, M, K, N, kind, _, _ = case
+    with Context(device.index) as ctx:
+        ops = WeightOps(ctx)
+        a = gen.normal((M, K), 99, name + ".a", dtype=torch.float16, device=device)
+        w = (gen.normal((N, K), 99, name + ".w", std=0.02, dtype=torch.float16, device=device) if kind == "F16"
+             else gen.kquant_blocks(getattr(A, kind), N * K // 256, 99, name + ".w", device=device))
+        for _ in range(n):
+            c = ops.mat_mul_weights(a, w, getattr(A, kind), N)
+        torch.cuda.synchronize()
+        ctx.sync_status()
+        print(f"profiled {name}: {n} calls, mean |c| {c.float().abs().mean().item():.4f}")
+
+
 def cpu_weights_baseline(name, M, K, N, kind, a, w, target_s):
     """The reference's per-call work on the host cores (oracle, faithful fp32): dequantise the
     whole weight (K-quants; ComputeOps.DequantizeInto runs on every call) and MatMulWeights over
@@ -1028,6 +1056,9 @@ def main():
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if args.profile_steps and args.profile_weights:
+        profile_weights(args.profile_weights, args.profile_steps, device)
+        return
     if args.profile_steps:
         pcfg = CONFIGS[args.config]
         if args.profile_new:

@@ -111,6 +111,27 @@ def test_decode_cfg5_q8_full_sample(ctx):
     check_call(ctx, CONFIGS[5], part=(0, 2, 0, 64))
 
 
+@pytest.mark.parametrize("batch,hq,hkv,lengths", [
+    (1, 8, 1, [5]),                                   # fewer tiles than CTAs: ranges of a few tiles
+    (3, 16, 2, [1, 700, 64]),                         # ragged: a 1-row unit, tile-aligned lengths
+    (4, 32, 8, [4095, 17, 2049, 300]),                # groups of 4 query heads
+    (64, 64, 8, None),                                # 512 (sequence, KV head) units
+    (65, 16, 8, None),
+    (513, 8, 1, "short"),                             # more sequences than the schedule takes: per-split kernel
+])
+def test_decode_q8_stream_k_partitions(ctx, batch, hq, hkv, lengths):
+    """Q8_0 decode over the stream-K schedule (every CTA an equal share of the cache tiles laid
+    end to end; units split between CTAs merged by the last part): every unit, whole or split,
+    must match the dequantise-then-attend oracle; the appended blocks byte for byte."""
+    import numpy as np
+
+    if lengths is None or lengths == "short":
+        hi = 1500 if lengths is None else 200
+        lengths = [int(x) for x in np.random.default_rng(batch).integers(1, hi, batch)]
+    cfg = CONFIGS[5].scaled(batch=batch, n_q_heads=hq, n_kv_heads=hkv, cached=None, cached_list=lengths)
+    check_call(ctx, cfg, part=(0, min(batch, 6), 0, hq))
+
+
 def test_decode_stale_nan_rows_ignored(ctx):
     """Cache rows past each sequence's length hold NaN bit patterns; they must not leak."""
     cfg = CONFIGS[3].scaled(batch=2, n_q_heads=8, n_kv_heads=2, cached_range=None, cached_list=[40, 300])

@@ -111,7 +111,10 @@ __device__ __forceinline__ float butterfly_reduce(float (&v)[GT], int lane, int&
   return r;
 }
 
-template <typename KV, int D, int GT>
+// SMALL (splits of at most 64 rows, D = 64): each warp's eight K and eight V rows are loaded at
+// kernel entry, before the Q rotation and the append, so a short decode pays one round trip to
+// memory for its rows instead of one per loop pass.
+template <typename KV, int D, int GT, bool SMALL>
 __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArgs a) {
   constexpr int E = D / 32;
   extern __shared__ float4 smem_raw[];
@@ -140,10 +143,29 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
   const int32_t n = min(a.chunk, Lk - t0);
   const int n_splits = (Lk + a.chunk - 1) / a.chunk;
 
+  const bool has_new = a.fuse_append && t0 + a.chunk >= Lk;
+  const uint8_t* kbase = static_cast<const uint8_t*>(a.k_cache) + kvh * a.kv.head_stride;
+  const uint8_t* vbase = static_cast<const uint8_t*>(a.v_cache) + kvh * a.kv.head_stride;
+  constexpr int PR = SMALL ? 64 / kDecodeWarps : 1;  // rows per warp preloaded
+  float kpre[PR][E], vpre[PR][E];
+  if constexpr (SMALL) {
+#pragma unroll
+    for (int u = 0; u < PR; ++u) {
+      const int j = warp + u * kDecodeWarps;
+      const bool load = j < n && !(has_new && j == n - 1);  // the new row comes from shared memory
+      if (load) {
+        RowLoader<KV, E>::load(kbase + kv_row_offset(a.kv, b, t0 + j), lane * E, kpre[u]);
+        RowLoader<KV, E>::load(vbase + kv_row_offset(a.kv, b, t0 + j), lane * E, vpre[u]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) kpre[u][e] = vpre[u][e] = 0.0f;
+      }
+    }
+  }
+
   // ---- the new token's rows (fused append, fp32 caches): rotated K / V of this KV head in
   // shared memory for this split's last row; the group's first CTA also writes them to the cache
   __shared__ __align__(16) float new_s[2][D];
-  const bool has_new = a.fuse_append && t0 + a.chunk >= Lk;
   if (has_new && warp < 2) {
     const bool is_k = warp == 0;
     const int64_t row = static_cast<int64_t>(b) * a.n_kv_heads + kvh;
@@ -202,13 +224,17 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
     for (int e = 0; e < E; ++e) qr[g][e] = q_s[g * D + lane * E + e];
 
   // row t of this sequence: base + kv_row_offset(kv, b, t) (through the block table for a paged cache)
-  const uint8_t* kbase = static_cast<const uint8_t*>(a.k_cache) + kvh * a.kv.head_stride;
-  const uint8_t* vbase = static_cast<const uint8_t*>(a.v_cache) + kvh * a.kv.head_stride;
   const float sl2 = a.scale * kLog2e;
 
   // ---- scores: warp w takes rows t0 + w, t0 + w + 8, ...
   constexpr int U = 4;
-  for (int j0 = warp; j0 < n; j0 += kDecodeWarps * U) {
+  // passes of U rows per warp; with SMALL at most two, unrolled, so the preload slot
+  // it * U + u is a compile-time index
+  constexpr int kPasses = SMALL ? 2 : (1 << 30);
+#pragma unroll
+  for (int it = 0; it < kPasses; ++it) {
+    const int j0 = warp + it * kDecodeWarps * U;
+    if (j0 >= n) break;
     float kx[U][E];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -216,6 +242,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
       if (has_new && j == n - 1) {
 #pragma unroll
         for (int e = 0; e < E; ++e) kx[u][e] = new_s[0][lane * E + e];
+      } else if constexpr (SMALL) {
+        const int pu = (it * U + u) % PR;  // this row's preload slot (it * U + u < PR for every row read)
+#pragma unroll
+        for (int e = 0; e < E; ++e) kx[u][e] = kpre[pu][e];
       } else if (j < n) RowLoader<KV, E>::load(kbase + kv_row_offset(a.kv, b, t0 + j), lane * E, kx[u]);
       else {
 #pragma unroll
@@ -265,7 +295,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
   for (int g = 0; g < GT; ++g)
 #pragma unroll
     for (int e = 0; e < E; ++e) acc[g][e] = 0.0f;
-  for (int j0 = warp; j0 < n; j0 += kDecodeWarps * U) {
+#pragma unroll
+  for (int it = 0; it < kPasses; ++it) {
+    const int j0 = warp + it * kDecodeWarps * U;
+    if (j0 >= n) break;
     float vx[U][E];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -273,6 +306,10 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_splitk_kernel(DecodeArg
       if (has_new && j == n - 1) {
 #pragma unroll
         for (int e = 0; e < E; ++e) vx[u][e] = new_s[1][lane * E + e];
+      } else if constexpr (SMALL) {
+        const int pu = (it * U + u) % PR;
+#pragma unroll
+        for (int e = 0; e < E; ++e) vx[u][e] = vpre[pu][e];
       } else if (j < n) RowLoader<KV, E>::load(vbase + kv_row_offset(a.kv, b, t0 + j), lane * E, vx[u]);
       else {
 #pragma unroll
@@ -404,7 +441,7 @@ cudaError_t launch_split(const DecodeArgs& a, cudaStream_t st) {
   const int G = a.n_q_heads / a.n_kv_heads;
   const int n_sub = (G + GT - 1) / GT;
   const size_t smem = sizeof(float) * (GT * D + GT * a.chunk + kDecodeWarps * GT * D);
-  auto kern = decode_splitk_kernel<KV, D, GT>;
+  auto kern = D == 64 && a.chunk <= 64 ? decode_splitk_kernel<KV, D, GT, D == 64> : decode_splitk_kernel<KV, D, GT, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   dim3 grid(a.max_splits, a.n_kv_heads * n_sub, a.batch);

@@ -258,9 +258,21 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
       for (int idx = et; idx < rows * groups; idx += 128) {
         const int rr = idx / groups, cg = idx % groups;
         const int64_t e = static_cast<int64_t>(m_lo + rr) * a.N + n_lo + cg * 4;
-        float4 acc = __ldcg(reinterpret_cast<const float4*>(a.partials + e));
-        for (int sp = 1; sp < a.k_splits; ++sp) {
-          const float4 x = __ldcg(reinterpret_cast<const float4*>(a.partials + static_cast<int64_t>(sp) * a.M * a.N + e));
+        // the splits' partials, four loads in flight at a time, summed in split order
+        const float4* src = reinterpret_cast<const float4*>(a.partials + e);
+        const int64_t step = static_cast<int64_t>(a.M) * a.N / 4;  // float4s between splits
+        float4 acc = __ldcg(src);
+        int sp = 1;
+        for (; sp + 4 <= a.k_splits; sp += 4) {
+          const float4 x0 = __ldcg(src + sp * step), x1 = __ldcg(src + (sp + 1) * step);
+          const float4 x2 = __ldcg(src + (sp + 2) * step), x3 = __ldcg(src + (sp + 3) * step);
+          acc.x = (((acc.x + x0.x) + x1.x) + x2.x) + x3.x;
+          acc.y = (((acc.y + x0.y) + x1.y) + x2.y) + x3.y;
+          acc.z = (((acc.z + x0.z) + x1.z) + x2.z) + x3.z;
+          acc.w = (((acc.w + x0.w) + x1.w) + x2.w) + x3.w;
+        }
+        for (; sp < a.k_splits; ++sp) {
+          const float4 x = __ldcg(src + sp * step);
           acc.x += x.x;
           acc.y += x.y;
           acc.z += x.z;

@@ -190,12 +190,15 @@ def cpu_sample_run(cfg, target_s: float):
         return dict(units=units, seconds=t, reps=reps, unit="TFLOP/s", scale=1e-12, cores=orc.num_threads(), nh=nh,
                     sample=f"1 sequence x {nh} query head(s) of one KV head (of {cfg.n_q_heads}), S={S}, {reps} "
                            f"run(s) (faithful fp32 oracle)")
-    # decode: a subset of sequences, all heads
+    # decode: a subset of sequences, all heads (inputs generated once per subset size)
     lengths_all = cfg.lengths()
     nb = 1
+    made = {}
     def run(nb):
-        sub = cfg.scaled(batch=nb, cached_range=None, cached=None, cached_list=lengths_all[:nb])
-        inp = make_inputs(sub, capacity=max(lengths_all[:nb]) + 1)
+        if nb not in made:
+            sub = cfg.scaled(batch=nb, cached_range=None, cached=None, cached_list=lengths_all[:nb])
+            made[nb] = (sub, make_inputs(sub, capacity=max(lengths_all[:nb]) + 1))
+        sub, inp = made[nb]
         desc = sub.spec(inp["capacity"]).desc()
         kc, vc = inp["k_cache"].numpy(), inp["v_cache"].numpy()
         t = time.perf_counter()
@@ -203,7 +206,11 @@ def cpu_sample_run(cfg, target_s: float):
                          inp["seq_len"].numpy(), mode=orc.FAITHFUL)
         return time.perf_counter() - t, sub
     t1, sub = run(1)
-    nb = int(max(1, min(cfg.batch, round(target_s / max(t1, 1e-3)))))
+    # bounded generation: at most ~32 M cache values per tensor in the sample (the timed oracle
+    # run is then repeated to fill target_s)
+    per_seq = (max(lengths_all) + 1) * cfg.n_kv_heads * cfg.head_dim
+    nb_gen = max(1, (32 << 20) // per_seq)
+    nb = int(max(1, min(cfg.batch, nb_gen, round(target_s / max(t1, 1e-3)))))
     if nb > 1:
         t1, sub = run(nb)
     t1, reps = _repeat_to(lambda: run(nb)[0], t1, target_s)

@@ -934,24 +934,24 @@ aihost_status check_matmul(const aihost_matmul_desc* d) {
 }
 
 struct GemmPlan {
-  int32_t block_n, k_splits, kt_per_split;
-  size_t a_stage, w_stage, partials;  // scratch bytes (each rounded to 256)
+  int32_t block_n, k_splits;
+  size_t a_stage, w_stage;  // scratch bytes (each rounded to 256)
 };
 
+// Output tiles that leave at least half of the CTA slots empty split their K range over a
+// cluster of 2, 4 or 8 CTAs (the largest power of two that fits in one wave of slots).
 GemmPlan plan_gemm(const aihost_matmul_desc* d, int32_t num_sms) {
   GemmPlan p;
   p.block_n = gemm_block_n(d->rows, d->n_out, num_sms);
   const int64_t tiles = gemm_tiles(d->rows, d->n_out, p.block_n);
-  const int32_t kt_total = d->k / 64;
+  const int64_t kt_total = d->k / 64;
   const int64_t slots = (p.block_n == 64 || p.block_n == -64 ? 2LL : 1LL) * num_sms;
-  int64_t splits = 1;
-  if (p.block_n != 256 && tiles < slots && tiles <= kMaxSplitCounters)
-    splits = std::min<int64_t>(kt_total, (slots + tiles - 1) / tiles);
-  p.kt_per_split = static_cast<int32_t>((kt_total + splits - 1) / splits);
-  p.k_splits = (kt_total + p.kt_per_split - 1) / p.kt_per_split;
+  int32_t splits = 1;
+  if (p.block_n != 256)
+    while (splits < 8 && 2 * splits <= kt_total && 2 * splits * tiles <= slots) splits *= 2;
+  p.k_splits = splits;
   p.a_stage = d->a_dtype == AIHOST_F16 ? 0 : round256(static_cast<size_t>(d->rows) * d->k * 2);
   p.w_stage = d->w_dtype == AIHOST_F16 ? 0 : round256(static_cast<size_t>(d->n_out) * d->k * 2);
-  p.partials = p.k_splits > 1 ? round256(static_cast<size_t>(p.k_splits) * d->rows * d->n_out * 4) : 0;
   return p;
 }
 
@@ -1002,7 +1002,7 @@ aihost_status aihost_matmul_workspace_size(const aihost_matmul_desc* desc, size_
   aihost_status s = check_matmul(desc);
   if (s != AIHOST_OK) return s;
   const GemmPlan p = plan_gemm(desc, current_sms());
-  *out_bytes = p.a_stage + p.w_stage + p.partials;
+  *out_bytes = p.a_stage + p.w_stage;
   return AIHOST_OK;
 }
 
@@ -1018,7 +1018,7 @@ aihost_status aihost_matmul_weights(aihost_attn_ctx* ctx, const aihost_matmul_de
   DeviceGuard g(ctx->device);
   if (!g.ok()) return fail(AIHOST_ECUDA, "cudaSetDevice(%d) failed", ctx->device);
   const GemmPlan p = plan_gemm(desc, ctx->num_sms);
-  const size_t need = p.a_stage + p.w_stage + p.partials;
+  const size_t need = p.a_stage + p.w_stage;
   if (need > ctx->scratch_bytes)
     return fail(AIHOST_ENOMEM, "this product needs %zu bytes of scratch, context has %zu (aihost_matmul_workspace_size)",
                 need, ctx->scratch_bytes);
@@ -1060,13 +1060,9 @@ aihost_status aihost_matmul_weights(aihost_attn_ctx* ctx, const aihost_matmul_de
   ga.K = desc->k;
   ga.part_cols = static_cast<int32_t>(part_cols);
   ga.k_splits = p.k_splits;
-  ga.kt_per_split = p.kt_per_split;
   ga.out = out;
   ga.out_dtype = desc->out_dtype;
   ga.ldc = N;
-  ga.partials = p.k_splits > 1 ? reinterpret_cast<float*>(sp) : nullptr;
-  ga.counters = ctx->counters;
-  ga.epoch = ctx->epoch++;
   ga.status = ctx->d_status;
   cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_MATMUL, st, [&] { return launch_gemm(ga, p.block_n, ctx->num_sms, st); });
   if (e != cudaSuccess) return cuda_fail(e, "matmul launch");

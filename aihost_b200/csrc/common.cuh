@@ -288,6 +288,28 @@ __device__ __forceinline__ bool split_arrive(unsigned long long* c, uint32_t epo
   return false;
 }
 
+// ------------------------------------------------------------------------------- thread-block clusters
+// Every thread of every CTA of the cluster arrives (release) and waits (acquire): shared-memory
+// writes made before it are visible to the peers' distributed-shared-memory reads after it. The
+// hardware co-schedules a cluster's CTAs, so the wait ends once each of them gets here.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The same shared-memory offset in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// Bulk copy of `bytes` (a multiple of 16, both ends 16-byte aligned) from this CTA's shared
+// memory into a peer CTA's (dst and the peer's mbarrier as shared::cluster addresses); the
+// bytes count on that mbarrier. A plain peer-to-peer copy inside the cluster, no multicast.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes, uint32_t peer_bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "r"(smem_u32(src)), "r"(bytes), "r"(peer_bar)
+               : "memory");
+}
+
 // ------------------------------------------------------------------------------- numeric helpers
 __device__ __forceinline__ float ld_as_float(const float* p) { return *p; }
 __device__ __forceinline__ float ld_as_float(const __half* p) { return __half2float(*p); }

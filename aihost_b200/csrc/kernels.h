@@ -198,13 +198,11 @@ struct GemmArgs {
   CUtensorMap a_map;   // fp16 A: dims {part_cols, M, n_parts}, box {64, 128 (BN when swapped), 1}, 128-byte swizzle
   CUtensorMap b_map;   // fp16 W: dims {K, N}, box {64, BN (128 when swapped)}, 128-byte swizzle
   int32_t M, N, K, part_cols;
-  int32_t k_splits, kt_per_split;  // K range split over CTAs (64-wide K tiles per split)
+  // K range split over the k_splits CTAs of a thread-block cluster (1: no split, persistent grid)
+  int32_t k_splits;
   void* out;           // [M][ldc] in out_dtype
   int32_t out_dtype;
   int64_t ldc;
-  float* partials;     // [k_splits][M][N] fp32 scratch (k_splits > 1)
-  unsigned long long* counters;  // per output tile, epoch-tagged (k_splits > 1)
-  uint32_t epoch;
   int32_t* status;
 };
 // Bytes of one 256-element GGUF block of a K-quant type (0 for other types).

@@ -14,15 +14,15 @@
 // part k / (K / n_parts). With n_parts = N ranks this is the rank-major buffer the KV-head
 // sharded all-gather leaves ([N][B][S][Hq/N][d]), consumed in place, with no permute.
 //
-// Kernel: persistent, one CTA per SM (BN = 256, 128) or two (BN = 64), 256 threads:
+// Kernel: one CTA per SM (BN = 256, 128) or two (BN = 64), 256 threads:
 //   warp 0      TMA producer: A [128 x 64] and W [BN x 64] tiles into an NS-stage ring
 //   warp 1      TMEM owner (2 x BN fp32 columns: two accumulators) and the tcgen05.mma issuer
 //               (M = 128, N = BN, K = 16, both operands K-major, 128-byte swizzle)
 //   warps 4-7   epilogue: tcgen05.ld of one accumulator (row per thread) while the MMA fills the
-//               other; output stores, or, with the K range split over CTAs (small M), an fp32
-//               partial per split and a reduction by the split that arrives last (epoch-tagged
-//               counter, no CTA ever waits on another).
-// No TMA multicast anywhere.
+//               other, then the output stores.
+// Enough tiles to fill the SMs: a persistent grid over the tiles. Too few (small M): the K range
+// is split over the CTAs of a thread-block cluster, which sum their fp32 partial tiles through
+// distributed shared memory (gemm_kernel's CL form). No TMA multicast anywhere.
 #include <type_traits>
 
 #include "common.cuh"
@@ -32,6 +32,7 @@ namespace aihost {
 namespace {
 
 constexpr int kGemmThreads = 256;
+constexpr int kGemmMaxSplits = 8;  // largest portable cluster
 constexpr int kGBM = 128;  // rows of A per tile (TMEM lanes)
 constexpr int kGBK = 64;   // K per stage: one 128-byte swizzle row of fp16
 
@@ -48,8 +49,8 @@ struct GemmCfg {
 
 struct GemmBars {
   uint64_t full[4], empty[4], acc_full[2], acc_empty[2];
+  uint64_t slices_in;  // CL: the peers' slices of this CTA's output rows have landed
   uint32_t tmem_base;
-  uint32_t last;
 };
 static_assert(sizeof(GemmBars) <= 256, "gemm_kernel reserves 256 bytes for its barriers");
 
@@ -74,9 +75,26 @@ __device__ __forceinline__ void store8(void* out, int32_t out_dtype, int64_t idx
 // its N = BN columns are rows of A, so the weight, not zero padding, fills the 128-row operand;
 // the accumulator then holds C^T and the epilogue stores it transposed (one row of C per TMEM
 // column: 32 lanes write 32 consecutive outputs).
-template <int BN, bool SWAP>
+//
+// CL (split K): the grid is the output tiles x k_splits (a power of two, <= 8), one unit per
+// CTA, and the k_splits CTAs of a tile form one thread-block cluster, CTA (cluster rank) s taking
+// K tiles [s * kt / k_splits, (s + 1) * kt / k_splits). Each CTA writes its fp32 partial tile
+// into its drained operand ring as [output row][output column] (rows = TMEM columns when
+// swapped, else TMEM lanes with one pad column, so a warp's 32 lanes hit 32 banks either way).
+// After a cluster barrier (every peer's ring is drained too), one thread bulk-copies slice q of
+// the tile's output rows to cluster rank q, counted on that rank's mbarrier; rank s then sums
+// slice s over the k_splits partials in rank order (the same fixed order every call) from its own
+// shared memory and stores it. A second cluster barrier keeps every CTA resident until all
+// copies out of it have landed. No global scratch, no counters, no CTA spins on another.
+template <int BN, bool SWAP, bool CL>
 __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
   using C = GemmCfg<BN>;
+  // CL: partial tile [OUT_ROWS][PS] floats at the ring's start, then k_splits receive slots of one
+  // slice (OUT_ROWS / k_splits rows) each
+  constexpr int OUT_ROWS = SWAP ? BN : kGBM, OUT_COLS = SWAP ? kGBM : BN;
+  constexpr int PS = SWAP ? OUT_COLS : OUT_COLS + 1;
+  static_assert(!CL || (((OUT_ROWS * PS + 31) & ~31) + OUT_ROWS * PS) * 4 <= C::BAR_OFF,
+                "partial tile and slices must fit in the ring");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   GemmBars& bar = *reinterpret_cast<GemmBars*>(smem + C::BAR_OFF);
@@ -86,7 +104,8 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
   const int R = SWAP ? a.N : a.M, NC = SWAP ? a.M : a.N;
   const int m_tiles = (R + kGBM - 1) / kGBM, n_tiles = (NC + BN - 1) / BN;
   const int kt_total = a.K / kGBK;
-  const int units = m_tiles * n_tiles * a.k_splits;
+  const int splits = CL ? a.k_splits : 1;
+  const int units = m_tiles * n_tiles * splits;
   int32_t* status = a.status;
 
   if (threadIdx.x == 0) {
@@ -98,6 +117,7 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
       mbar_init(&bar.acc_full[i], 1);
       mbar_init(&bar.acc_empty[i], 128);
     }
+    mbar_init(&bar.slices_in, 1);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(&bar.tmem_base, C::TMEM_COLS);
@@ -106,13 +126,13 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
   tc_fence_after();
   const uint32_t tmem = bar.tmem_base;
 
-  // unit u -> (m tile, n tile, K split); the splits of one tile are adjacent, tiles n-fastest
+  // unit u -> (m tile, n tile, K range); a tile's splits are adjacent (one cluster), tiles n-fastest
   auto unit_coords = [&](int u, int& mt, int& nt, int& kt0, int& kt1) {
-    const int ks = u % a.k_splits, tile = u / a.k_splits;
+    const int ks = u % splits, tile = u / splits;
     nt = tile % n_tiles;
     mt = tile / n_tiles;
-    kt0 = ks * a.kt_per_split;
-    kt1 = min(kt_total, kt0 + a.kt_per_split);
+    kt0 = ks * kt_total / splits;
+    kt1 = (ks + 1) * kt_total / splits;
   };
 
   if (warp == 0) {
@@ -174,118 +194,98 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // accumulator row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const int et = threadIdx.x - 128;   // 0..127 within the epilogue warpgroup
+    float* const part = reinterpret_cast<float*>(smem);  // CL: this CTA's partial tile
     int j = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
       int mt, nt, kt0, kt1;
       unit_coords(u, mt, nt, kt0, kt1);
       const int buf = j & 1;
-      // the four epilogue warps leave together (they meet at named barrier 1 below)
+      // the four epilogue warps leave together (they meet at named barrier 1 inside)
       if (!bar1_and_128(mbar_wait(&bar.acc_full[buf], (j >> 1) & 1, status))) break;
       tc_fence_after();
-      const int ks = u % a.k_splits;
-      // fp32 partial of this split (split-K), or the output itself
-      float* part = a.k_splits > 1 ? a.partials + static_cast<int64_t>(ks) * a.M * a.N : nullptr;
-      if constexpr (SWAP) {
-        // lane r = output column n, TMEM column j = output row m: for each j the warp's 32 lanes
-        // write 32 consecutive outputs of row m
-        const int n = mt * kGBM + r, m0 = nt * BN;
-        const bool col_ok = n < a.N;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tmem + lane_base + static_cast<uint32_t>(buf * BN + c * 32), v);
-          tmem_wait_ld();
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + static_cast<uint32_t>(buf * BN + c * 32), v);
+        tmem_wait_ld();
+        if constexpr (CL) {
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) {
-            const int m = m0 + c * 32 + jj;
-            if (!col_ok || m >= a.M) continue;
+            const int col = c * 32 + jj;  // TMEM column
+            part[SWAP ? col * PS + r : r * PS + col] = __uint_as_float(v[jj]);
+          }
+        } else if constexpr (SWAP) {
+          // lane r = output column n, TMEM column = output row m: for each m the warp's 32 lanes
+          // write 32 consecutive outputs of row m
+          const int n = mt * kGBM + r, m0 = nt * BN + c * 32;
+          if (n >= a.N) continue;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int m = m0 + jj;
+            if (m >= a.M) break;
             const float f = __uint_as_float(v[jj]);
-            if (part) part[static_cast<int64_t>(m) * a.N + n] = f;
-            else if (a.out_dtype == AIHOST_F16) static_cast<__half*>(a.out)[static_cast<int64_t>(m) * a.ldc + n] = __float2half_rn(f);
+            if (a.out_dtype == AIHOST_F16) static_cast<__half*>(a.out)[static_cast<int64_t>(m) * a.ldc + n] = __float2half_rn(f);
             else static_cast<float*>(a.out)[static_cast<int64_t>(m) * a.ldc + n] = f;
           }
-        }
-      } else {
-        const int m = mt * kGBM + r, n0 = nt * BN;
-        const bool row_ok = m < a.M;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tmem + lane_base + static_cast<uint32_t>(buf * BN + c * 32), v);
-          tmem_wait_ld();
-          if (!row_ok) continue;
+        } else {
+          const int m = mt * kGBM + r, n0 = nt * BN + c * 32;
+          if (m >= a.M) continue;
 #pragma unroll
           for (int g8 = 0; g8 < 4; ++g8) {
-            const int n = n0 + c * 32 + g8 * 8;
+            const int n = n0 + g8 * 8;
             if (n >= a.N) break;
             float f[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[g8 * 8 + i]);
-            const int64_t idx = static_cast<int64_t>(m) * a.N + n;
-            if (part) {
-              float4* d = reinterpret_cast<float4*>(part + idx);
-              d[0] = make_float4(f[0], f[1], f[2], f[3]);
-              d[1] = make_float4(f[4], f[5], f[6], f[7]);
-            } else {
-              store8(a.out, a.out_dtype, static_cast<int64_t>(m) * a.ldc + n, f);
-            }
+            store8(a.out, a.out_dtype, static_cast<int64_t>(m) * a.ldc + n, f);
           }
         }
       }
       // the accumulator may be overwritten by the unit after next
       tc_fence_before();
       mbar_arrive(&bar.acc_empty[buf]);
-      if (!part) continue;
-      // split-K: the split of this tile that arrives last sums every split's partial in split
-      // order (deterministic) and writes the output; the partials are read coalesced, 4 columns
-      // per thread
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) {
-        unsigned long long* counter = &a.counters[mt * n_tiles + nt];
-        const bool last = split_arrive(counter, a.epoch, a.k_splits, status);
-        if (last) atomicExch(counter, 0ull);
-        bar.last = last ? 1u : 0u;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (!bar.last) continue;
-      __threadfence();
-      // the output tile: rows [m_lo, m_lo + rows) and columns [n_lo, n_lo + cols) of C
-      const int m_lo = SWAP ? nt * BN : mt * kGBM, n_lo = SWAP ? mt * kGBM : nt * BN;
-      const int rows = min(SWAP ? BN : kGBM, a.M - m_lo), cols = min(SWAP ? kGBM : BN, a.N - n_lo);
-      const int groups = cols / 4;  // N % 8 == 0
-      for (int idx = et; idx < rows * groups; idx += 128) {
-        const int rr = idx / groups, cg = idx % groups;
-        const int64_t e = static_cast<int64_t>(m_lo + rr) * a.N + n_lo + cg * 4;
-        // the splits' partials, four loads in flight at a time, summed in split order
-        const float4* src = reinterpret_cast<const float4*>(a.partials + e);
-        const int64_t step = static_cast<int64_t>(a.M) * a.N / 4;  // float4s between splits
-        float4 acc = __ldcg(src);
-        int sp = 1;
-        for (; sp + 4 <= a.k_splits; sp += 4) {
-          const float4 x0 = __ldcg(src + sp * step), x1 = __ldcg(src + (sp + 1) * step);
-          const float4 x2 = __ldcg(src + (sp + 2) * step), x3 = __ldcg(src + (sp + 3) * step);
-          acc.x = (((acc.x + x0.x) + x1.x) + x2.x) + x3.x;
-          acc.y = (((acc.y + x0.y) + x1.y) + x2.y) + x3.y;
-          acc.z = (((acc.z + x0.z) + x1.z) + x2.z) + x3.z;
-          acc.w = (((acc.w + x0.w) + x1.w) + x2.w) + x3.w;
-        }
-        for (; sp < a.k_splits; ++sp) {
-          const float4 x = __ldcg(src + sp * step);
-          acc.x += x.x;
-          acc.y += x.y;
-          acc.z += x.z;
-          acc.w += x.w;
-        }
-        const int64_t o = static_cast<int64_t>(m_lo + rr) * a.ldc + n_lo + cg * 4;
-        if (a.out_dtype == AIHOST_F16) {
-          *reinterpret_cast<uint2*>(static_cast<__half*>(a.out) + o) = make_uint2(pack2h(acc.x, acc.y), pack2h(acc.z, acc.w));
-        } else {
-          *reinterpret_cast<float4*>(static_cast<float*>(a.out) + o) = acc;
-        }
+    }
+  }
+
+  if constexpr (CL) {
+    // ---------------------------------------------------------------- split-K sum over the cluster
+    const int ks = static_cast<int>(blockIdx.x) % splits;  // == cluster rank (clusters of `splits` CTAs)
+    const int slice_rows = OUT_ROWS / splits, slice_floats = slice_rows * PS;
+    const uint32_t slice_bytes = static_cast<uint32_t>(slice_floats) * 4u;
+    float* const part = reinterpret_cast<float*>(smem);
+    float* const slots = part + ((OUT_ROWS * PS + 31) & ~31);  // 128-byte aligned
+    if (warp >= 4) fence_proxy_async_smem();  // the partial tile, for the bulk copies
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar.slices_in, static_cast<uint32_t>(splits - 1) * slice_bytes);
+    __syncwarp();
+    cluster_sync_all();  // every CTA's partial tile is written and its operand ring drained
+    if (threadIdx.x == 0) {
+      for (int q = 1; q < splits; ++q) {
+        const int dst = (ks + q) % splits;
+        bulk_copy_to_peer(map_to_rank(smem_u32(slots + ks * slice_floats), dst), part + dst * slice_floats,
+                          slice_bytes, map_to_rank(smem_u32(&bar.slices_in), dst));
       }
     }
+    const bool ok = mbar_wait(&bar.slices_in, 0, status);
+    int mt, nt, kt0, kt1;
+    unit_coords(blockIdx.x, mt, nt, kt0, kt1);
+    const int m_base = SWAP ? nt * BN : mt * kGBM, n_base = SWAP ? mt * kGBM : nt * BN;
+    for (int e = threadIdx.x; ok && e < slice_floats; e += kGemmThreads) {
+      const int orow = ks * slice_rows + e / PS, ocol = e % PS;
+      if (ocol >= OUT_COLS) continue;  // pad column
+      float acc = 0.0f;
+      for (int p = 0; p < splits; ++p) {
+        const float x = p == ks ? part[ks * slice_floats + e] : slots[p * slice_floats + e];
+        acc = p == 0 ? x : acc + x;
+      }
+      const int m = m_base + orow, n = n_base + ocol;
+      if (m < a.M && n < a.N) {
+        const int64_t o = static_cast<int64_t>(m) * a.ldc + n;
+        if (a.out_dtype == AIHOST_F16) static_cast<__half*>(a.out)[o] = __float2half_rn(acc);
+        else static_cast<float*>(a.out)[o] = acc;
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // every copy out of every CTA has landed: none leaves with one in flight
   }
 
   tc_fence_before();
@@ -474,14 +474,27 @@ __global__ void __launch_bounds__(256) f32_to_f16_kernel(const float* __restrict
   }
 }
 
-template <int BN, bool SWAP>
+template <int BN, bool SWAP, bool CL>
 cudaError_t launch_gemm_bn(const GemmArgs& a, int grid, cudaStream_t st) {
   using C = GemmCfg<BN>;
-  auto kern = gemm_kernel<BN, SWAP>;
+  auto kern = gemm_kernel<BN, SWAP, CL>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kGemmThreads, C::SMEM, st>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (CL) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(a.k_splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace
@@ -532,14 +545,24 @@ int64_t gemm_tiles(int32_t M, int32_t N, int32_t block_n) {
 }
 
 cudaError_t launch_gemm(const GemmArgs& a, int32_t block_n, int32_t num_sms, cudaStream_t st) {
-  const int64_t units = gemm_tiles(a.M, a.N, block_n) * a.k_splits;
+  if (a.k_splits < 1 || a.k_splits > kGemmMaxSplits || (a.k_splits & (a.k_splits - 1)) || (a.k_splits > 1 && block_n == 256))
+    return cudaErrorInvalidValue;
+  const int64_t tiles = gemm_tiles(a.M, a.N, block_n);
+  if (a.k_splits > 1) {  // one CTA per (tile, split), clusters of k_splits
+    const int grid = static_cast<int>(tiles * a.k_splits);
+    switch (block_n) {
+      case -64: return launch_gemm_bn<64, true, true>(a, grid, st);
+      case -128: return launch_gemm_bn<128, true, true>(a, grid, st);
+      default: return launch_gemm_bn<64, false, true>(a, grid, st);
+    }
+  }
   const int64_t per_sm = (block_n == 64 || block_n == -64) ? 2 : 1;
-  const int grid = static_cast<int>(units < per_sm * num_sms ? units : per_sm * num_sms);
+  const int grid = static_cast<int>(tiles < per_sm * num_sms ? tiles : per_sm * num_sms);
   switch (block_n) {
-    case 256: return launch_gemm_bn<256, false>(a, grid, st);
-    case -64: return launch_gemm_bn<64, true>(a, grid, st);
-    case -128: return launch_gemm_bn<128, true>(a, grid, st);
-    default: return launch_gemm_bn<64, false>(a, grid, st);
+    case 256: return launch_gemm_bn<256, false, false>(a, grid, st);
+    case -64: return launch_gemm_bn<64, true, false>(a, grid, st);
+    case -128: return launch_gemm_bn<128, true, false>(a, grid, st);
+    default: return launch_gemm_bn<64, false, false>(a, grid, st);
   }
 }
 

@@ -79,7 +79,9 @@ def test_matmul_kquant_matches_reference_shader(ctx, i, out_dtype):
     (1, 2048, 1024, A.Q4_K),      # one token
     (77, 1536, 200, A.Q6_K),      # ragged rows and columns
     (4096, 2048, 2048, A.F16),    # 256-wide tiles fill the SMs: persistent, no split
-    (300, 1024, 1032, A.Q5_K),
+    (300, 1024, 1032, A.Q5_K),    # 64-wide tiles, K split over a cluster of 5
+    (16, 256, 512, A.F16),        # 4 K tiles: a cluster of 4, one K tile each
+    (8, 64, 264, A.F16),          # one K tile: no split
 ])
 def test_matmul_shapes_against_exact_product(ctx, rows, k, n_out, kind):
     ops = WeightOps(ctx)

@@ -96,7 +96,7 @@ def test_matmul_abi_validates_arguments():
 
 
 def test_matmul_workspace_covers_staging():
-    """Scratch = fp16 copy of an fp32 A + fp16 copy of a non-fp16 weight (+ split-K partials)."""
+    """Scratch = fp16 copy of an fp32 A + fp16 copy of a non-fp16 weight (split K needs none)."""
     _, f16 = _ws(_desc(rows=8192, w_dtype=A.F16))  # tiles fill the SMs: no split, no staging
     assert f16 == 0
     _, q4 = _ws(_desc(rows=8192, w_dtype=A.Q4_K))

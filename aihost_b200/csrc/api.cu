@@ -935,23 +935,28 @@ aihost_status check_matmul(const aihost_matmul_desc* d) {
 
 struct GemmPlan {
   int32_t block_n, k_splits;
+  bool fused;               // K-quant weight dequantised inside the GEMM (no fp16 copy)
   size_t a_stage, w_stage;  // scratch bytes (each rounded to 256)
 };
 
 // Output tiles that leave at least half of the CTA slots empty split their K range over a
-// cluster of 2, 4 or 8 CTAs (the largest power of two that fits in one wave of slots).
+// cluster of 2, 4 or 8 CTAs (the largest power of two that fits in one wave of slots; with the
+// weight dequantised in the GEMM, one that also splits the 256-value super-blocks evenly).
 GemmPlan plan_gemm(const aihost_matmul_desc* d, int32_t num_sms) {
   GemmPlan p;
   p.block_n = gemm_block_n(d->rows, d->n_out, num_sms);
   const int64_t tiles = gemm_tiles(d->rows, d->n_out, p.block_n);
   const int64_t kt_total = d->k / 64;
   const int64_t slots = (p.block_n == 64 || p.block_n == -64 ? 2LL : 1LL) * num_sms;
+  p.fused = gemm_fuses_dequant(d->w_dtype, p.block_n);
   int32_t splits = 1;
   if (p.block_n != 256)
-    while (splits < 8 && 2 * splits <= kt_total && 2 * splits * tiles <= slots) splits *= 2;
+    while (splits < 8 && 2 * splits <= kt_total && 2 * splits * tiles <= slots &&
+           (!p.fused || (d->k / 256) % (2 * splits) == 0))
+      splits *= 2;
   p.k_splits = splits;
   p.a_stage = d->a_dtype == AIHOST_F16 ? 0 : round256(static_cast<size_t>(d->rows) * d->k * 2);
-  p.w_stage = d->w_dtype == AIHOST_F16 ? 0 : round256(static_cast<size_t>(d->n_out) * d->k * 2);
+  p.w_stage = d->w_dtype == AIHOST_F16 || p.fused ? 0 : round256(static_cast<size_t>(d->n_out) * d->k * 2);
   return p;
 }
 
@@ -974,6 +979,24 @@ aihost_status encode_2d_f16(CUtensorMap* map, const void* base, uint64_t inner, 
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what, static_cast<int>(r));
+  return AIHOST_OK;
+}
+
+// The raw GGUF rows of a K-quant weight as bytes: dims {row bytes, rows}, box {one 256-value
+// block, 128 rows}, no swizzle (the block sizes used, 144 and 176, are multiples of 16).
+aihost_status encode_raw_rows(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
+                              uint32_t block_bytes) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned(base, 16) || row_bytes % 16 || block_bytes % 16) return fail(AIHOST_EINVAL, "w must be 16-byte aligned");
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {block_bytes, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AIHOST_ECUDA, "cuTensorMapEncodeTiled(w raw) failed with %d", static_cast<int>(r));
   return AIHOST_OK;
 }
 
@@ -1036,7 +1059,7 @@ aihost_status aihost_matmul_weights(aihost_attn_ctx* ctx, const aihost_matmul_de
     if (e != cudaSuccess) return cuda_fail(e, "A conversion launch");
     a16 = dst;
   }
-  if (desc->w_dtype != AIHOST_F16) {
+  if (desc->w_dtype != AIHOST_F16 && !p.fused) {
     __half* dst = reinterpret_cast<__half*>(sp);
     sp += p.w_stage;
     cudaError_t e = timed_launch(ctx, AIHOST_KERNEL_CONVERT, st, [&] {
@@ -1053,7 +1076,13 @@ aihost_status aihost_matmul_weights(aihost_attn_ctx* ctx, const aihost_matmul_de
   const uint32_t a_rows = swap ? static_cast<uint32_t>(-p.block_n) : 128u, w_rows = swap ? 128u : p.block_n;
   s = encode_3d_f16(&ga.a_map, a16, part_cols, M, parts, part_cols * 2, M * part_cols * 2, 64, a_rows, "a");
   if (s != AIHOST_OK) return s;
-  s = encode_2d_f16(&ga.b_map, w16, K, N, K * 2, 64, w_rows, "w");
+  ga.w_type = p.fused ? desc->w_dtype : AIHOST_F16;
+  if (p.fused) {
+    const uint32_t bb = static_cast<uint32_t>(weight_block_bytes(desc->w_dtype));
+    s = encode_raw_rows(&ga.w_raw_map, w, K / 256 * bb, N, bb);
+  } else {
+    s = encode_2d_f16(&ga.b_map, w16, K, N, K * 2, 64, w_rows, "w");
+  }
   if (s != AIHOST_OK) return s;
   ga.M = desc->rows;
   ga.N = desc->n_out;

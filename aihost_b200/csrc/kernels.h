@@ -204,6 +204,10 @@ struct GemmArgs {
   int32_t out_dtype;
   int64_t ldc;
   int32_t* status;
+  // AIHOST_F16: W through b_map. Q4_K / Q5_K: W's raw GGUF rows through w_raw_map (uint8 dims
+  // {row bytes, N}, box {one super-block, 128 rows}), dequantised inside the GEMM (swapped form)
+  int32_t w_type;
+  CUtensorMap w_raw_map;
 };
 // Bytes of one 256-element GGUF block of a K-quant type (0 for other types).
 int32_t weight_block_bytes(int32_t wt);
@@ -215,6 +219,8 @@ cudaError_t launch_f32_to_f16(const float* x, __half* y, int64_t n, int32_t num_
 int32_t gemm_block_n(int32_t M, int32_t N, int32_t num_sms);
 // Output tiles of that shape and width.
 int64_t gemm_tiles(int32_t M, int32_t N, int32_t block_n);
+// True when a weight of this type is dequantised inside the GEMM for this output-tile width.
+bool gemm_fuses_dequant(int32_t w_dtype, int32_t block_n);
 cudaError_t launch_gemm(const GemmArgs& a, int32_t block_n, int32_t num_sms, cudaStream_t st);
 
 }  // namespace aihost

@@ -32,27 +32,52 @@ namespace aihost {
 namespace {
 
 constexpr int kGemmThreads = 256;
+// WQ forms: warps 8-11 join warps 4-7 in dequantising (two threads per weight row)
+__host__ __device__ constexpr int gemm_threads(int wq) { return wq == 0 ? kGemmThreads : kGemmThreads + 128; }
 constexpr int kGemmMaxSplits = 8;  // largest portable cluster
 constexpr int kGBM = 128;  // rows of A per tile (TMEM lanes)
 constexpr int kGBK = 64;   // K per stage: one 128-byte swizzle row of fp16
 
-template <int BN>
+// Bytes of one row's 256-value super-block for the weight types dequantised inside the GEMM.
+__host__ __device__ constexpr int fused_block_bytes(int wq) {
+  return wq == AIHOST_Q4_K ? 144 : wq == AIHOST_Q5_K ? 176 : 0;
+}
+
+// WQ = 0: NS stages, each one A tile and one B tile by TMA (STAGE apart, B A_BYTES after A).
+// WQ = Q4_K / Q5_K (swapped: the MMA's A operand is the weight): the raw super-blocks of 128
+// weight rows by TMA into a two-deep raw ring; the dequantising warps write each fp16 weight tile
+// into tensor memory (row r in TMEM lane r, 32 columns per 64-wide K tile, a two-deep ring after
+// the accumulators), which the MMA reads as its A operand; the TMA keeps NS activation tiles in
+// flight in shared memory (B_STEP apart from offset 0). The ring sizes leave room for the CL
+// partial tile.
+template <int BN, int WQ = 0>
 struct GemmCfg {
-  static constexpr int NS = 4;
+  static constexpr int NS = WQ == 0 ? 4 : (BN == 128 ? 6 : 4);  // WQ: activation tiles only
+  static constexpr int NSA = 4;  // WQ: weight tiles in tensor memory
   static constexpr int A_BYTES = kGBM * kGBK * 2;
   static constexpr int B_BYTES = BN * kGBK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = NS * STAGE;
-  static constexpr int SMEM = BAR_OFF + 256 + 1024;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;  // 128 or 512: powers of two >= 32
+  static constexpr int B_OFF = WQ == 0 ? A_BYTES : 0;
+  static constexpr int B_STEP = WQ == 0 ? STAGE : B_BYTES;  // between consecutive B tiles
+  static constexpr int RAW_ROW = fused_block_bytes(WQ);
+  static constexpr int RAW_STAGE = kGBM * RAW_ROW;
+  static constexpr int RAW_OFF = WQ == 0 ? NS * STAGE : NS * B_BYTES;
+  static constexpr int BAR_OFF = RAW_OFF + 2 * RAW_STAGE;
+  static constexpr int SMEM = BAR_OFF + 512 + 1024;
+  static constexpr uint32_t A_COL = 2 * BN;  // WQ: first TMEM column of the weight-tile ring
+  // powers of two >= 32: two accumulators (+ the WQ weight tiles)
+  static constexpr uint32_t TMEM_COLS = WQ == 0 ? 2 * BN : (BN == 64 ? 256 : 512);
+  static_assert(WQ == 0 || A_COL + NSA * 32 <= TMEM_COLS, "weight-tile ring exceeds the TMEM allocation");
 };
 
 struct GemmBars {
-  uint64_t full[4], empty[4], acc_full[2], acc_empty[2];
-  uint64_t slices_in;  // CL: the peers' slices of this CTA's output rows have landed
+  uint64_t full[8], empty[8], acc_full[2], acc_empty[2];
+  uint64_t slices_in;                  // CL: the peers' slices of this CTA's output rows have landed
+  uint64_t raw_full[2], raw_empty[2];  // WQ: raw super-block ring
+  uint64_t a_full[4], a_empty[4];      // WQ: dequantised weight-tile ring
   uint32_t tmem_base;
 };
-static_assert(sizeof(GemmBars) <= 256, "gemm_kernel reserves 256 bytes for its barriers");
+static_assert(sizeof(GemmBars) <= 512, "gemm_kernel reserves 512 bytes for its barriers");
 
 __device__ __forceinline__ uint32_t pack2h(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
@@ -71,6 +96,97 @@ __device__ __forceinline__ void store8(void* out, int32_t out_dtype, int64_t idx
   }
 }
 
+__device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mul.rn.f32x2 rd, ra, rb;\n"
+      " mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n add.rn.f32x2 rd, ra, rb;\n"
+      " mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// Eight fp16 weights (t * q) - dm from the eight unsigned quants held in the bytes of w0 and w1:
+// each byte becomes the float 2^23 + q exactly (byte permute under exponent 0x4B), minus 2^23
+// gives q; then the dequantisation shaders' two fp32 roundings, then one rounding to fp16, the
+// same values dequant_kernel writes.
+__device__ __forceinline__ uint4 dequant_chunk8(uint32_t w0, uint32_t w1, float t, float dm) {
+  const float2 shift = make_float2(-8388608.0f, -8388608.0f), tt = make_float2(t, t), ndm = make_float2(-dm, -dm);
+  uint32_t h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t w = i < 2 ? w0 : w1, b = (i & 1) * 2;
+    const float2 q = fadd2_rn(make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | b)),
+                                          __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (b + 1)))),
+                              shift);
+    const float2 v = fadd2_rn(fmul2_rn(tt, q), ndm);
+    h[i] = pack2h(v.x, v.y);
+  }
+  return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// Byte i (0..11) of the 12 scale bytes held in words y, z, w of a Q4_K / Q5_K block header.
+__device__ __forceinline__ uint32_t scale_byte(const uint4& hdr, int i) {
+  const uint32_t word = i < 4 ? hdr.y : (i < 8 ? hdr.z : hdr.w);
+  return (word >> ((i & 3) * 8)) & 0xffu;
+}
+// get_scale_min_k4 on the header in registers (the integer steps of scale_min_k4 below).
+__device__ __forceinline__ void scale_min_k4_hdr(int j, const uint4& hdr, float* sc, float* mn) {
+  if (j < 4) {
+    *sc = static_cast<float>(scale_byte(hdr, j) & 63);
+    *mn = static_cast<float>(scale_byte(hdr, j + 4) & 63);
+  } else {
+    *sc = static_cast<float>((scale_byte(hdr, j + 4) & 0xF) | ((scale_byte(hdr, j - 4) >> 6) << 4));
+    *mn = static_cast<float>((scale_byte(hdr, j + 4) >> 4) | ((scale_byte(hdr, j) >> 6) << 4));
+  }
+}
+
+// Half `hf` of one weight row's 64 values of K tile `quarter` (0..3) of a raw Q4_K / Q5_K
+// super-block in shared memory (hf 0: tile values 0..31, the low nibbles; hf 1: values 32..63,
+// the high ones) as 16 fp16 pairs, value 2i in the low half of out[i]. The fields and formulas are
+// dequant8_q4k's / dequant8_q5k's (including the Q5_K high-bit offset the reference shader uses).
+template <int WQ>
+__device__ __forceinline__ void dequant_row_half(const uint8_t* raw_row, int quarter, int hf, uint32_t (&out)[16]) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(raw_row);
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr.x & 0xffffu)));
+  const float dmin = __half2float(__ushort_as_half(static_cast<unsigned short>(hdr.x >> 16)));
+  float sc, mn;
+  scale_min_k4_hdr(2 * quarter + hf, hdr, &sc, &mn);
+  const float t = __fmul_rn(d, sc), dm = __fmul_rn(dmin, mn);
+  constexpr int QL = WQ == AIHOST_Q4_K ? 16 : 48;  // low-bit quants of K tile 0
+  const uint4* ql = reinterpret_cast<const uint4*>(raw_row + QL + 32 * quarter);
+  const uint4 qa = ql[0], qb = ql[1];
+  const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  uint32_t hb[8];
+  if constexpr (WQ == AIHOST_Q5_K) {
+    const uint4* qh = reinterpret_cast<const uint4*>(raw_row + 16 + 32 * quarter);
+    const uint4 ha = qh[0], hbv = qh[1];
+    hb[0] = ha.x; hb[1] = ha.y; hb[2] = ha.z; hb[3] = ha.w;
+    hb[4] = hbv.x; hb[5] = hbv.y; hb[6] = hbv.z; hb[7] = hbv.w;
+  }
+  const int nshift = 4 * hf, hshift = 2 * quarter + hf;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t q0 = (w[2 * c] >> nshift) & 0x0F0F0F0Fu, q1 = (w[2 * c + 1] >> nshift) & 0x0F0F0F0Fu;
+    if constexpr (WQ == AIHOST_Q5_K) {
+      q0 |= ((hb[2 * c] >> hshift) & 0x01010101u) << 4;
+      q1 |= ((hb[2 * c + 1] >> hshift) & 0x01010101u) << 4;
+    }
+    const uint4 h = dequant_chunk8(q0, q1, t, dm);
+    out[4 * c] = h.x;
+    out[4 * c + 1] = h.y;
+    out[4 * c + 2] = h.z;
+    out[4 * c + 3] = h.w;
+  }
+}
+
 // SWAP (few rows of A, i.e. decode): the MMA's M = 128 rows are weight rows (output columns) and
 // its N = BN columns are rows of A, so the weight, not zero padding, fills the 128-row operand;
 // the accumulator then holds C^T and the epilogue stores it transposed (one row of C per TMEM
@@ -86,9 +202,16 @@ __device__ __forceinline__ void store8(void* out, int32_t out_dtype, int64_t idx
 // slice s over the k_splits partials in rank order (the same fixed order every call) from its own
 // shared memory and stores it. A second cluster barrier keeps every CTA resident until all
 // copies out of it have landed. No global scratch, no counters, no CTA spins on another.
-template <int BN, bool SWAP, bool CL>
-__global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
-  using C = GemmCfg<BN>;
+//
+// WQ (Q4_K / Q5_K, swapped CL form only): the weight stays in its GGUF blocks in HBM. The producer
+// moves the raw super-block of the tile's 128 weight rows (one row per 144 / 176-byte box row)
+// into a two-deep raw ring every four K tiles, and each activation tile into the operand ring;
+// the four epilogue warps, idle until the accumulator is ready, dequantise one weight row each
+// into the operand tile and arrive on its full barrier with the producer.
+template <int BN, bool SWAP, bool CL, int WQ>
+__global__ void __launch_bounds__(gemm_threads(WQ), BN == 64 ? 2 : 1) gemm_kernel(const __grid_constant__ GemmArgs a) {
+  using C = GemmCfg<BN, WQ>;
+  static_assert(WQ == 0 || (SWAP && CL), "weights are dequantised in the GEMM only in the swapped split-K form");
   // CL: partial tile [OUT_ROWS][PS] floats at the ring's start, then k_splits receive slots of one
   // slice (OUT_ROWS / k_splits rows) each
   constexpr int OUT_ROWS = SWAP ? BN : kGBM, OUT_COLS = SWAP ? kGBM : BN;
@@ -112,6 +235,14 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
     for (int i = 0; i < C::NS; ++i) {
       mbar_init(&bar.full[i], 1);
       mbar_init(&bar.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar.raw_full[i], 1);
+      mbar_init(&bar.raw_empty[i], 8);  // the eight dequantising warps
+    }
+    for (int i = 0; i < C::NSA; ++i) {
+      mbar_init(&bar.a_full[i], 8);
+      mbar_init(&bar.a_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar.acc_full[i], 1);
@@ -139,18 +270,34 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&a.a_map);
-      tma_prefetch_desc(&a.b_map);
+      if constexpr (WQ != 0) tma_prefetch_desc(&a.w_raw_map);
+      else tma_prefetch_desc(&a.b_map);
       int g = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
         int mt, nt, kt0, kt1;
         unit_coords(u, mt, nt, kt0, kt1);
         for (int kt = kt0; kt < kt1; ++kt, ++g) {
+          if constexpr (WQ != 0) {
+            if (((kt - kt0) & 3) == 0) {  // a new super-block (K ranges start on one)
+              const int lsb = (kt - kt0) >> 2, rs = lsb & 1;
+              if (!mbar_wait(&bar.raw_empty[rs], ((lsb >> 1) & 1) ^ 1, status)) { ok = false; break; }
+              mbar_arrive_expect_tx(&bar.raw_full[rs], C::RAW_STAGE);
+              tma_load_2d(smem + C::RAW_OFF + rs * C::RAW_STAGE, &a.w_raw_map, &bar.raw_full[rs], (kt >> 2) * C::RAW_ROW,
+                          mt * kGBM);
+            }
+          }
           const int s = g % C::NS;
           if (!mbar_wait(&bar.empty[s], ((g / C::NS) & 1) ^ 1, status)) { ok = false; break; }
           uint8_t* st = smem + s * C::STAGE;
-          mbar_arrive_expect_tx(&bar.full[s], C::STAGE);
           const int k = kt * kGBK;
+          if constexpr (WQ != 0) {  // the activation ring; the weight tiles come from the dequantising warps
+            mbar_arrive_expect_tx(&bar.full[s], C::B_BYTES);
+            tma_load_3d(smem + C::B_OFF + s * C::B_BYTES, &a.a_map, &bar.full[s], k % a.part_cols, nt * BN,
+                        k / a.part_cols);
+            continue;
+          }
+          mbar_arrive_expect_tx(&bar.full[s], C::STAGE);
           if constexpr (SWAP) {  // A operand: weight rows; B operand: rows of A
             tma_load_2d(st, &a.b_map, &bar.full[s], k, mt * kGBM);
             tma_load_3d(st + C::A_BYTES, &a.a_map, &bar.full[s], k % a.part_cols, nt * BN, k / a.part_cols);
@@ -166,6 +313,9 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_f16(kGBM, BN, 0, 0);
       const uint32_t base = smem_u32(smem);
+      // descriptors of the ring's first tiles; a tile's K step adds its byte offset / 16 to the
+      // 14-bit start-address field (shared addresses stay below 2^18, so it never carries)
+      const uint64_t a_desc0 = make_sw128_desc(base, 16, 1024), b_desc0 = make_sw128_desc(base + C::B_OFF, 16, 1024);
       int g = 0, j = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x, ++j) {
@@ -176,15 +326,21 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
         for (int kt = kt0; kt < kt1; ++kt, ++g) {
-          const int s = g % C::NS;
+          const int s = g % C::NS, sw = g % C::NSA;
           if (!mbar_wait(&bar.full[s], (g / C::NS) & 1, status)) { ok = false; break; }
+          if (WQ != 0 && !mbar_wait(&bar.a_full[sw], (g / C::NSA) & 1, status)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = base + s * C::STAGE, sb = sa + C::A_BYTES;
+          const uint64_t ad = a_desc0 + static_cast<uint64_t>((s * C::STAGE) >> 4);
+          const uint64_t bd = b_desc0 + static_cast<uint64_t>((s * C::B_STEP) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kGBK / 16; ++kk)
-            umma_f16_ss(d, make_sw128_desc(sa + kk * 32, 16, 1024), make_sw128_desc(sb + kk * 32, 16, 1024), idesc,
-                        (kt > kt0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kGBK / 16; ++kk) {
+            if constexpr (WQ != 0)  // the weight tile from tensor memory: 16 values = 8 columns per K step
+              umma_f16_ts(d, tmem + C::A_COL + sw * 32 + kk * 8, bd + 2 * kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+            else
+              umma_f16_ss(d, ad + 2 * kk, bd + 2 * kk, idesc, (kt > kt0 || kk > 0) ? 1u : 0u);
+          }
           umma_commit(&bar.empty[s]);
+          if constexpr (WQ != 0) umma_commit(&bar.a_empty[sw]);
         }
         if (ok) umma_commit(&bar.acc_full[buf]);
       }
@@ -195,8 +351,33 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
     const int r = quarter * 32 + lane;  // accumulator row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     float* const part = reinterpret_cast<float*>(smem);  // CL: this CTA's partial tile
+    const int hf = warp >= 8 ? 1 : 0;                    // WQ: which half of weight row r
+    if constexpr (WQ != 0) {
+      // ---------------------------------------------------------------- weight dequantisation
+      int mt, nt, kt0, kt1;
+      unit_coords(blockIdx.x, mt, nt, kt0, kt1);
+      bool ok = true;
+      for (int kt = kt0, g = 0; ok && kt < kt1; ++kt, ++g) {
+        const int lsb = (kt - kt0) >> 2, rs = lsb & 1, sw = g % C::NSA;
+        if (((kt - kt0) & 3) == 0) ok = mbar_wait(&bar.raw_full[rs], (lsb >> 1) & 1, status);
+        if (ok) ok = mbar_wait(&bar.a_empty[sw], ((g / C::NSA) & 1) ^ 1, status);
+        // the vote keeps the tcgen05.st warp-collective (a lane that gave up leaves the warp with it)
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();  // the MMA that read this slot is complete
+          uint32_t h[16];
+          dequant_row_half<WQ>(smem + C::RAW_OFF + rs * C::RAW_STAGE + r * C::RAW_ROW, kt & 3, hf, h);
+          tmem_st16(tmem + lane_base + C::A_COL + sw * 32 + hf * 16, h);
+          tmem_wait_st();
+          tc_fence_before();
+        }
+        __syncwarp();
+        if (ok && lane == 0) mbar_arrive(&bar.a_full[sw]);
+        if (ok && ((kt & 3) == 3 || kt + 1 == kt1) && lane == 0) mbar_arrive(&bar.raw_empty[rs]);
+      }
+    }
     int j = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+    for (int u = blockIdx.x; hf == 0 && u < units; u += gridDim.x, ++j) {
       int mt, nt, kt0, kt1;
       unit_coords(u, mt, nt, kt0, kt1);
       const int buf = j & 1;
@@ -269,7 +450,7 @@ __global__ void __launch_bounds__(kGemmThreads, BN == 64 ? 2 : 1) gemm_kernel(co
     int mt, nt, kt0, kt1;
     unit_coords(blockIdx.x, mt, nt, kt0, kt1);
     const int m_base = SWAP ? nt * BN : mt * kGBM, n_base = SWAP ? mt * kGBM : nt * BN;
-    for (int e = threadIdx.x; ok && e < slice_floats; e += kGemmThreads) {
+    for (int e = threadIdx.x; ok && e < slice_floats; e += gemm_threads(WQ)) {
       const int orow = ks * slice_rows + e / PS, ocol = e % PS;
       if (ocol >= OUT_COLS) continue;  // pad column
       float acc = 0.0f;
@@ -474,15 +655,15 @@ __global__ void __launch_bounds__(256) f32_to_f16_kernel(const float* __restrict
   }
 }
 
-template <int BN, bool SWAP, bool CL>
+template <int BN, bool SWAP, bool CL, int WQ = 0>
 cudaError_t launch_gemm_bn(const GemmArgs& a, int grid, cudaStream_t st) {
-  using C = GemmCfg<BN>;
-  auto kern = gemm_kernel<BN, SWAP, CL>;
+  using C = GemmCfg<BN, WQ>;
+  auto kern = gemm_kernel<BN, SWAP, CL, WQ>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.blockDim = dim3(gemm_threads(WQ), 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -537,6 +718,10 @@ int32_t gemm_block_n(int32_t M, int32_t N, int32_t num_sms) {
   return tiles256 >= num_sms ? 256 : 64;
 }
 
+bool gemm_fuses_dequant(int32_t w_dtype, int32_t block_n) {
+  return block_n < 0 && (w_dtype == AIHOST_Q4_K || w_dtype == AIHOST_Q5_K);
+}
+
 int64_t gemm_tiles(int32_t M, int32_t N, int32_t block_n) {
   const bool swap = block_n < 0;
   const int bn = swap ? -block_n : block_n;
@@ -548,6 +733,14 @@ cudaError_t launch_gemm(const GemmArgs& a, int32_t block_n, int32_t num_sms, cud
   if (a.k_splits < 1 || a.k_splits > kGemmMaxSplits || (a.k_splits & (a.k_splits - 1)) || (a.k_splits > 1 && block_n == 256))
     return cudaErrorInvalidValue;
   const int64_t tiles = gemm_tiles(a.M, a.N, block_n);
+  if (a.w_type != AIHOST_F16) {  // raw K-quant weight, dequantised in the GEMM (swapped, clusters)
+    const int grid = static_cast<int>(tiles * a.k_splits);
+    if (block_n == -64 && a.w_type == AIHOST_Q4_K) return launch_gemm_bn<64, true, true, AIHOST_Q4_K>(a, grid, st);
+    if (block_n == -64 && a.w_type == AIHOST_Q5_K) return launch_gemm_bn<64, true, true, AIHOST_Q5_K>(a, grid, st);
+    if (block_n == -128 && a.w_type == AIHOST_Q4_K) return launch_gemm_bn<128, true, true, AIHOST_Q4_K>(a, grid, st);
+    if (block_n == -128 && a.w_type == AIHOST_Q5_K) return launch_gemm_bn<128, true, true, AIHOST_Q5_K>(a, grid, st);
+    return cudaErrorInvalidValue;
+  }
   if (a.k_splits > 1) {  // one CTA per (tile, split), clusters of k_splits
     const int grid = static_cast<int>(tiles * a.k_splits);
     switch (block_n) {

@@ -840,13 +840,18 @@ def bench_weights(args, device, ctx, pk, pk_kind, cpu_s):
                     "frac": ach / pk["bf16_tflops"], "kernel": "gemm_kernel<256>", "kernel_ms": k_ms,
                     "algorithmic_per_launch": flops, "peak_source": f"{pk_kind} bf16 burst", "traffic": None}
         else:
-            w16 = 2.0 * N * K  # the GEMM reads the fp16 weight (dequantised copy for K-quants)
-            gbytes = w16 + 2.0 * M * K + 2.0 * M * N
+            # the GEMM reads the weight as stored when it dequantises inside (no dequantisation
+            # launch), else the fp16 weight (the dequantised copy for K-quants)
+            fused = kind != "F16" and n_cv == 0
+            wread = weight_bytes(kind, N, K) if fused else 2.0 * N * K
+            gbytes = wread + 2.0 * M * K + 2.0 * M * N
             ach = gbytes / (k_ms * 1e-3) * 1e-9
             roof = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
-                    "kernel": "gemm_kernel<64>", "kernel_ms": k_ms, "algorithmic_per_launch": gbytes,
+                    "kernel": f"gemm_kernel<64> (dequantising {kind})" if fused else "gemm_kernel<64>",
+                    "kernel_ms": k_ms, "algorithmic_per_launch": gbytes,
                     "peak_source": f"{pk_kind} copy", "traffic": None,
-                    "note": "bytes of the GEMM launch: fp16 weight + A + C"}
+                    "note": ("bytes of the GEMM launch: weight as stored + A + C" if fused
+                             else "bytes of the GEMM launch: fp16 weight + A + C")}
         # end to end: A from pinned host memory, C back, per step
         ha = a.cpu().pin_memory()
         hc = torch.empty(c.shape, dtype=c.dtype, pin_memory=True)
@@ -867,7 +872,7 @@ def bench_weights(args, device, ctx, pk, pk_kind, cpu_s):
                "weight_stream_gbs": weight_bytes(kind, N, K) / (ms * 1e-3) * 1e-9,
                "roofline": roof, "kernels": {"matmul": {"launches": n_mm, "mean_ms": k_ms},
                                              "dequant": {"launches": n_cv, "mean_ms": (t_cv / n_cv if n_cv else None)}},
-               "gpu_launches": args.steps * (2 if kind != "F16" else 1),
+               "gpu_launches": n_mm + n_cv,
                "e2e": {"value": flops / (statistics.mean(e_ms) * 1e-3) * 1e-12, "unit": "TFLOP/s",
                        "h2d_bytes_per_step": ha.numel() * 2, "d2h_bytes_per_step": hc.numel() * 2,
                        "ms_per_step": statistics.mean(e_ms)},

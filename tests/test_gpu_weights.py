@@ -82,6 +82,10 @@ def test_matmul_kquant_matches_reference_shader(ctx, i, out_dtype):
     (300, 1024, 1032, A.Q5_K),    # 64-wide tiles, K split over a cluster of 5
     (16, 256, 512, A.F16),        # 4 K tiles: a cluster of 4, one K tile each
     (8, 64, 264, A.F16),          # one K tile: no split
+    (64, 4096, 1024, A.Q5_K),     # Q5_K dequantised inside the GEMM, clusters of 8
+    (128, 1536, 520, A.Q4_K),     # 128-row swapped tiles, ragged weight rows, 6 super-blocks: clusters of 2
+    (16, 256, 264, A.Q5_K),       # one super-block: no split (clusters of one)
+    (96, 2048, 4096, A.Q4_K),
 ])
 def test_matmul_shapes_against_exact_product(ctx, rows, k, n_out, kind):
     ops = WeightOps(ctx)

@@ -537,6 +537,26 @@ def bench_layers(cfg, layers, steps, warmup, device, ctx):
     return ms, w["kernel_bytes"] * layers
 
 
+def time_allgather(nbytes: int, ws: int, device, steps: int, warmup: int, dist_on: bool) -> float:
+    """Mean device time (CUDA events, max over ranks) of an NCCL all-gather of `nbytes` per rank
+    on the bench's process group: the collective the head-sharded step runs, timed alone."""
+    import torch
+    import torch.distributed as tdist
+
+    x = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    y = torch.empty(ws * nbytes, dtype=torch.uint8, device=device)
+    for _ in range(max(warmup, 3)):
+        tdist.all_gather_into_tensor(y, x)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in ev:
+        e0.record()
+        tdist.all_gather_into_tensor(y, x)
+        e1.record()
+    torch.cuda.synchronize()
+    return max_over_ranks(statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev), dist_on)
+
+
 def max_over_ranks(x: float, dist_on: bool) -> float:
     if not dist_on:
         return x
@@ -1029,8 +1049,12 @@ def config_object(cfg, shard_mode, args, device, ctx, dist_on, ws, rank, pk, pk_
     res["dtype"] = "f32" if cfg.q_dtype == 0 else "f16 (fp32 accumulate)"
     kern_ms = sum(v["mean_ms"] or 0.0 for v in res["kernels"].values() if v["launches"])
     if ws > 1 and shard_mode != "seq":
-        # NCCL collective(s) plus launch gaps: the step time this library's kernels do not cover
-        res["collective_ms"] = max(0.0, res["ms_per_step"] - max_over_ranks(kern_ms, dist_on))
+        # the step time this library's kernels do not cover (NCCL plus launch gaps; 0 when the
+        # kernels' own overlap hides it), and an all-gather of the same bytes timed alone
+        res["step_minus_kernels_ms"] = max(0.0, res["ms_per_step"] - max_over_ranks(kern_ms, dist_on))
+        out_elem = 4 if cfg.q_dtype == 0 else 2
+        res["collective_ms"] = time_allgather(cfg.batch * cfg.n_new * (cfg.n_q_heads // ws) * cfg.head_dim * out_elem,
+                                              ws, device, max(args.steps, 10), args.warmup, dist_on)
     if layers > 0 and cfg.n_new == 1 and ws == 1:
         l_ms, l_bytes = bench_layers(cfg, layers, max(args.steps, 10), args.warmup, device, ctx)
         res["layers"] = {"layers": layers, "ms_per_step": l_ms, "tokens_per_s": cfg.batch * layers / (l_ms * 1e-3),
@@ -1113,7 +1137,7 @@ def main():
                 "kv_layout": (f"paged: {args.paged}-row pages of a shared pool, shuffled order, block table"
                               if args.paged else "contiguous per sequence"),
                 "gpu_launches": main_res["gpu_launches"], "clocks": clk, "kernels": main_res["kernels"]}
-        for key in ("layers", "collective_ms", "kv_read_gbs", "kv_read_frac_of_8tbs"):
+        for key in ("layers", "collective_ms", "step_minus_kernels_ms", "kv_read_gbs", "kv_read_frac_of_8tbs"):
             if key in main_res:
                 line[key] = main_res[key]
         line.update(extra)

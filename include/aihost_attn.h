@@ -283,7 +283,9 @@ aihost_status aihost_attn_merge_partials(aihost_attn_ctx* ctx, int32_t n_parts, 
  * [N][batch][n_new][Hq/N][head_dim] buffer aihost_attn_forward_sharded gathers, read in place.
  * fp16 operands on the tensor cores (fp32 A is rounded to fp16 first; K-quant weights are
  * dequantised with the reference shaders' formulas, then rounded once to fp16), fp32
- * accumulation. Needs aihost_matmul_workspace_size bytes of the context's scratch. */
+ * accumulation. With at most 128 rows, Q4_K and Q5_K weights are dequantised inside the one GEMM
+ * launch; other K-quant and fp32 weights are first copied to fp16 in the context's scratch. Needs
+ * aihost_matmul_workspace_size bytes of that scratch (0 for fp16 A with fp16, or in-GEMM, weights). */
 typedef struct {
   int32_t rows;       /* M: rows of A and of the output */
   int32_t k;          /* K: a multiple of 64 (of 256 for K-quant weights); k / n_parts a multiple of 64 */

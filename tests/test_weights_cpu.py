@@ -103,3 +103,16 @@ def test_matmul_workspace_covers_staging():
     assert q4 == 4096 * 4096 * 2
     _, both = _ws(_desc(rows=8192, a_dtype=A.F32, w_dtype=A.F32))
     assert both == 2 * 8192 * 4096 + 4096 * 4096 * 2
+
+
+def test_matmul_workspace_in_gemm_dequantisation():
+    """At most 128 rows of A with Q4_K / Q5_K weights: the GEMM dequantises the blocks itself, so
+    no fp16 weight copy is staged; other K-quant types, fp32 weights and larger row counts stage it."""
+    for kind in (A.Q4_K, A.Q5_K):
+        for rows in (1, 64, 128):
+            assert _ws(_desc(rows=rows, w_dtype=kind)) == (A.OK, 0)
+        assert _ws(_desc(rows=129, w_dtype=kind))[1] == 4096 * 4096 * 2
+    for kind in (A.Q2_K, A.Q3_K, A.Q6_K, A.F32):
+        assert _ws(_desc(rows=64, w_dtype=kind))[1] == 4096 * 4096 * 2
+    # an fp32 A is still converted, with the weight dequantised in the GEMM
+    assert _ws(_desc(rows=64, a_dtype=A.F32, w_dtype=A.Q4_K))[1] == 64 * 4096 * 2
